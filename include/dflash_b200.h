@@ -1,0 +1,178 @@
+/*
+ * dflash_b200.h -- C ABI of the B200-native DFlash draft-model forward.
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer
+ * (caller-owned) unless stated otherwise; `stream` is a cudaStream_t passed as
+ * void*.  Every call returns a status code; dflash_last_error() gives the
+ * message of the last failure on the calling thread.  Status mapping for a
+ * Python shim: DFLASH_ERR_INVALID -> ValueError, anything else -> RuntimeError
+ * (the reference raises PyValueError on weight-length mismatches and
+ * PyRuntimeError("ANE kernel '<name>' ... failed") on execution errors,
+ * ane/src/wrapper.rs:397-405 and :204-209).
+ *
+ * Threading: calls on different handles are independent; dflash_forward on
+ * one handle serialises internally (its workspace is shared), like the
+ * reference's kernels that must not be re-entered on the same buffers.
+ * None of these calls needs the Python GIL (ctypes releases it), matching the
+ * reference's py.allow_threads around every native call (wrapper.rs:58-221).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   dflash_create    ANEDraftModel.__init__ + load_weights_q8
+ *                    (mirror_sd/ane_model.py:47-110, :312-344) and the native
+ *                    compile_dflash_kernels_q8 / Q8LayerWeights
+ *                    (ane/src/wrapper.rs:363-428, :437-502)
+ *   dflash_forward   DFlashDraftModel.__call__ (mirror_sd/dflash.py:384-403)
+ *                    and its ANE twin forward / run_kernels /
+ *                    read_draft_tokens (ane_model.py:384-416, :564-604),
+ *                    followed by lm_head + greedy sample on the last block-1
+ *                    rows (mirror_sd/generate.py:604-606)
+ *   dflash_accept    the longest-prefix acceptance loop (generate.py:722-728)
+ *   dflash_quantize_q8  ANEDraftModel._quantize_weight_q8 (ane_model.py:265-279)
+ *   dflash_destroy   drop of the native kernels / buffers (wrapper.rs)
+ */
+#ifndef DFLASH_B200_H
+#define DFLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFLASH_OK 0
+#define DFLASH_ERR_INVALID 1 /* bad argument or shape */
+#define DFLASH_ERR_CUDA 2    /* CUDA runtime / launch error */
+#define DFLASH_ERR_OOM 3     /* device allocation failed */
+#define DFLASH_ERR_DEVICE 4  /* a bounded device-side wait expired */
+
+/* Model dimensions (DFlashConfig, mirror_sd/dflash.py:34-50) plus the
+ * capacities the workspace is sized for. head_dim must be 128. */
+typedef struct DFlashDims {
+  int32_t hidden_size;
+  int32_t num_hidden_layers;
+  int32_t intermediate_size;
+  int32_t num_attention_heads;
+  int32_t num_key_value_heads;
+  int32_t head_dim;
+  int32_t vocab_size;
+  int32_t num_target_features; /* len(target_layer_ids), 5 in every config */
+  float rms_norm_eps;
+  float rope_theta;
+  int32_t max_batch;
+  int32_t max_block;
+  int32_t max_ctx;
+} DFlashDims;
+
+/* One decoder layer in the reference's W8A16 format: row-major int8
+ * [out, in] weights with per-output-channel fp16 scales (the bytes
+ * _quantize_weight_q8 returns), fp32 norm weights.  Copied and repacked by
+ * dflash_create; the caller may free them afterwards. */
+typedef struct DFlashLayerWeights {
+  const int8_t* wq; const uint16_t* sq; /* [NQ*128, H] */
+  const int8_t* wk; const uint16_t* sk; /* [NKV*128, H] */
+  const int8_t* wv; const uint16_t* sv; /* [NKV*128, H] */
+  const int8_t* wo; const uint16_t* so; /* [H, NQ*128] */
+  const int8_t* wg; const uint16_t* sg; /* [I, H] */
+  const int8_t* wu; const uint16_t* su; /* [I, H] */
+  const int8_t* wd; const uint16_t* sd; /* [H, I] */
+  const float* input_layernorm;          /* [H] */
+  const float* post_attention_layernorm; /* [H] */
+  const float* q_norm;                   /* [128] */
+  const float* k_norm;                   /* [128] */
+} DFlashLayerWeights;
+
+typedef struct DFlashWeightsView {
+  const uint16_t* fc;          /* bf16 [H, F*H]; copied */
+  const float* hidden_norm;    /* [H]; copied */
+  const float* norm;           /* [H]; copied */
+  const uint16_t* lm_head;     /* bf16 [V, H]: the target's (tied) embedding,
+                                  referenced, NOT copied; must outlive the handle */
+  const DFlashLayerWeights* layers; /* HOST array of num_hidden_layers entries */
+} DFlashWeightsView;
+
+/* One stateless draft step (cache=None in dflash.py): RoPE positions are
+ * rope_offset + row for the ctx_len context rows and rope_offset + ctx_len + j
+ * for the block rows (dflash.py:299-305). */
+typedef struct DFlashForwardArgs {
+  int32_t batch;
+  int32_t block;          /* block_size, 2..max_block, batch*block <= 64 */
+  int32_t ctx_len;        /* context rows per sequence, 0..max_ctx */
+  int32_t rope_offset;
+  int32_t num_layers;     /* 1..num_hidden_layers (DFlashDraftModel.num_draft_layers) */
+  const uint16_t* noise;          /* bf16 [batch, block, H] */
+  const uint16_t* target_hidden;  /* bf16 [batch, ctx_len, F*H] */
+  void* out_hidden;               /* [batch, block, H] final-normed hidden states, or NULL:
+                                     bf16, or fp32 when out_hidden_fp32 != 0 */
+  int32_t out_hidden_fp32;
+  int32_t* out_tokens;            /* [batch, block-1] greedy draft ids, or NULL */
+  const int32_t* target_tokens;   /* [batch, block] verifier posterior, or NULL */
+  int32_t* acc_len;               /* [batch], written when target_tokens != NULL */
+  int32_t* correction;            /* [batch], target_tokens[b][acc_len[b]] */
+  /* Optional phase timing: when n_phase_events >= DFLASH_PHASES, event k
+   * (a cudaEvent_t) is recorded on `stream` at phase boundary k:
+   * 0 start, 1 after RoPE table + residual init, 2 after the fc GEMM,
+   * 3 after hidden_norm, 4 after the context K/V GEMM, 5 after the decoder
+   * layers, 6 after the final norm, 7 after lm_head + argmax (+ accept). */
+  void* const* phase_events;
+  int32_t n_phase_events;
+} DFlashForwardArgs;
+
+#define DFLASH_PHASES 8
+
+int dflash_create(const DFlashDims* dims, const DFlashWeightsView* weights, int device,
+                  void** handle);
+int dflash_forward(void* handle, const DFlashForwardArgs* args, void* stream);
+int dflash_accept(const int32_t* draft, const int32_t* target, int batch, int block,
+                  int32_t* acc_len, int32_t* correction, void* stream);
+int dflash_quantize_q8(const float* w, int oc, int ic, int8_t* q, uint16_t* scale_fp16,
+                       void* stream);
+/* Reads and clears the handle's device error word (DFLASH_ERR_DEVICE when a
+ * kernel gave up on a bounded wait).  Synchronises the given stream. */
+int dflash_device_status(void* handle, void* stream);
+int dflash_destroy(void* handle);
+/* Number of kernel launches the last dflash_forward on this handle issued. */
+int dflash_last_launch_count(void* handle);
+int dflash_last_error(char* buf, size_t len);
+int dflash_version(void);
+
+/* ---- kernel-level entry points (one hot-path kernel each) ---------------- */
+
+/* y[M, N] (f16) = x[M, K] (f16) . (q[N, K] * s[N])^T on the W8A16 skinny
+ * kernel (the q/k/v/o/gate/up/down projections of the block rows; the
+ * reference's conv1x1_proj_q8, ane/src/dflash.rs:146-149).  M <= 64. */
+int dflash_w8_linear(const int8_t* q, const uint16_t* s_fp16, int N, int K, const uint16_t* x_f16,
+                     int M, uint16_t* y_f16, void* stream);
+
+/* D[M, N] (fp32) = A[M, K] . B[N, K]^T on the tcgen05 GEMM; ab_bf16 selects
+ * bf16 (1) or f16 (0) operands (the fc projection, dflash.py:373-378, and the
+ * context K/V projection, dflash.py:293-294). */
+int dflash_tc_gemm(const uint16_t* A, const uint16_t* B, int M, int N, int K, int ab_bf16,
+                   float* D, void* stream);
+
+/* Fused per-head QK RMSNorm + neox RoPE + non-causal GQA attention
+ * (dflash.py:291-317; ANE gqa_tile + attn_out, ane/src/dflash.rs:226-278).
+ * q [batch, NQ, block, 128], k/v [batch, NKV, kv_len, 128] f16;
+ * out [batch, block, NQ*128] f16.  When normrope != 0, q row j is normalised
+ * and rotated at position q_pos0 + j and k row i at k_pos0 + i; otherwise q/k
+ * are used as given.  workspace: dflash_attention_workspace_size() bytes. */
+size_t dflash_attention_workspace_size(int batch, int nq, int nkv, int block, int kv_len);
+int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int batch, int nq,
+                     int nkv, int block, int kv_len, int normrope, const float* q_norm,
+                     const float* k_norm, float rope_theta, int q_pos0, int k_pos0, float eps,
+                     uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Tied lm_head + greedy argmax (+ acceptance when target != NULL) on
+ * final-normed hidden rows: hn [batch, block, H] bf16, E [V, H] bf16; writes
+ * tokens [batch, block-1] for rows 1..block-1 (generate.py:604-606, :722-728).
+ * workspace: dflash_lm_head_workspace_size() bytes. */
+size_t dflash_lm_head_workspace_size(int batch, int block);
+int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H,
+                          int V, int32_t* tokens, const int32_t* target, int32_t* acc_len,
+                          int32_t* correction, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DFLASH_B200_H */

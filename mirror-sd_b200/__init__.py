@@ -1,0 +1,14 @@
+"""mirror-sd_b200: B200-native DFlash draft-model forward (sm_100a CUDA).
+
+Import with ``importlib.import_module("mirror-sd_b200")`` (the folder name
+carries a hyphen).  The compute path is the CUDA library ``lib/libdflash_b200.so``
+(C ABI: ``include/dflash_b200.h``), built by ``build.py``.
+"""
+from . import _native
+from .dflash import (DFlashConfig, DFlashDraftModel, DFlashKVCache, DFlashWeightsQ8, Q8Layer,
+                     accept, build_target_layer_ids, extract_context_feature, quantize_q8, sample)
+from .weights import synth_weights_q8, weights_from_q8_numpy
+
+__all__ = ["DFlashConfig", "DFlashDraftModel", "DFlashKVCache", "DFlashWeightsQ8", "Q8Layer",
+           "accept", "build_target_layer_ids", "extract_context_feature", "quantize_q8", "sample",
+           "synth_weights_q8", "weights_from_q8_numpy"]

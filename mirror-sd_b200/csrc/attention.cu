@@ -1,0 +1,301 @@
+// Non-causal GQA block attention of the DFlash draft (dflash.py:310-319).
+//
+// One CTA per (batch, kv head, KV split).  All G = NQ/NKV query heads that
+// share the kv head are processed together (R = G * block query rows), so each
+// K/V row is read from HBM once per CTA.  One warp per 16-row m-tile; K/V
+// tiles of 64 rows are double-buffered in shared memory with cp.async; QK^T
+// and PV run on mma.sync m16n8k16 (f16 in, fp32 accumulate) with an online
+// base-2 softmax.  Each CTA writes an unnormalised partial (O, m, l) that a
+// combine kernel merges across splits in a fixed order.
+//
+// With `normrope` set the kernel also applies the per-head RMSNorm and neox
+// RoPE of dflash.py:291-305 to the raw Q and K rows as they land in shared
+// memory (the attention-only configuration); in the draft forward both are
+// already applied by the projection epilogues.
+#include "kernels.cuh"
+
+namespace dfl {
+
+
+constexpr int AT_TK = 64;          // kv rows per shared tile
+constexpr int AT_LD = 128 + 8;     // halves per shared row (+16 B pad)
+
+__device__ __forceinline__ void normrope_row(__half* row, const float* w, const float2* cs_row,
+                                             float eps, int lane) {
+  // lane owns d = 4*lane .. 4*lane+3
+  uint2 raw = *reinterpret_cast<uint2*>(row + lane * 4);
+  __half2 h0 = *reinterpret_cast<__half2*>(&raw.x), h1 = *reinterpret_cast<__half2*>(&raw.y);
+  float y[4] = {__low2float(h0), __high2float(h0), __low2float(h1), __high2float(h1)};
+  float ss = warp_sum(y[0] * y[0] + y[1] * y[1] + y[2] * y[2] + y[3] * y[3]);
+  const float r = rsqrtf(ss / 128.0f + eps);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) y[e] = y[e] * r * __ldg(w + lane * 4 + e);
+  float z[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) z[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+  const bool lo = lane < 16;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int i = (lane & 15) * 4 + e;
+    const float2 t = __ldg(cs_row + i);
+    const float c = t.x, s = t.y;
+    y[e] = lo ? (y[e] * c - z[e] * s) : (z[e] * s + y[e] * c);
+  }
+  raw.x = pack_f16x2(y[0], y[1]);
+  raw.y = pack_f16x2(y[2], y[3]);
+  *reinterpret_cast<uint2*>(row + lane * 4) = raw;
+}
+
+__global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int split = blockIdx.x, kvh = blockIdx.y, bi = blockIdx.z;
+  const int G = p.nq / p.nkv;
+  const int R = G * p.block;
+  const int nwarps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int RP = nwarps * 16;
+
+  __half* qs = reinterpret_cast<__half*>(smem);
+  __half* ks = qs + (size_t)RP * AT_LD;               // [2][TK][LD]
+  __half* vs = ks + (size_t)2 * AT_TK * AT_LD;        // [2][TK][LD]
+
+  const int kv0 = split * p.chunk;
+  const int kv1 = min(p.kv_len, kv0 + p.chunk);
+  const int ntiles = (kv1 - kv0 + AT_TK - 1) / AT_TK;
+
+  const __half* qg = p.q + ((size_t)bi * p.nq + (size_t)kvh * G) * p.block * 128;
+  const __half* kg = p.k + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+  const __half* vg = p.v + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+
+  // Q tile (rows >= R zero)
+  for (int idx = threadIdx.x; idx < RP * 16; idx += blockDim.x) {
+    const int r = idx >> 4, cc = (idx & 15) * 8;
+    cp_async16_zfill(smem_u32(qs + (size_t)r * AT_LD + cc), qg + (size_t)min(r, R - 1) * 128 + cc,
+                     r < R);
+  }
+  auto load_kv = [&](int t, int buf) {
+    const int base = kv0 + t * AT_TK;
+    for (int idx = threadIdx.x; idx < AT_TK * 16; idx += blockDim.x) {
+      const int r = idx >> 4, cc = (idx & 15) * 8;
+      const int row = base + r;
+      const bool ok = row < kv1;
+      const size_t off = (size_t)min(row, p.kv_len - 1) * 128 + cc;
+      cp_async16_zfill(smem_u32(ks + ((size_t)buf * AT_TK + r) * AT_LD + cc), kg + off, ok);
+      cp_async16_zfill(smem_u32(vs + ((size_t)buf * AT_TK + r) * AT_LD + cc), vg + off, ok);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+
+  const uint32_t qs_addr = smem_u32(qs);
+  const uint32_t ks_addr = smem_u32(ks);
+  const uint32_t vs_addr = smem_u32(vs);
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) load_kv(t + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (p.normrope) {
+      if (t == 0) {
+        for (int r = warp; r < R; r += nwarps)
+          normrope_row(qs + (size_t)r * AT_LD, p.q_norm,
+                       p.rope + (size_t)(p.q_row0 + r % p.block) * 64, p.eps, lane);
+      }
+      const int base = kv0 + t * AT_TK;
+      for (int r = warp; r < AT_TK; r += nwarps)
+        if (base + r < kv1)
+          normrope_row(ks + ((size_t)buf * AT_TK + r) * AT_LD, p.k_norm,
+                       p.rope + (size_t)(p.k_row0 + base + r) * 64, p.eps, lane);
+      __syncthreads();
+    }
+
+    // S = Q K^T for this warp's 16 rows x 64 kv
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldmatrix_x4(qs_addr + (uint32_t)(((warp * 16 + (lane & 15)) * AT_LD + kk * 16 + (lane >> 4) * 8) * 2),
+                  a0, a1, a2, a3);
+#pragma unroll
+      for (int nt = 0; nt < 8; nt += 2) {
+        const int mat = lane >> 3;
+        const int krow = nt * 8 + (lane & 7) + (mat >> 1) * 8;
+        const int kcol = kk * 16 + (mat & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(ks_addr + (uint32_t)((((size_t)buf * AT_TK + krow) * AT_LD + kcol) * 2), b0, b1,
+                    b2, b3);
+        mma_f16_16816(s[nt], a0, a1, a2, a3, b0, b1);
+        mma_f16_16816(s[nt + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // scale, mask, online softmax (rows g and g+8 of the m-tile)
+    const int base = kv0 + t * AT_TK;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = base + nt * 8 + 2 * c + (e & 1);
+        float val = s[nt][e] * p.scale_log2;
+        if (col >= kv1) val = -INFINITY;
+        s[nt][e] = val;
+        mx[e >> 1] = fmaxf(mx[e >> 1], val);
+      }
+    }
+    float corr[2], msafe[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float mnew = fmaxf(m_run[h], mx[h]);
+      msafe[h] = (mnew == -INFINITY) ? 0.f : mnew;
+      corr[h] = exp2f(m_run[h] - msafe[h]);
+      m_run[h] = mnew;
+    }
+    float ls[2] = {0.f, 0.f};
+    uint32_t pa[8][2];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const float p0 = exp2f(s[nt][0] - msafe[0]);
+      const float p1 = exp2f(s[nt][1] - msafe[0]);
+      const float p2 = exp2f(s[nt][2] - msafe[1]);
+      const float p3 = exp2f(s[nt][3] - msafe[1]);
+      ls[0] += p0 + p1;
+      ls[1] += p2 + p3;
+      pa[nt][0] = pack_f16x2(p0, p1);
+      pa[nt][1] = pack_f16x2(p2, p3);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      ls[h] += __shfl_xor_sync(0xffffffffu, ls[h], 1);
+      ls[h] += __shfl_xor_sync(0xffffffffu, ls[h], 2);
+      l_run[h] = l_run[h] * corr[h] + ls[h];
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      o[i][0] *= corr[0]; o[i][1] *= corr[0];
+      o[i][2] *= corr[1]; o[i][3] *= corr[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kt = 0; kt < 4; ++kt) {
+      const uint32_t a0 = pa[2 * kt][0], a1 = pa[2 * kt][1];
+      const uint32_t a2 = pa[2 * kt + 1][0], a3 = pa[2 * kt + 1][1];
+#pragma unroll
+      for (int dt = 0; dt < 16; dt += 2) {
+        const int mat = lane >> 3;
+        const int vrow = kt * 16 + (lane & 7) + (mat & 1) * 8;
+        const int vcol = dt * 8 + (mat >> 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(vs_addr + (uint32_t)((((size_t)buf * AT_TK + vrow) * AT_LD + vcol) * 2), b0,
+                          b1, b2, b3);
+        mma_f16_16816(o[dt], a0, a1, a2, a3, b0, b1);
+        mma_f16_16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
+  }
+
+  // partials
+  const size_t pbase = (((size_t)bi * p.nkv + kvh) * p.splits + split) * (size_t)R;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = warp * 16 + g + h * 8;
+    if (r < R) {
+      float* orow = p.opart + (pbase + r) * 128;
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+        *reinterpret_cast<float2*>(orow + dt * 8 + 2 * c) = make_float2(o[dt][2 * h], o[dt][2 * h + 1]);
+      if (c == 0) {
+        p.mpart[pbase + r] = m_run[h];
+        p.lpart[pbase + r] = l_run[h];
+      }
+    }
+  }
+}
+
+// merge split partials -> out [b*B, NQ*128] f16 (row = bi*B + j, col = head*128 + d)
+__global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out) {
+  const int G = p.nq / p.nkv;
+  const int R = G * p.block;
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int bi = blockIdx.y;
+  const int rows_per_b = p.nq * p.block;
+  if (warp_global >= rows_per_b) return;
+  const int head = warp_global / p.block, j = warp_global % p.block;
+  const int kvh = head / G;
+  const int r = (head - kvh * G) * p.block + j;
+  const size_t base = (((size_t)bi * p.nkv + kvh) * p.splits) * (size_t)R + r;
+  float M = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.mpart[base + (size_t)s * R]);
+  const float Ms = (M == -INFINITY) ? 0.f : M;
+  float L = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < p.splits; ++s) {
+    const size_t idx = base + (size_t)s * R;
+    const float w = exp2f(p.mpart[idx] - Ms);
+    L += p.lpart[idx] * w;
+    const float4 ov = *reinterpret_cast<const float4*>(p.opart + idx * 128 + lane * 4);
+    acc[0] += ov.x * w; acc[1] += ov.y * w; acc[2] += ov.z * w; acc[3] += ov.w * w;
+  }
+  const float inv = 1.0f / L;
+  uint2 pk;
+  pk.x = pack_f16x2(acc[0] * inv, acc[1] * inv);
+  pk.y = pack_f16x2(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(out + ((size_t)bi * p.block + j) * ((size_t)p.nq * 128) +
+                            (size_t)head * 128 + lane * 4) = pk;
+}
+
+size_t attn_smem_bytes(int nq, int nkv, int block) {
+  const int R = nq / nkv * block;
+  const int RP = (R + 15) / 16 * 16;
+  return ((size_t)RP * AT_LD + (size_t)4 * AT_TK * AT_LD) * 2;
+}
+
+// choose the KV split so that b * NKV * splits covers the SMs about twice
+void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits) {
+  const int per = batch * nkv;
+  int s = (2 * num_sms + per - 1) / per;
+  const int max_s = (kv_len + AT_TK - 1) / AT_TK;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  int ch = (kv_len + s - 1) / s;
+  ch = (ch + AT_TK - 1) / AT_TK * AT_TK;
+  s = (kv_len + ch - 1) / ch;
+  *chunk = ch;
+  *splits = s;
+}
+
+cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st) {
+  const int G = p.nq / p.nkv;
+  const int R = G * p.block;
+  if (p.nq % p.nkv || R < 1 || R > 192 || p.kv_len < 1 || p.chunk % AT_TK) return cudaErrorInvalidValue;
+  const int nwarps = (R + 15) / 16;
+  const size_t smem = attn_smem_bytes(p.nq, p.nkv, p.block);
+  cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  attn_partial_kernel<<<dim3(p.splits, p.nkv, batch), nwarps * 32, smem, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int rows = p.nq * p.block;
+  attn_combine_kernel<<<dim3((rows + 7) / 8, batch), 256, 0, st>>>(p, out);
+  return cudaGetLastError();
+}
+
+}  // namespace dfl

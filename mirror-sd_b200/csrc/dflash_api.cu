@@ -1,0 +1,596 @@
+// C ABI (include/dflash_b200.h): handle with device-resident weights and
+// workspace, the stateless draft step, and the kernel-level entry points.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/dflash_b200.h"
+#include "kernels.cuh"
+
+using namespace dfl;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+#define CK(call)                                                                        \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess) {                                                            \
+      if (e_ == cudaErrorInvalidValue)                                                  \
+        return fail(DFLASH_ERR_INVALID, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                    __FILE__, __LINE__);                                                \
+      return fail(e_ == cudaErrorMemoryAllocation ? DFLASH_ERR_OOM : DFLASH_ERR_CUDA,   \
+                  "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__);  \
+    }                                                                                   \
+  } while (0)
+
+// device allocations owned by a handle, released together
+struct Arena {
+  std::vector<void*> ptrs;
+  template <class T>
+  cudaError_t alloc(T** p, size_t count) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, count * sizeof(T) > 0 ? count * sizeof(T) : 16);
+    if (e != cudaSuccess) return e;
+    ptrs.push_back(q);
+    *p = static_cast<T*>(q);
+    return cudaSuccess;
+  }
+  void release() {
+    for (void* p : ptrs) cudaFree(p);
+    ptrs.clear();
+  }
+};
+
+struct Layer {
+  uint8_t* w_qkv; float* s_qkv;
+  uint8_t* w_o; float* s_o;
+  uint8_t* w_gu; float* s_gu;
+  uint8_t* w_d; float* s_d;
+  float *in_norm, *post_norm, *q_norm;
+};
+
+struct Handle {
+  int device = 0;
+  int num_sms = 148;
+  int max_splits = 16;
+  DFlashDims d{};
+  Arena arena;
+  std::mutex mu;
+  // weights
+  __nv_bfloat16* fc = nullptr;
+  const __nv_bfloat16* lm_head = nullptr;
+  float *hidden_norm = nullptr, *norm = nullptr, *inv_freq = nullptr;
+  float* k_norm_all = nullptr;     // [L, 128]
+  __half* w_kv_ctx = nullptr;      // [L*2*NKV*128, H] exact f16 of the int8 K|V weights
+  float* s_kv_ctx = nullptr;       // [L*2*NKV*128]
+  std::vector<Layer> layers;
+  // workspace
+  float2* rope = nullptr;
+  float *h = nullptr, *hstat = nullptr;
+  float* ctx_raw = nullptr;          // fc output, fp32 (hidden_norm input)
+  float* ctx_part = nullptr;
+  __half* ctx_n = nullptr;
+  __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
+  float *opart = nullptr, *mpart = nullptr, *lpart = nullptr;
+  size_t attn_part_rows = 0;
+  __nv_bfloat16* hn = nullptr;
+  float* lm_val = nullptr;
+  int* lm_idx = nullptr;
+  int* dev_err = nullptr;
+  int last_launches = 0;
+};
+
+int check_dims(const DFlashDims* d) {
+  if (!d) return fail(DFLASH_ERR_INVALID, "dims is NULL");
+  if (d->head_dim != 128) return fail(DFLASH_ERR_INVALID, "head_dim must be 128 (got %d)", d->head_dim);
+  if (d->hidden_size <= 0 || d->hidden_size % 256)
+    return fail(DFLASH_ERR_INVALID, "hidden_size must be a positive multiple of 256 (got %d)", d->hidden_size);
+  if (d->intermediate_size <= 0 || d->intermediate_size % 128)
+    return fail(DFLASH_ERR_INVALID, "intermediate_size must be a multiple of 128 (got %d)", d->intermediate_size);
+  if (d->num_attention_heads <= 0 || d->num_key_value_heads <= 0 ||
+      d->num_attention_heads % d->num_key_value_heads)
+    return fail(DFLASH_ERR_INVALID, "num_attention_heads must be a multiple of num_key_value_heads");
+  if ((d->num_attention_heads + 2 * d->num_key_value_heads) % 2)
+    return fail(DFLASH_ERR_INVALID, "num_attention_heads + 2*num_key_value_heads must be even");
+  if (d->num_hidden_layers < 1 || d->vocab_size < 1 || d->num_target_features < 1)
+    return fail(DFLASH_ERR_INVALID, "layers, vocab and target features must be positive");
+  if (d->max_batch < 1 || d->max_block < 2 || d->max_block > 1024 || d->max_ctx < 0 ||
+      d->max_batch * d->max_block > 64)
+    return fail(DFLASH_ERR_INVALID, "capacities: max_batch*max_block must be in [2, 64], max_ctx >= 0");
+  const int G = d->num_attention_heads / d->num_key_value_heads;
+  if (G * d->max_block > 192)
+    return fail(DFLASH_ERR_INVALID, "query rows per kv head (heads/kv_heads * block) must be <= 192");
+  return DFLASH_OK;
+}
+
+size_t attn_rows_capacity(int max_batch, int nkv, int R, int kv_len_max, int num_sms) {
+  size_t best = 0;
+  for (int b = 1; b <= max_batch; ++b) {
+    int chunk, splits;
+    attn_pick_split(b, nkv, kv_len_max, num_sms, &chunk, &splits);
+    // splits can only shrink for shorter kv_len, so the max-length case bounds it
+    size_t rows = (size_t)b * nkv * splits * R;
+    if (rows > best) best = rows;
+    // also cover every shorter length that yields more splits (never: splits <= kv tiles)
+  }
+  return best;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dflash_version(void) { return 1; }
+
+int dflash_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return (int)g_err.size();
+  snprintf(buf, len, "%s", g_err.c_str());
+  return (int)g_err.size();
+}
+
+int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device, void** out) {
+  if (int r = check_dims(dims)) return r;
+  if (!w || !out || !w->fc || !w->hidden_norm || !w->norm || !w->lm_head || !w->layers)
+    return fail(DFLASH_ERR_INVALID, "weights view has NULL members");
+  const DFlashDims d = *dims;
+  const int H = d.hidden_size, I = d.intermediate_size, NQ = d.num_attention_heads,
+            NKV = d.num_key_value_heads, L = d.num_hidden_layers, F = d.num_target_features;
+  for (int l = 0; l < L; ++l) {
+    const DFlashLayerWeights& lw = w->layers[l];
+    if (!lw.wq || !lw.sq || !lw.wk || !lw.sk || !lw.wv || !lw.sv || !lw.wo || !lw.so || !lw.wg ||
+        !lw.sg || !lw.wu || !lw.su || !lw.wd || !lw.sd || !lw.input_layernorm ||
+        !lw.post_attention_layernorm || !lw.q_norm || !lw.k_norm)
+      return fail(DFLASH_ERR_INVALID, "layer %d has NULL weight pointers", l);
+  }
+  CK(cudaSetDevice(device));
+  Handle* hd = new Handle();
+  hd->device = device;
+  hd->d = d;
+  int rc = DFLASH_OK;
+  auto cleanup = [&]() {
+    cudaDeviceSynchronize();
+    hd->arena.release();
+    delete hd;
+  };
+#define CKC(call)                         \
+  do {                                    \
+    cudaError_t e_ = (call);              \
+    if (e_ != cudaSuccess) {              \
+      rc = fail(e_ == cudaErrorMemoryAllocation ? DFLASH_ERR_OOM : DFLASH_ERR_CUDA, "%s: %s", #call, \
+                cudaGetErrorString(e_));  \
+      cleanup();                          \
+      return rc;                          \
+    }                                     \
+  } while (0)
+  CKC(cudaDeviceGetAttribute(&hd->num_sms, cudaDevAttrMultiProcessorCount, device));
+  Arena& A = hd->arena;
+  cudaStream_t st = 0;
+  // ---- weights
+  const size_t fc_elems = (size_t)H * F * H;
+  CKC(A.alloc(&hd->fc, fc_elems));
+  CKC(cudaMemcpyAsync(hd->fc, w->fc, fc_elems * 2, cudaMemcpyDeviceToDevice, st));
+  hd->lm_head = reinterpret_cast<const __nv_bfloat16*>(w->lm_head);
+  CKC(A.alloc(&hd->hidden_norm, H));
+  CKC(A.alloc(&hd->norm, H));
+  CKC(cudaMemcpyAsync(hd->hidden_norm, w->hidden_norm, H * 4, cudaMemcpyDeviceToDevice, st));
+  CKC(cudaMemcpyAsync(hd->norm, w->norm, H * 4, cudaMemcpyDeviceToDevice, st));
+  {
+    std::vector<float> inv(64);
+    for (int i = 0; i < 64; ++i) inv[i] = (float)std::pow((double)d.rope_theta, -2.0 * i / 128.0);
+    CKC(A.alloc(&hd->inv_freq, 64));
+    CKC(cudaMemcpy(hd->inv_freq, inv.data(), 64 * 4, cudaMemcpyHostToDevice));
+  }
+  const int nqkv = (NQ + 2 * NKV) * 128;
+  const int nkvc = 2 * NKV * 128;
+  CKC(A.alloc(&hd->k_norm_all, (size_t)L * 128));
+  CKC(A.alloc(&hd->w_kv_ctx, (size_t)L * nkvc * H));
+  CKC(A.alloc(&hd->s_kv_ctx, (size_t)L * nkvc));
+  const int big = 1 << 30;
+  for (int l = 0; l < L; ++l) {
+    const DFlashLayerWeights& lw = w->layers[l];
+    Layer ly{};
+    CKC(A.alloc(&ly.w_qkv, (size_t)nqkv * H));
+    CKC(A.alloc(&ly.s_qkv, nqkv));
+    CKC(w8_repack_launch(lw.wq, NQ * 128, H, ly.w_qkv, big, 0, 0, st));
+    CKC(w8_repack_launch(lw.wk, NKV * 128, H, ly.w_qkv, big, 0, NQ * 8, st));
+    CKC(w8_repack_launch(lw.wv, NKV * 128, H, ly.w_qkv, big, 0, (NQ + NKV) * 8, st));
+    CKC(w8_scale_launch((const __half*)lw.sq, NQ * 128, ly.s_qkv, big, 0, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, ly.s_qkv, big, 0, NQ * 8, st));
+    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, ly.s_qkv, big, 0, (NQ + NKV) * 8, st));
+    CKC(A.alloc(&ly.w_o, (size_t)H * NQ * 128));
+    CKC(A.alloc(&ly.s_o, H));
+    CKC(w8_repack_launch(lw.wo, H, NQ * 128, ly.w_o, big, 0, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.so, H, ly.s_o, big, 0, 0, st));
+    // gate/up interleaved per 256-channel tile: 8 gate row-blocks then 8 up row-blocks
+    CKC(A.alloc(&ly.w_gu, (size_t)2 * I * H));
+    CKC(A.alloc(&ly.s_gu, 2 * I));
+    CKC(w8_repack_launch(lw.wg, I, H, ly.w_gu, 8, 16, 0, st));
+    CKC(w8_repack_launch(lw.wu, I, H, ly.w_gu, 8, 16, 8, st));
+    CKC(w8_scale_launch((const __half*)lw.sg, I, ly.s_gu, 8, 16, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.su, I, ly.s_gu, 8, 16, 8, st));
+    CKC(A.alloc(&ly.w_d, (size_t)H * I));
+    CKC(A.alloc(&ly.s_d, H));
+    CKC(w8_repack_launch(lw.wd, H, I, ly.w_d, big, 0, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.sd, H, ly.s_d, big, 0, 0, st));
+    CKC(A.alloc(&ly.in_norm, H));
+    CKC(A.alloc(&ly.post_norm, H));
+    CKC(A.alloc(&ly.q_norm, 128));
+    CKC(cudaMemcpyAsync(ly.in_norm, lw.input_layernorm, H * 4, cudaMemcpyDeviceToDevice, st));
+    CKC(cudaMemcpyAsync(ly.post_norm, lw.post_attention_layernorm, H * 4, cudaMemcpyDeviceToDevice, st));
+    CKC(cudaMemcpyAsync(ly.q_norm, lw.q_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
+    CKC(cudaMemcpyAsync(hd->k_norm_all + l * 128, lw.k_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
+    // context K|V operand: exact f16 of the int8 values, scales applied in the epilogue
+    __half* kv = hd->w_kv_ctx + (size_t)l * nkvc * H;
+    CKC(i8_to_f16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
+    CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
+    CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 8, st));
+    hd->layers.push_back(ly);
+  }
+  // ---- workspace
+  const int Mx = d.max_batch * d.max_block;
+  const int Cx = d.max_batch * d.max_ctx;
+  const int kvcap = d.max_ctx + d.max_block;
+  const int G = NQ / NKV;
+  CKC(A.alloc(&hd->rope, (size_t)kvcap * 64));
+  CKC(A.alloc(&hd->h, (size_t)Mx * H));
+  CKC(A.alloc(&hd->hstat, (size_t)(H / 128) * Mx));
+  if (Cx > 0) {
+    CKC(A.alloc(&hd->ctx_raw, (size_t)Cx * H));
+    CKC(A.alloc(&hd->ctx_part, (size_t)(H / 256) * Cx));
+    CKC(A.alloc(&hd->ctx_n, (size_t)Cx * H));
+  }
+  const size_t kv_elems = (size_t)L * d.max_batch * NKV * kvcap * 128;
+  CKC(A.alloc(&hd->K, kv_elems));
+  CKC(A.alloc(&hd->V, kv_elems));
+  CKC(A.alloc(&hd->Q, (size_t)Mx * NQ * 128));
+  CKC(A.alloc(&hd->attn_out, (size_t)Mx * NQ * 128));
+  CKC(A.alloc(&hd->act, (size_t)Mx * I));
+  hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, kvcap, hd->num_sms);
+  CKC(A.alloc(&hd->opart, hd->attn_part_rows * 128));
+  CKC(A.alloc(&hd->mpart, hd->attn_part_rows));
+  CKC(A.alloc(&hd->lpart, hd->attn_part_rows));
+  CKC(A.alloc(&hd->hn, (size_t)Mx * H));
+  CKC(A.alloc(&hd->lm_val, (size_t)hd->num_sms * Mx));
+  CKC(A.alloc(&hd->lm_idx, (size_t)hd->num_sms * Mx));
+  CKC(A.alloc(&hd->dev_err, 1));
+  CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
+  CKC(cudaDeviceSynchronize());
+#undef CKC
+  *out = hd;
+  return DFLASH_OK;
+}
+
+int dflash_destroy(void* handle) {
+  if (!handle) return fail(DFLASH_ERR_INVALID, "NULL handle");
+  Handle* hd = static_cast<Handle*>(handle);
+  cudaSetDevice(hd->device);
+  cudaDeviceSynchronize();
+  hd->arena.release();
+  delete hd;
+  return DFLASH_OK;
+}
+
+int dflash_device_status(void* handle, void* stream) {
+  if (!handle) return fail(DFLASH_ERR_INVALID, "NULL handle");
+  Handle* hd = static_cast<Handle*>(handle);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  CK(cudaMemcpyAsync(&v, hd->dev_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (v != 0) {
+    CK(cudaMemsetAsync(hd->dev_err, 0, sizeof(int), st));
+    CK(cudaStreamSynchronize(st));
+    return fail(DFLASH_ERR_DEVICE, "device wait limit reached (code %d)", v);
+  }
+  return DFLASH_OK;
+}
+
+int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
+  if (!handle || !a) return fail(DFLASH_ERR_INVALID, "NULL handle or args");
+  Handle* hd = static_cast<Handle*>(handle);
+  const DFlashDims& d = hd->d;
+  const int H = d.hidden_size, I = d.intermediate_size, NQ = d.num_attention_heads,
+            NKV = d.num_key_value_heads, F = d.num_target_features;
+  const int b = a->batch, B = a->block, C = a->ctx_len, nl = a->num_layers;
+  if (b < 1 || b > d.max_batch) return fail(DFLASH_ERR_INVALID, "batch %d outside [1, %d]", b, d.max_batch);
+  if (B < 2 || B > d.max_block) return fail(DFLASH_ERR_INVALID, "block %d outside [2, %d]", B, d.max_block);
+  if (C < 0 || C > d.max_ctx) return fail(DFLASH_ERR_INVALID, "ctx_len %d outside [0, %d]", C, d.max_ctx);
+  if (nl < 1 || nl > d.num_hidden_layers)
+    return fail(DFLASH_ERR_INVALID, "num_layers %d outside [1, %d]", nl, d.num_hidden_layers);
+  if (a->rope_offset < 0) return fail(DFLASH_ERR_INVALID, "rope_offset must be >= 0");
+  if (!a->noise || (C > 0 && !a->target_hidden))
+    return fail(DFLASH_ERR_INVALID, "noise / target_hidden must not be NULL");
+  if (a->target_tokens && (!a->acc_len || !a->correction))
+    return fail(DFLASH_ERR_INVALID, "acc_len and correction are required with target_tokens");
+  std::lock_guard<std::mutex> lock(hd->mu);
+  CK(cudaSetDevice(hd->device));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int M = b * B;
+  const int kv_cap = C + B;
+  const int G = NQ / NKV;
+  const size_t layer_stride = (size_t)b * NKV * kv_cap * 128;
+  const bool timing = a->phase_events && a->n_phase_events >= DFLASH_PHASES;
+  auto mark = [&](int k) -> cudaError_t {
+    return timing ? cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[k]), st) : cudaSuccess;
+  };
+  int launches = 0;
+
+  CK(mark(0));
+  CK(rope_table_launch(a->rope_offset, kv_cap, hd->inv_freq, hd->rope, st));
+  CK(init_h_launch(reinterpret_cast<const __nv_bfloat16*>(a->noise), M, H, hd->h, hd->hstat, st));
+  launches += 2;
+  CK(mark(1));
+
+  if (C > 0) {
+    TcParams fp{};
+    fp.M = b * C; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
+    fp.out_f32 = hd->ctx_raw; fp.sumsq_part = hd->ctx_part;
+    CK(tc_gemm_launch(a->target_hidden, hd->fc, true, kTcFc, fp, st));
+    CK(mark(2));
+    CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, b * C, H, hd->hidden_norm, d.rms_norm_eps,
+                       hd->ctx_n, st));
+    CK(mark(3));
+    TcParams kp{};
+    kp.M = b * C; kp.N = nl * 2 * NKV * 128; kp.K = H; kp.err = hd->dev_err;
+    kp.scale = hd->s_kv_ctx; kp.k_norm = hd->k_norm_all; kp.rope = hd->rope;
+    kp.k_out = hd->K; kp.v_out = hd->V; kp.layer_stride = layer_stride;
+    kp.nkv = NKV; kp.rows_per_seq = C; kp.kv_cap = kv_cap; kp.kv_row0 = 0; kp.eps = d.rms_norm_eps;
+    CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, false, kTcCtxKV, kp, st));
+    CK(mark(4));
+    launches += 3;
+  } else {
+    CK(mark(2));
+    CK(mark(3));
+    CK(mark(4));
+  }
+
+  int chunk, splits;
+  attn_pick_split(b, NKV, kv_cap, hd->num_sms, &chunk, &splits);
+  if ((size_t)b * NKV * splits * G * B > hd->attn_part_rows)
+    return fail(DFLASH_ERR_INVALID, "attention workspace too small");
+  int hparts = 1;
+  for (int l = 0; l < nl; ++l) {
+    const Layer& ly = hd->layers[l];
+    __half* Kl = hd->K + l * layer_stride;
+    __half* Vl = hd->V + l * layer_stride;
+    // q | k | v of the block rows: input RMSNorm fused into the activation load
+    W8Params p{};
+    p.w = ly.w_qkv; p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
+    p.h = hd->h; p.hstat = hd->hstat; p.hparts = hparts; p.norm_w = ly.in_norm; p.eps = d.rms_norm_eps;
+    p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
+    p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.kv_rows = kv_cap;
+    p.kv_row0 = C; p.err = hd->dev_err;
+    p.splits = w8_pick_splits(p.N, p.K, M, hd->num_sms, hd->max_splits);
+    CK(w8_gemm_launch(p, kQKV, kXHNorm, st));
+    // attention over [context ; block]
+    AttnParams ap{};
+    ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kv_cap;
+    ap.kv_cap = kv_cap; ap.chunk = chunk; ap.splits = splits; ap.opart = hd->opart;
+    ap.mpart = hd->mpart; ap.lpart = hd->lpart;
+    ap.scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+    ap.normrope = 0;
+    CK(attn_launch(ap, b, hd->attn_out, st));
+    // o_proj + residual
+    W8Params o{};
+    o.w = ly.w_o; o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
+    o.h_out = hd->h; o.hstat_out = hd->hstat; o.err = hd->dev_err;
+    o.splits = w8_pick_splits(o.N, o.K, M, hd->num_sms, hd->max_splits);
+    CK(w8_gemm_launch(o, kResid, kXF16, st));
+    hparts = H / 128;
+    // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
+    W8Params gu{};
+    gu.w = ly.w_gu; gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
+    gu.h = hd->h; gu.hstat = hd->hstat; gu.hparts = hparts; gu.norm_w = ly.post_norm;
+    gu.eps = d.rms_norm_eps; gu.act = hd->act; gu.err = hd->dev_err;
+    gu.splits = w8_pick_splits(gu.N, gu.K, M, hd->num_sms, hd->max_splits);
+    CK(w8_gemm_launch(gu, kSiluMul, kXHNorm, st));
+    // down + residual
+    W8Params dn{};
+    dn.w = ly.w_d; dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
+    dn.h_out = hd->h; dn.hstat_out = hd->hstat; dn.err = hd->dev_err;
+    dn.splits = w8_pick_splits(dn.N, dn.K, M, hd->num_sms, hd->max_splits);
+    CK(w8_gemm_launch(dn, kResid, kXF16, st));
+    launches += 6;  // qkv, attention partial + combine, o, gate|up, down
+  }
+  CK(mark(5));
+  CK(final_norm_launch(hd->h, hd->hstat, hparts, M, H, hd->norm, d.rms_norm_eps, hd->hn,
+                       a->out_hidden, a->out_hidden_fp32 != 0, st));
+  launches += 1;
+  CK(mark(6));
+  if (a->out_tokens || a->target_tokens) {
+    LmParams lp{};
+    lp.E = hd->lm_head; lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
+    lp.best_val = hd->lm_val; lp.best_idx = hd->lm_idx;
+    CK(lm_argmax_launch(lp, hd->num_sms, st));
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, hd->num_sms, M, B, b, a->out_tokens,
+                            a->target_tokens, a->acc_len, a->correction, st));
+    launches += 2;
+  }
+  CK(mark(7));
+  hd->last_launches = launches;
+  return DFLASH_OK;
+}
+
+int dflash_last_launch_count(void* handle) {
+  if (!handle) return fail(DFLASH_ERR_INVALID, "NULL handle");
+  return static_cast<Handle*>(handle)->last_launches;
+}
+
+int dflash_accept(const int32_t* draft, const int32_t* target, int batch, int block,
+                  int32_t* acc_len, int32_t* correction, void* stream) {
+  if (!draft || !target || !acc_len || !correction) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (batch < 1 || block < 2) return fail(DFLASH_ERR_INVALID, "batch >= 1 and block >= 2 required");
+  CK(accept_launch(draft, target, batch, block, acc_len, correction, static_cast<cudaStream_t>(stream)));
+  return DFLASH_OK;
+}
+
+int dflash_quantize_q8(const float* w, int oc, int ic, int8_t* q, uint16_t* s, void* stream) {
+  if (!w || !q || !s) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (oc < 1 || ic < 1) return fail(DFLASH_ERR_INVALID, "oc and ic must be positive");
+  CK(quantize_q8_launch(w, oc, ic, q, reinterpret_cast<__half*>(s), static_cast<cudaStream_t>(stream)));
+  return DFLASH_OK;
+}
+
+// ---------------------------------------------------------------- kernel-level
+int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uint16_t* x, int M,
+                     uint16_t* y, void* stream) {
+  if (!q || !s || !x || !y) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (N % 256 || K % 64 || M < 1 || M > 64)
+    return fail(DFLASH_ERR_INVALID, "need N %% 256 == 0, K %% 64 == 0, 1 <= M <= 64");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  uint8_t* wp = nullptr;
+  float* sp = nullptr;
+  CK(cudaMallocAsync(&wp, (size_t)N * K, st));
+  CK(cudaMallocAsync(&sp, (size_t)N * 4, st));
+  CK(w8_repack_launch(q, N, K, wp, 1 << 30, 0, 0, st));
+  CK(w8_scale_launch(reinterpret_cast<const __half*>(s), N, sp, 1 << 30, 0, 0, st));
+  W8Params p{};
+  p.w = wp; p.scale = sp; p.N = N; p.K = K; p.M = M;
+  p.x = reinterpret_cast<const __half*>(x); p.y = reinterpret_cast<__half*>(y);
+  p.splits = w8_pick_splits(N, K, M, sms, 16);
+  cudaError_t e = w8_gemm_launch(p, kStore, kXF16, st);
+  cudaFreeAsync(wp, st);
+  cudaFreeAsync(sp, st);
+  CK(e);
+  return DFLASH_OK;
+}
+
+int dflash_tc_gemm(const uint16_t* A, const uint16_t* B, int M, int N, int K, int ab_bf16, float* D,
+                   void* stream) {
+  if (!A || !B || !D) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (M < 1 || N % 256 || K % 64 || K < 64)
+    return fail(DFLASH_ERR_INVALID, "need M >= 1, N %% 256 == 0, K %% 64 == 0");
+  TcParams p{};
+  p.M = M; p.N = N; p.K = K; p.out_f32 = D;
+  int* err = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CK(cudaMallocAsync(&err, sizeof(int), st));
+  CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  p.err = err;
+  cudaError_t e = tc_gemm_launch(A, B, ab_bf16 != 0, kTcStoreF32, p, st);
+  int hv = 0;
+  if (e == cudaSuccess) {
+    cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    e = cudaStreamSynchronize(st);
+  }
+  cudaFreeAsync(err, st);
+  CK(e);
+  if (hv) return fail(DFLASH_ERR_DEVICE, "tcgen05 GEMM gave up on a bounded wait (code %d)", hv);
+  return DFLASH_OK;
+}
+
+size_t dflash_attention_workspace_size(int batch, int nq, int nkv, int block, int kv_len) {
+  if (batch < 1 || nkv < 1 || nq % nkv || kv_len < 1) return 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int chunk, splits;
+  attn_pick_split(batch, nkv, kv_len, sms, &chunk, &splits);
+  const size_t rows = (size_t)batch * nkv * splits * (nq / nkv) * block;
+  const size_t rope_rows = (size_t)kv_len + block;
+  return rows * 130 * 4 + rope_rows * 64 * 8 + 64 * 4 + 256;
+}
+
+int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int batch, int nq,
+                     int nkv, int block, int kv_len, int normrope, const float* q_norm,
+                     const float* k_norm, float rope_theta, int q_pos0, int k_pos0, float eps,
+                     uint16_t* out, void* workspace, size_t ws_bytes, void* stream) {
+  if (!q || !k || !v || !out || !workspace) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (batch < 1 || nkv < 1 || nq % nkv || block < 1 || kv_len < 1)
+    return fail(DFLASH_ERR_INVALID, "bad attention shape");
+  if ((nq / nkv) * block > 192) return fail(DFLASH_ERR_INVALID, "heads/kv_heads * block must be <= 192");
+  if (normrope && (!q_norm || !k_norm || q_pos0 < 0 || k_pos0 < 0))
+    return fail(DFLASH_ERR_INVALID, "normrope needs q_norm, k_norm and non-negative positions");
+  const size_t need = dflash_attention_workspace_size(batch, nq, nkv, block, kv_len);
+  if (ws_bytes < need) return fail(DFLASH_ERR_INVALID, "workspace too small (%zu < %zu)", ws_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  int chunk, splits;
+  attn_pick_split(batch, nkv, kv_len, sms, &chunk, &splits);
+  const size_t rows = (size_t)batch * nkv * splits * (nq / nkv) * block;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  AttnParams p{};
+  p.opart = reinterpret_cast<float*>(ws);
+  p.mpart = p.opart + rows * 128;
+  p.lpart = p.mpart + rows;
+  float2* rope = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(p.lpart + rows) + 15) & ~uintptr_t(15));
+  float* inv = reinterpret_cast<float*>(rope + (size_t)(kv_len + block) * 64);
+  p.q = reinterpret_cast<const __half*>(q);
+  p.k = reinterpret_cast<const __half*>(k);
+  p.v = reinterpret_cast<const __half*>(v);
+  p.nq = nq; p.nkv = nkv; p.block = block; p.kv_len = kv_len; p.kv_cap = kv_len;
+  p.chunk = chunk; p.splits = splits;
+  p.scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+  p.normrope = normrope;
+  if (normrope) {
+    // table rows cover both position ranges: row r <-> position r
+    const int maxpos = std::max(q_pos0 + block, k_pos0 + kv_len);
+    if ((size_t)maxpos > (size_t)(kv_len + block))
+      return fail(DFLASH_ERR_INVALID, "positions must lie below kv_len + block");
+    std::vector<float> invh(64);
+    for (int i = 0; i < 64; ++i) invh[i] = (float)std::pow((double)rope_theta, -2.0 * i / 128.0);
+    CK(cudaMemcpyAsync(inv, invh.data(), 64 * 4, cudaMemcpyHostToDevice, st));
+    CK(rope_table_launch(0, kv_len + block, inv, rope, st));
+    p.q_norm = q_norm; p.k_norm = k_norm; p.rope = rope; p.eps = eps;
+    p.q_row0 = q_pos0; p.k_row0 = k_pos0;
+  }
+  CK(attn_launch(p, batch, reinterpret_cast<__half*>(out), st));
+  return DFLASH_OK;
+}
+
+size_t dflash_lm_head_workspace_size(int batch, int block) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return (size_t)sms * batch * block * 8 + 256;
+}
+
+int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H, int V,
+                          int32_t* tokens, const int32_t* target, int32_t* acc_len, int32_t* correction,
+                          void* workspace, size_t ws_bytes, void* stream) {
+  if (!hn || !E || !workspace) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (batch < 1 || block < 2 || batch * block > 64 || H % 32 || V < 1)
+    return fail(DFLASH_ERR_INVALID, "bad lm_head shape");
+  if (target && (!acc_len || !correction)) return fail(DFLASH_ERR_INVALID, "acc_len/correction required");
+  if (ws_bytes < dflash_lm_head_workspace_size(batch, block))
+    return fail(DFLASH_ERR_INVALID, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int M = batch * block;
+  LmParams p{};
+  p.E = reinterpret_cast<const __nv_bfloat16*>(E);
+  p.hn = reinterpret_cast<const __nv_bfloat16*>(hn);
+  p.V = V; p.H = H; p.M = M;
+  p.best_val = static_cast<float*>(workspace);
+  p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)sms * M);
+  CK(lm_argmax_launch(p, sms, st));
+  CK(argmax_accept_launch(p.best_val, p.best_idx, sms, M, block, batch, tokens, target, acc_len,
+                          correction, st));
+  return DFLASH_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,159 @@
+// Small bandwidth kernels around the projections:
+//   rope_table   : (cos, sin) of (offset + row) * inv_freq, once per forward
+//                  (the ANE host precomputes the same tables, ane_model.py:484-527)
+//   init_h       : residual stream h = noise (fp32) and its sum-of-squares
+//   ctx_norm     : hidden_norm of the fc output (dflash.py:392) -> f16 rows
+//   final_norm   : final RMSNorm (dflash.py:403) -> bf16 for the lm_head and
+//                  the optional hidden-state output
+//   i8_to_f16    : exact f16 copy of int8 weights (context K/V GEMM operand)
+#include "kernels.cuh"
+
+namespace dfl {
+
+__global__ void rope_table_kernel(int pos0, int rows, const float* __restrict__ inv_freq,
+                                  float2* __restrict__ out) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * 64) return;
+  const int r = idx >> 6, i = idx & 63;
+  const float ang = static_cast<float>(pos0 + r) * inv_freq[i];
+  float s, c;
+  sincosf(ang, &s, &c);
+  out[idx] = make_float2(c, s);
+}
+
+// one warp per row
+__global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, int H,
+                              float* __restrict__ h, float* __restrict__ hstat) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float ss = 0.f;
+  for (int k = lane * 8; k < H; k += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(noise + (size_t)row * H + k);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = __bfloat1622float2(b[e]);
+      f[2 * e] = t.x;
+      f[2 * e + 1] = t.y;
+    }
+    float4* dst = reinterpret_cast<float4*>(h + (size_t)row * H + k);
+    dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+    dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) hstat[row] = ss;
+}
+
+// ctx_out[r, k] = f16(raw[r, k] * rsqrt(sum_p part[p, r] / H + eps) * w[k]); one CTA per row
+__global__ void ctx_norm_kernel(const float* __restrict__ raw, const float* __restrict__ part,
+                                int nparts, int rows, int H, const float* __restrict__ w, float eps,
+                                __half* __restrict__ out) {
+  const int r = blockIdx.x;
+  __shared__ float rs;
+  if (threadIdx.x == 0) {
+    float ss = 0.f;
+    for (int q = 0; q < nparts; ++q) ss += part[(size_t)q * rows + r];
+    rs = rsqrtf(ss / static_cast<float>(H) + eps);
+  }
+  __syncthreads();
+  const float rstd = rs;
+  for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
+    const float4 a = *reinterpret_cast<const float4*>(raw + (size_t)r * H + k);
+    const float4 c = *reinterpret_cast<const float4*>(raw + (size_t)r * H + k + 4);
+    const float4 w0 = *reinterpret_cast<const float4*>(w + k);
+    const float4 w1 = *reinterpret_cast<const float4*>(w + k + 4);
+    uint4 o;
+    o.x = pack_f16x2(a.x * rstd * w0.x, a.y * rstd * w0.y);
+    o.y = pack_f16x2(a.z * rstd * w0.z, a.w * rstd * w0.w);
+    o.z = pack_f16x2(c.x * rstd * w1.x, c.y * rstd * w1.y);
+    o.w = pack_f16x2(c.z * rstd * w1.z, c.w * rstd * w1.w);
+    *reinterpret_cast<uint4*>(out + (size_t)r * H + k) = o;
+  }
+}
+
+// hn = bf16(h * rstd * w) for every row; also the caller's hidden output
+// (bf16, or fp32 when out_f32) when given
+template <bool OUT_F32>
+__global__ void final_norm_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
+                                  int hparts, int M, int H, const float* __restrict__ w, float eps,
+                                  __nv_bfloat16* __restrict__ hn, void* __restrict__ out) {
+  const int row = blockIdx.x;
+  __shared__ float rs;
+  if (threadIdx.x == 0) {
+    float ss = 0.f;
+    for (int q = 0; q < hparts; ++q) ss += hstat[(size_t)q * M + row];
+    rs = rsqrtf(ss / static_cast<float>(H) + eps);
+  }
+  __syncthreads();
+  const float rstd = rs;
+  for (int k = threadIdx.x * 4; k < H; k += blockDim.x * 4) {
+    const float4 x = *reinterpret_cast<const float4*>(h + (size_t)row * H + k);
+    const float4 wv = *reinterpret_cast<const float4*>(w + k);
+    const float4 y = make_float4(x.x * rstd * wv.x, x.y * rstd * wv.y, x.z * rstd * wv.z,
+                                 x.w * rstd * wv.w);
+    uint2 o;
+    o.x = pack_bf16x2(y.x, y.y);
+    o.y = pack_bf16x2(y.z, y.w);
+    *reinterpret_cast<uint2*>(hn + (size_t)row * H + k) = o;
+    if (out) {
+      if (OUT_F32)
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)row * H + k) = y;
+      else
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + (size_t)row * H + k) = o;
+    }
+  }
+}
+
+__global__ void i8_to_f16_kernel(const int8_t* __restrict__ src, size_t n, __half* __restrict__ dst) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __int2half_rn(static_cast<int>(src[i]));
+}
+
+__global__ void f16_to_f32_kernel(const __half* __restrict__ src, size_t n, float* __restrict__ dst) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __half2float(src[i]);
+}
+
+cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st) {
+  if (rows < 1) return cudaSuccess;
+  rope_table_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(pos0, rows, inv_freq, out);
+  return cudaGetLastError();
+}
+cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
+                          cudaStream_t st) {
+  if (H % 8) return cudaErrorInvalidValue;
+  init_h_kernel<<<(M + 7) / 8, 256, 0, st>>>(noise, M, H, h, hstat);
+  return cudaGetLastError();
+}
+cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
+                            const float* w, float eps, __half* out, cudaStream_t st) {
+  if (H % 8 || rows < 1) return cudaErrorInvalidValue;
+  ctx_norm_kernel<<<rows, 256, 0, st>>>(raw, part, nparts, rows, H, w, eps, out);
+  return cudaGetLastError();
+}
+cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
+                              const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
+                              cudaStream_t st) {
+  if (H % 4) return cudaErrorInvalidValue;
+  if (out_f32)
+    final_norm_kernel<true><<<M, 256, 0, st>>>(h, hstat, hparts, M, H, w, eps, hn, out);
+  else
+    final_norm_kernel<false><<<M, 256, 0, st>>>(h, hstat, hparts, M, H, w, eps, hn, out);
+  return cudaGetLastError();
+}
+cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st) {
+  i8_to_f16_kernel<<<1024, 256, 0, st>>>(src, n, dst);
+  return cudaGetLastError();
+}
+cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st) {
+  f16_to_f32_kernel<<<256, 256, 0, st>>>(src, n, dst);
+  return cudaGetLastError();
+}
+
+}  // namespace dfl

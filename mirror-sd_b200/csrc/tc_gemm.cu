@@ -1,0 +1,282 @@
+// Dense context-side GEMMs on the 5th-gen tensor cores (tcgen05 + TMA).
+//
+//   D[M, N] = A[M, K] . B[N, K]^T      A, B K-major (row-major, K contiguous)
+//
+// Used for the two context projections of the draft forward whose M is the
+// number of context rows (thousands):
+//   * fc        (dflash.py:392):  target_hidden [rows, F*H] x Wfc [H, F*H]  (bf16)
+//       epilogue: bf16 store + per-256-column partial sum of squares for the
+//       following RMSNorm (hidden_norm).
+//   * ctx K/V   (dflash.py:293-305): normalised context [rows, H] x the K|V
+//       weights of all layers [L*2*NKV*128, H] (f16, exact int8 values; the
+//       fp16 per-channel scale is applied in the epilogue).
+//       epilogue: scale, per-head k RMSNorm + neox RoPE, f16 store into the
+//       per-layer K / V buffers.
+//
+// CTA tile 128 x 256, K step 64 (one 128-byte swizzle atom), 4-stage TMA ring.
+// Warp 0: TMA producer.  Warp 1: TMEM allocator + single-thread UMMA issuer
+// (tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, fp32 accumulator in
+// 256 TMEM columns).  Warps 2-5: epilogue (tcgen05.ld, each thread owns one
+// accumulator row, so per-row and per-head reductions are thread-local).
+// Every mbarrier wait is bounded; a timeout sets the device error word and the
+// CTA unwinds (TMEM is released on every path).
+#include "kernels.cuh"
+
+namespace dfl {
+
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;   // 16 KB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;   // 32 KB
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
+constexpr int TC_THREADS = 192;
+constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+
+
+template <int AB_FMT, int MODE>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* accum = empty + TC_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
+  const int nk = p.K / TC_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TC_BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % TC_STAGES;
+        const uint32_t ph = (kb / TC_STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) break;
+        uint8_t* sa = smem + s * TC_STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
+        tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, m0);
+        tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(TC_BM, TC_BN, AB_FMT);
+      bool ok = true;
+      for (int kb = 0; kb < nk && ok; ++kb) {
+        const int s = kb % TC_STAGES;
+        const uint32_t ph = (kb / TC_STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
+        const uint64_t adesc = umma_desc_sw128(sa);
+        const uint64_t bdesc = umma_desc_sw128(sa + TC_A_BYTES);
+#pragma unroll
+        for (int k = 0; k < TC_BK / 16; ++k) {
+          // advance 16 elements (32 bytes) inside the swizzle atom: +2 in 16-byte units
+          umma_f16(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);  // fires once every issued MMA has retired
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int q = warp & 3;
+    const int row_local = q * 32 + lane;
+    const int row = m0 + row_local;
+    const bool row_ok = row < p.M;
+    const bool ok = mbar_wait(accum, 0, p.err, abort_flag) && !*abort_flag;
+    tc_fence_after();
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    if (ok) {
+      if (MODE == kTcFc || MODE == kTcStoreF32) {
+        float ss = 0.f;
+#pragma unroll 1
+        for (int ch = 0; ch < TC_BN / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(tbase + ch * 32, r);
+          tmem_ld_wait();
+          if (row_ok) {
+            float4* dst = reinterpret_cast<float4*>(p.out_f32 + (size_t)row * p.N + n0 + ch * 32);
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const float4 f = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                           __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+              if (MODE == kTcFc) ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
+              dst[v] = f;
+            }
+          }
+        }
+        if (MODE == kTcFc && row_ok) p.sumsq_part[(size_t)blockIdx.x * p.M + row] = ss;
+      } else {  // kTcCtxKV: two 128-wide heads per tile
+        const int bi = row / p.rows_per_seq;
+        const int i = row - bi * p.rows_per_seq;  // context row inside its sequence
+        const int per_layer = 2 * p.nkv * 128;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int col0 = n0 + hh * 128;
+          const int layer = col0 / per_layer;
+          const int within = col0 - layer * per_layer;
+          const bool is_v = within >= p.nkv * 128;
+          const int kvh = (within % (p.nkv * 128)) / 128;
+          const float* sc = p.scale + col0;
+          float rstd = 1.f;
+          if (!is_v) {
+            float ss = 0.f;
+#pragma unroll 1
+            for (int ch = 0; ch < 4; ++ch) {
+              uint32_t r[32];
+              tmem_ld32(tbase + hh * 128 + ch * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) {
+                const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
+                ss += y * y;
+              }
+            }
+            rstd = rsqrtf(ss / 128.0f + p.eps);
+          }
+          __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
+                        (((size_t)bi * p.nkv + kvh) * p.kv_cap + p.kv_row0 + i) * 128;
+          const float* kn = p.k_norm + layer * 128;
+          const float2* cs = p.rope + (size_t)(p.kv_row0 + i) * 64;
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            uint32_t r1[32], r2[32];
+            tmem_ld32(tbase + hh * 128 + half * 32, r1);
+            tmem_ld32(tbase + hh * 128 + 64 + half * 32, r2);
+            tmem_ld_wait();
+            if (row_ok) {
+              uint32_t o1[16], o2[16];
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float a[2], b[2];
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                  const int d = half * 32 + e + t;
+                  float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
+                  float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
+                  if (!is_v) {
+                    y1 = y1 * rstd * __ldg(kn + d);
+                    y2 = y2 * rstd * __ldg(kn + d + 64);
+                    const float2 t2 = __ldg(cs + d);
+                    const float cth = t2.x, sth = t2.y;
+                    a[t] = y1 * cth - y2 * sth;
+                    b[t] = y1 * sth + y2 * cth;
+                  } else {
+                    a[t] = y1;
+                    b[t] = y2;
+                  }
+                }
+                o1[e / 2] = pack_f16x2(a[0], a[1]);
+                o2[e / 2] = pack_f16x2(b[0], b[1]);
+              }
+              uint4* d1 = reinterpret_cast<uint4*>(dst + half * 32);
+              uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + half * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                d1[v] = make_uint4(o1[4 * v], o1[4 * v + 1], o1[4 * v + 2], o1[4 * v + 3]);
+                d2[v] = make_uint4(o2[4 * v], o2[4 * v + 1], o2[4 * v + 2], o2[4 * v + 3]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_BN);
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major map: inner dim K (elements), outer dim rows; box 64 x box_rows, 128B swizzle
+static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t K, uint64_t rows,
+                     uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K * 2};
+  cuuint32_t box[2] = {TC_BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int FMT, int MODE>
+static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p,
+                               cudaStream_t st) {
+  auto kern = tc_gemm_kernel<FMT, MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid(p.N / TC_BN, (p.M + TC_BM - 1) / TC_BM);
+  kern<<<grid, TC_THREADS, TC_SMEM, st>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+// a_bf16: A/B element type (true: bf16, false: f16).  mode: TcMode.
+cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
+                           cudaStream_t st) {
+  if (p.M < 1 || p.N % TC_BN || p.K % TC_BK || p.K < TC_BK) return cudaErrorInvalidValue;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, A, bf16, p.K, p.M, TC_BM) || !make_map(&mb, B, bf16, p.K, p.N, TC_BN))
+    return cudaErrorInvalidValue;
+  if (bf16) {
+    if (mode == kTcFc) return tc_launch_t<1, kTcFc>(ma, mb, p, st);
+    if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32>(ma, mb, p, st);
+  } else {
+    if (mode == kTcCtxKV) return tc_launch_t<0, kTcCtxKV>(ma, mb, p, st);
+    if (mode == kTcStoreF32) return tc_launch_t<0, kTcStoreF32>(ma, mb, p, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace dfl

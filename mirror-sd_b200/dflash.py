@@ -1,0 +1,406 @@
+"""Host side of the B200 DFlash draft model, mirroring ``mirror_sd.dflash``.
+
+Same names, arguments and error behaviour as the reference's
+``mirror_sd/dflash.py`` so a decode loop written against it
+(``generate.py:591-606``) can hold this object instead:
+
+* ``DFlashConfig`` (dflash.py:34-105) with ``from_dict`` / ``qwen3_8b`` /
+  ``qwen3_4b``; ``build_target_layer_ids`` (:108-119);
+  ``extract_context_feature`` (:122-130); ``sample`` (:133-136).
+* ``DFlashDraftModel.__call__(noise_embedding, target_hidden, mask=None,
+  cache=None)`` -> final-normed hidden states ``[b, q, H]`` (:384-403), with
+  ``block_size``, ``mask_token_id``, ``config`` and a settable
+  ``num_draft_layers`` (:380-382, generate.py:419-440).
+* The fused draft step the reference exposes through its ANE split API
+  (``prepare_forward`` / ``run_kernels`` / ``read_output`` /
+  ``read_draft_tokens``, ane_model.py:538-604): lm_head + greedy argmax (+
+  acceptance) inside the same call.
+
+Every compute call goes through the CUDA library (``_native``); there is no
+CPU or PyTorch fallback.  torch is used for device memory and streams only.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import torch
+
+from . import _native as N
+
+
+# ----------------------------------------------------------------------------
+# config (mirror_sd/dflash.py:34-105)
+# ----------------------------------------------------------------------------
+@dataclass
+class DFlashConfig:
+    hidden_size: int = 4096
+    num_hidden_layers: int = 5
+    intermediate_size: int = 12288
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    max_position_embeddings: int = 40960
+    vocab_size: int = 151936
+    block_size: int = 16
+    mask_token_id: int = 151669
+    target_layer_ids: List[int] = field(default_factory=lambda: [4, 12, 19, 26, 33])
+    num_target_layers: int = 36
+    rope_scaling: Optional[dict] = None
+
+    @classmethod
+    def qwen3_8b(cls, num_target_layers: int = 36) -> "DFlashConfig":
+        cfg = cls(num_target_layers=num_target_layers)
+        cfg.target_layer_ids = build_target_layer_ids(num_target_layers, cfg.num_hidden_layers)
+        return cfg
+
+    @classmethod
+    def qwen3_4b(cls, num_target_layers: int = 36) -> "DFlashConfig":
+        cfg = cls(hidden_size=2560, num_hidden_layers=5, intermediate_size=6912,
+                  num_attention_heads=20, num_key_value_heads=4, head_dim=128, vocab_size=151936)
+        cfg.num_target_layers = num_target_layers
+        cfg.target_layer_ids = build_target_layer_ids(num_target_layers, cfg.num_hidden_layers)
+        return cfg
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "DFlashConfig":
+        """HF ``config.json`` -> config, with the reference's fall-back
+        defaults (dflash.py:77-105)."""
+        dc = d.get("dflash_config", {})
+        nhl = d.get("num_hidden_layers", dc.get("num_hidden_layers", 5))
+        ntl = dc.get("num_target_layers", d.get("num_target_layers", 36))
+        cfg = cls(hidden_size=d.get("hidden_size", 4096), num_hidden_layers=nhl,
+                  intermediate_size=d.get("intermediate_size", 10944),
+                  num_attention_heads=d.get("num_attention_heads", 32),
+                  num_key_value_heads=d.get("num_key_value_heads", 2),
+                  head_dim=d.get("head_dim", 128), rms_norm_eps=d.get("rms_norm_eps", 1e-6),
+                  rope_theta=d.get("rope_theta", 10000.0),
+                  max_position_embeddings=d.get("max_position_embeddings", 4096),
+                  vocab_size=d.get("vocab_size", 151936),
+                  block_size=dc.get("block_size", d.get("block_size", 16)),
+                  mask_token_id=dc.get("mask_token_id", d.get("mask_token_id", 151667)),
+                  num_target_layers=ntl)
+        cfg.target_layer_ids = (dc["target_layer_ids"] if "target_layer_ids" in dc
+                                else build_target_layer_ids(cfg.num_target_layers, cfg.num_hidden_layers))
+        if "rope_scaling" in d:
+            cfg.rope_scaling = d["rope_scaling"]
+        return cfg
+
+
+def build_target_layer_ids(num_target_layers: int, num_draft_layers: int) -> List[int]:
+    """Evenly spaced target layers in [1, n-3] (dflash.py:108-119)."""
+    if num_draft_layers == 1:
+        return [num_target_layers // 2]
+    start, end = 1, num_target_layers - 3
+    span = end - start
+    return [int(round(start + (i * span) / (num_draft_layers - 1))) for i in range(num_draft_layers)]
+
+
+def extract_context_feature(hidden_states, layer_ids):
+    """Concatenate captured target layers on the feature axis (dflash.py:122-130)."""
+    if len(hidden_states) == len(layer_ids):
+        return torch.cat(list(hidden_states), dim=-1)
+    return torch.cat([hidden_states[lid + 1] for lid in layer_ids], dim=-1)
+
+
+def sample(logits: torch.Tensor, temperature: float = 0.0) -> torch.Tensor:
+    """Greedy argmax, first index on ties (dflash.py:133-136).  Sampling with
+    temperature is part of the target-side loop and is not on this path."""
+    if temperature < 1e-5:
+        return torch.argmax(logits, dim=-1)
+    raise NotImplementedError("temperature sampling is outside the draft forward")
+
+
+# ----------------------------------------------------------------------------
+# weights in the reference's W8A16 format (ane_model.py:265-344)
+# ----------------------------------------------------------------------------
+PROJ = ["wq", "wk", "wv", "wo", "wg", "wu", "wd"]
+
+
+@dataclass
+class Q8Layer:
+    """One decoder layer: int8 [out, in] + fp16 [out] per projection, fp32 norms."""
+    q: dict            # name -> int8 tensor (device)
+    s: dict            # name -> fp16 tensor (device)
+    input_layernorm: torch.Tensor
+    post_attention_layernorm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+@dataclass
+class DFlashWeightsQ8:
+    fc: torch.Tensor             # bf16 [H, F*H]
+    hidden_norm: torch.Tensor    # fp32 [H]
+    norm: torch.Tensor           # fp32 [H]
+    layers: List[Q8Layer]
+
+
+def quantize_q8(w: torch.Tensor):
+    """Symmetric per-output-channel int8 with fp16 scales on the GPU, bit-exact
+    with ``ANEDraftModel._quantize_weight_q8`` (ane_model.py:265-279).
+    ``w``: [oc, ic] CUDA tensor.  Returns ``(q int8 [oc, ic], s fp16 [oc])``."""
+    if not w.is_cuda:
+        raise ValueError("quantize_q8 expects a CUDA tensor")
+    lib = N.load()
+    w32 = w.detach().to(torch.float32).contiguous()
+    oc, ic = w32.shape
+    q = torch.empty((oc, ic), dtype=torch.int8, device=w.device)
+    s = torch.empty((oc,), dtype=torch.float16, device=w.device)
+    st = torch.cuda.current_stream(w.device).cuda_stream
+    N.check(lib.dflash_quantize_q8(N.ptr(w32), oc, ic, N.ptr(q), N.ptr(s), ctypes.c_void_p(st)),
+            "dflash_quantize_q8")
+    return q, s
+
+
+# ----------------------------------------------------------------------------
+# KV cache bookkeeping (dflash.py:139-212)
+# ----------------------------------------------------------------------------
+class DFlashKVCache:
+    """Offset / trim bookkeeping of the reference's draft cache.  The stateless
+    draft step (cache=None) is what this build runs on the device; a cache
+    that already holds keys is rejected by ``DFlashDraftModel.__call__``."""
+
+    def __init__(self, sink_size: int = 0, window_size: int = 0):
+        self.keys = None
+        self.values = None
+        self.offset = 0
+        self.sink_size = int(sink_size)
+        self.window_size = int(window_size)
+
+    def trim(self, n: int):
+        if self.keys is not None and n > 0:
+            keep = max(self.keys.shape[2] - n, 0)
+            self.keys = self.keys[..., :keep, :]
+            self.values = self.values[..., :keep, :]
+            self.offset -= n
+
+    def state(self):
+        return [] if self.keys is None else [self.keys, self.values]
+
+
+# ----------------------------------------------------------------------------
+# the draft model
+# ----------------------------------------------------------------------------
+class DFlashDraftModel:
+    """B200 DFlash draft model with the reference's call signature.
+
+    ``lm_head`` is the target's (tied) embedding matrix [V, H] in bf16; it is
+    referenced, not copied (generate.py:435-436: the draft does not own it).
+    """
+
+    def __init__(self, config: DFlashConfig, weights: DFlashWeightsQ8, lm_head: torch.Tensor,
+                 max_batch: int = 1, max_ctx: int = 4096, max_block: Optional[int] = None,
+                 device=None):
+        self.config = config
+        self.block_size = config.block_size
+        self.mask_token_id = config.mask_token_id
+        self.num_draft_layers = config.num_hidden_layers
+        self.device = torch.device(device) if device is not None else weights.fc.device
+        if self.device.type != "cuda":
+            raise ValueError("DFlashDraftModel runs on a CUDA device only")
+        self._lib = N.load()
+        self._lm_head = lm_head.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        self._weights = weights
+        H, F = config.hidden_size, len(config.target_layer_ids)
+        if tuple(weights.fc.shape) != (H, F * H):
+            raise ValueError(f"fc weight shape {tuple(weights.fc.shape)} != {(H, F * H)}")
+        if tuple(self._lm_head.shape) != (config.vocab_size, H):
+            raise ValueError(f"lm_head shape {tuple(self._lm_head.shape)} != {(config.vocab_size, H)}")
+        self.max_batch = int(max_batch)
+        self.max_ctx = int(max_ctx)
+        self.max_block = int(max_block or config.block_size)
+        dims = N.DFlashDims(
+            hidden_size=H, num_hidden_layers=config.num_hidden_layers,
+            intermediate_size=config.intermediate_size,
+            num_attention_heads=config.num_attention_heads,
+            num_key_value_heads=config.num_key_value_heads, head_dim=config.head_dim,
+            vocab_size=config.vocab_size, num_target_features=F,
+            rms_norm_eps=config.rms_norm_eps, rope_theta=config.rope_theta,
+            max_batch=self.max_batch, max_block=self.max_block, max_ctx=self.max_ctx)
+        keep = []  # tensors whose pointers the create call reads
+
+        def dev(t, dtype):
+            t = t.to(device=self.device, dtype=dtype).contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        layers = (N.DFlashLayerWeights * config.num_hidden_layers)()
+        for i, lw in enumerate(weights.layers):
+            L = layers[i]
+            for name in PROJ:
+                setattr(L, name, dev(lw.q[name], torch.int8))
+                setattr(L, "s" + name[1], dev(lw.s[name], torch.float16))
+            L.input_layernorm = dev(lw.input_layernorm, torch.float32)
+            L.post_attention_layernorm = dev(lw.post_attention_layernorm, torch.float32)
+            L.q_norm = dev(lw.q_norm, torch.float32)
+            L.k_norm = dev(lw.k_norm, torch.float32)
+        view = N.DFlashWeightsView(fc=dev(weights.fc, torch.bfloat16),
+                                   hidden_norm=dev(weights.hidden_norm, torch.float32),
+                                   norm=dev(weights.norm, torch.float32),
+                                   lm_head=self._lm_head.data_ptr(), layers=layers)
+        handle = ctypes.c_void_p()
+        torch.cuda.synchronize(self.device)
+        N.check(self._lib.dflash_create(ctypes.byref(dims), ctypes.byref(view),
+                                        self.device.index or 0, ctypes.byref(handle)),
+                "dflash_create")
+        self._handle = handle
+        # ANE-style split API state
+        self._pending = None
+        self._out_hidden = None
+        self._out_tokens = None
+        self.b_logits = True  # lm_head + argmax is fused (read_draft_tokens is valid)
+
+    # -- lifecycle -----------------------------------------------------------
+    def close(self):
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            N.check(self._lib.dflash_destroy(self._handle), "dflash_destroy")
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def make_cache(self, sink_size: int = 64, window_size: int = 1024) -> list:
+        return [DFlashKVCache(sink_size=sink_size, window_size=window_size)
+                for _ in range(self.num_draft_layers)]
+
+    def set_block_size(self, new_block: int) -> None:
+        """Change the active block size (ane_model.py:611-630: ValueError
+        outside [1, capacity])."""
+        if new_block < 1 or new_block > self.max_block:
+            raise ValueError(f"new_seq_q={new_block} must be in [1, {self.max_block}]")
+        self.block_size = new_block
+        self.config.block_size = new_block
+
+    # -- core step -----------------------------------------------------------
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _as_dev(self, t, dtype):
+        if t.device != self.device:
+            t = t.to(self.device, non_blocking=True)
+        return t.to(dtype).contiguous()
+
+    def draft_step(self, noise_embedding, target_hidden, rope_offset: int = 0,
+                   target_tokens=None, want_hidden: bool = True, want_tokens: bool = True,
+                   out_hidden=None, out_tokens=None, acc_len=None, correction=None,
+                   hidden_fp32: bool = False, phase_events=None):
+        """One stateless draft step on the device: final-normed hidden states
+        (bf16, or fp32 with ``hidden_fp32``), greedy draft ids for rows 1..q-1
+        and, given the verifier's posterior ``target_tokens`` [b, q], the
+        accepted length and correction token.  ``phase_events``: optional list
+        of 8 ``torch.cuda.Event`` recorded at the phase boundaries."""
+        noise = self._as_dev(noise_embedding, torch.bfloat16)
+        th = self._as_dev(target_hidden, torch.bfloat16)
+        if noise.dim() != 3 or th.dim() != 3 or noise.shape[0] != th.shape[0]:
+            raise ValueError("noise_embedding [b, q, H] and target_hidden [b, ctx, F*H] expected")
+        b, q, H = noise.shape
+        if H != self.config.hidden_size or th.shape[2] != len(self.config.target_layer_ids) * H:
+            raise ValueError("hidden size mismatch")
+        if want_hidden and out_hidden is None:
+            out_hidden = torch.empty((b, q, H), dtype=torch.float32 if hidden_fp32 else torch.bfloat16,
+                                     device=self.device)
+        if out_hidden is not None:
+            hidden_fp32 = out_hidden.dtype == torch.float32
+        if (want_tokens or target_tokens is not None) and out_tokens is None:
+            out_tokens = torch.empty((b, q - 1), dtype=torch.int32, device=self.device)
+        tt = None
+        if target_tokens is not None:
+            tt = self._as_dev(target_tokens, torch.int32)
+            if acc_len is None:
+                acc_len = torch.empty((b,), dtype=torch.int32, device=self.device)
+            if correction is None:
+                correction = torch.empty((b,), dtype=torch.int32, device=self.device)
+        args = N.DFlashForwardArgs(
+            batch=b, block=q, ctx_len=th.shape[1], rope_offset=int(rope_offset),
+            num_layers=int(self.num_draft_layers),
+            noise=noise.data_ptr(), target_hidden=th.data_ptr() if th.numel() else None,
+            out_hidden=out_hidden.data_ptr() if out_hidden is not None else None,
+            out_hidden_fp32=int(bool(hidden_fp32)),
+            out_tokens=out_tokens.data_ptr() if out_tokens is not None else None,
+            target_tokens=tt.data_ptr() if tt is not None else None,
+            acc_len=acc_len.data_ptr() if acc_len is not None else None,
+            correction=correction.data_ptr() if correction is not None else None)
+        if phase_events is not None:
+            if len(phase_events) < N.DFLASH_PHASES:
+                raise ValueError(f"phase_events needs {N.DFLASH_PHASES} events")
+            arr = (ctypes.c_void_p * len(phase_events))(*[ctypes.c_void_p(e.cuda_event) for e in phase_events])
+            args.phase_events = ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p))
+            args.n_phase_events = len(phase_events)
+        N.check(self._lib.dflash_forward(self._handle, ctypes.byref(args), self._stream()),
+                "dflash_forward")
+        return out_hidden, out_tokens, acc_len, correction
+
+    def __call__(self, noise_embedding, target_hidden, mask=None, cache=None, **kwargs):
+        """``DFlashDraftModel.__call__`` (dflash.py:384-403): returns the
+        final-normed hidden states [b, q, H] (bf16)."""
+        if mask is not None:
+            raise ValueError("the DFlash draft attention is non-causal; mask must be None")
+        rope_offset = 0
+        if cache is not None:
+            if any(c.keys is not None for c in cache):
+                raise NotImplementedError("a draft KV cache that already holds keys is not supported;"
+                                          " call with cache=None (stateless draft step)")
+            rope_offset = cache[0].offset if len(cache) else 0
+        hidden, _, _, _ = self.draft_step(noise_embedding, target_hidden, rope_offset,
+                                          want_hidden=True, want_tokens=False)
+        return hidden
+
+    def draft_tokens(self, noise_embedding, target_hidden, rope_offset: int = 0):
+        """lm_head + greedy argmax fused on the device: ids [b, q-1] for rows
+        1..q-1 (generate.py:604-606)."""
+        _, toks, _, _ = self.draft_step(noise_embedding, target_hidden, rope_offset,
+                                        want_hidden=False, want_tokens=True)
+        return toks
+
+    # -- ANE-style split API (ane_model.py:538-604) ---------------------------
+    def prepare_forward(self, noise_embedding, precomputed_context, cache, target_hidden):
+        if precomputed_context is not None:
+            raise ValueError("precomputed_context is not used: fc + hidden_norm run on the device")
+        off = cache[0].offset if cache is not None and len(cache) and cache[0].offset > 0 else 0
+        self._pending = (noise_embedding, target_hidden, off)
+
+    def run_kernels(self):
+        if self._pending is None:
+            raise RuntimeError("prepare_forward() must be called first")
+        noise, th, off = self._pending
+        self._out_hidden, self._out_tokens, _, _ = self.draft_step(noise, th, off)
+        self._pending = None
+
+    def read_output(self):
+        if self._out_hidden is None:
+            raise RuntimeError("run_kernels() has not produced an output")
+        return self._out_hidden
+
+    def read_draft_tokens(self):
+        """[1, q] ids like the reference (position 0 is the anchor row, whose
+        id is not computed and reads as -1); callers slice [:, 1:q]."""
+        if self._out_tokens is None:
+            raise RuntimeError("run_kernels() has not produced tokens")
+        b = self._out_tokens.shape[0]
+        head = torch.full((b, 1), -1, dtype=torch.int32, device=self.device)
+        return torch.cat([head, self._out_tokens], dim=1)
+
+
+def accept(draft_tokens: torch.Tensor, target_tokens: torch.Tensor):
+    """Longest matching prefix on the device (generate.py:722-728).
+    draft [b, q-1], target [b, q] int32 CUDA tensors -> (acc_len [b], correction [b])."""
+    lib = N.load()
+    d = draft_tokens.to(torch.int32).contiguous()
+    t = target_tokens.to(torch.int32).contiguous()
+    if d.dim() == 1:
+        d, t = d[None], t[None]
+    b, q = t.shape
+    if d.shape != (b, q - 1):
+        raise ValueError("draft must be [b, q-1] for target [b, q]")
+    acc = torch.empty((b,), dtype=torch.int32, device=t.device)
+    cor = torch.empty((b,), dtype=torch.int32, device=t.device)
+    st = ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    N.check(lib.dflash_accept(N.ptr(d), N.ptr(t), b, q, N.ptr(acc), N.ptr(cor), st), "dflash_accept")
+    return acc, cor

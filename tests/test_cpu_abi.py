@@ -1,0 +1,81 @@
+"""CPU-only checks of the boundary: the C-ABI library loads and exports every
+function include/dflash_b200.h declares (no compute call without a GPU), and
+the host-side mirror of the reference interface."""
+import ctypes
+import json
+import os
+import re
+
+import pytest
+
+from oracle import dflash_oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    with open(os.path.join(ROOT, "include", "dflash_b200.h")) as f:
+        src = f.read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(dflash_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ["dflash_create", "dflash_forward", "dflash_accept", "dflash_destroy",
+              "dflash_last_error", "dflash_quantize_q8"]:
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._native.load()
+    for name in _declared():
+        assert hasattr(lib, name), name
+        assert name in pkg._native.EXPORTS, f"{name} has no ctypes binding"
+
+
+def test_version_and_error_string_without_gpu(pkg):
+    lib = pkg._native.load()
+    assert lib.dflash_version() >= 1
+    # argument validation runs before any CUDA call
+    h = ctypes.c_void_p()
+    dims = pkg._native.DFlashDims(hidden_size=256, num_hidden_layers=1, intermediate_size=256,
+                                  num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                                  vocab_size=10, num_target_features=5, rms_norm_eps=1e-6,
+                                  rope_theta=1e6, max_batch=1, max_block=8, max_ctx=8)
+    st = lib.dflash_create(ctypes.byref(dims), None, 0, ctypes.byref(h))
+    assert st == pkg._native.DFLASH_ERR_INVALID
+    assert "head_dim" in pkg._native.last_error()
+    with pytest.raises(ValueError):
+        pkg._native.check(st, "dflash_create")
+    assert lib.dflash_forward(None, None, None) == pkg._native.DFLASH_ERR_INVALID
+
+
+def test_config_from_dict_defaults_match_reference(pkg):
+    # dflash.py:77-105 fall-backs differ from the dataclass defaults
+    c = pkg.DFlashConfig.from_dict({})
+    assert (c.rope_theta, c.mask_token_id, c.intermediate_size, c.num_key_value_heads) == \
+        (10000.0, 151667, 10944, 2)
+    c = pkg.DFlashConfig.from_dict({"hidden_size": 5120, "dflash_config": {
+        "block_size": 32, "mask_token_id": 5, "target_layer_ids": [1, 2, 3, 4, 5]}})
+    assert (c.block_size, c.mask_token_id, c.target_layer_ids) == (32, 5, [1, 2, 3, 4, 5])
+    d = pkg.DFlashConfig()
+    assert (d.rope_theta, d.mask_token_id, d.target_layer_ids) == (1e6, 151669, [4, 12, 19, 26, 33])
+
+
+def test_target_layer_ids_match_fixture(pkg, golden_dir):
+    with open(os.path.join(golden_dir, "layer_ids.json")) as f:
+        ids = json.load(f)
+    for key, val in ids.items():
+        nt, nd = map(int, key.split(","))
+        assert pkg.build_target_layer_ids(nt, nd) == val
+
+
+def test_extract_context_feature_and_sample(pkg):
+    import torch
+    hs = [torch.full((1, 3, 2), float(i)) for i in range(6)]
+    out = pkg.extract_context_feature(hs, [0, 2, 4])    # embedding first -> shift by one
+    assert out[0, 0].tolist() == [1, 1, 3, 3, 5, 5]
+    out = pkg.extract_context_feature(hs[:3], [7, 8, 9])
+    assert out.shape == (1, 3, 6)
+    assert pkg.sample(torch.tensor([[1.0, 3.0, 3.0]])).tolist() == [1]
