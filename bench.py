@@ -1,0 +1,415 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 DFlash draft step (one JSON line on rank 0).
+
+Workload (BASELINE.json metric): Qwen3.5-27B-class DFlash draft -- hidden
+5120, 40 q / 8 kv heads, head_dim 128, SwiGLU 17408, 5 layers, vocab 151936 --
+W8A16 (int8 per-output-channel weights, fp16 scales), block 32, context 4096,
+batch 1 per GPU.  A step is one stateless draft forward: fc + hidden_norm over
+the 4096 context rows, 5 decoder layers, final norm, tied lm_head + greedy
+argmax over the vocabulary and acceptance against synthetic target tokens
+that keep each drafted token with probability 0.9.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs under torchrun, one rank per GPU, each rank drafting its own
+sequence (requests shard by batch with no collective on the hot path);
+value = sum over ranks of drafted tokens / max over ranks of the step time.
+`--impl reference` times the reference algorithm on the host CPU (the fp32
+CPU restatement in oracle/, MLX being unavailable) on rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "draft tok/s & µs/draft-step (27B-class, block 32, ctx 4K); % HBM roofline"
+CFG_27B = dict(hidden_size=5120, num_hidden_layers=5, intermediate_size=17408, num_attention_heads=40,
+               num_key_value_heads=8, head_dim=128, vocab_size=151936, block_size=32)
+CFG_8B = dict(hidden_size=4096, num_hidden_layers=5, intermediate_size=12288, num_attention_heads=32,
+              num_key_value_heads=8, head_dim=128, vocab_size=151936, block_size=16)
+F = 5
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def step_bytes(c, ctx, batch):
+    """Algorithmic HBM bytes of one draft step: int8 projection weights + fp32
+    scales, bf16 fc and lm_head, bf16 target_hidden and noise rows."""
+    H, I, nq, nkv, L, V = (c["hidden_size"], c["intermediate_size"], c["num_attention_heads"],
+                           c["num_key_value_heads"], c["num_hidden_layers"], c["vocab_size"])
+    per_layer = (nq * 128 * H) + 2 * (nkv * 128 * H) + H * nq * 128 + 3 * I * H
+    scales = (nq * 128 + 2 * nkv * 128 + H + 2 * I + H) * 2
+    return (L * (per_layer + scales) + H * F * H * 2 + V * H * 2
+            + batch * ctx * F * H * 2 + batch * c["block_size"] * H * 2)
+
+
+def step_flops(c, ctx, batch):
+    H, I, nq, nkv, L, V, B = (c["hidden_size"], c["intermediate_size"], c["num_attention_heads"],
+                              c["num_key_value_heads"], c["num_hidden_layers"], c["vocab_size"],
+                              c["block_size"])
+    rows_kv = ctx + B
+    fc = 2 * ctx * F * H * H
+    per_layer = 2 * B * H * nq * 128 + 2 * rows_kv * H * 2 * nkv * 128 + 2 * B * nq * 128 * H \
+        + 2 * B * H * 2 * I + 2 * B * I * H + 4 * B * nq * rows_kv * 128
+    return batch * (fc + L * per_layer + 2 * (B - 1) * V * H)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.rows, self.proc, self.marks = [], None, []
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(gpu_id)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        rows = [r for t, r in self.rows if t0 - 0.25 <= t <= t1 + 0.25] or [r for _, r in self.rows]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[3]) for r in rows if r[3].replace(".", "").isdigit()), default=None)}
+
+
+def build_model(pkg, cfgd, ctx, batch, device, seed=0):
+    import torch
+    cfg = pkg.DFlashConfig(**cfgd)
+    cfg.target_layer_ids = list(range(F))
+    w, lm = pkg.synth_weights_q8(cfg, seed=seed, device=device)
+    model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=batch, max_ctx=ctx, max_block=cfg.block_size,
+                                 device=device)
+    return cfg, w, lm, model
+
+
+def synth_inputs(cfgd, ctx, batch, device, seed):
+    import torch
+    g = torch.Generator(device=device).manual_seed(1000 + seed)
+    H, B = cfgd["hidden_size"], cfgd["block_size"]
+    noise = (torch.randn(batch, B, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    th = torch.randn(batch, ctx, F * H, generator=g, device=device).to(torch.bfloat16)
+    return noise, th
+
+
+def synth_targets(toks, vocab, p_keep, seed):
+    """Target posterior that keeps each drafted id with probability p_keep."""
+    import torch
+    g = torch.Generator(device=toks.device).manual_seed(77 + seed)
+    b, n = toks.shape
+    keep = torch.rand(b, n, generator=g, device=toks.device) < p_keep
+    other = (toks + 1 + torch.randint(0, vocab - 1, (b, n), generator=g, device=toks.device)) % vocab
+    t = torch.where(keep, toks, other)
+    bonus = torch.randint(0, vocab, (b, 1), generator=g, device=toks.device, dtype=torch.int32)
+    return torch.cat([t.to(torch.int32), bonus], dim=1)
+
+
+# ---------------------------------------------------------------- CPU (oracle) leg
+def cpu_oracle_weights(w, lm):
+    import torch
+    from oracle import dflash_oracle as O
+    deq = lambda l, k: (l.q[k].float() * l.s[k].float()[:, None]).cpu()
+    layers = [O.OracleLayer(**{k: deq(l, k) for k in ["wq", "wk", "wv", "wo", "wg", "wu", "wd"]},
+                            in_norm=l.input_layernorm.float().cpu(),
+                            post_norm=l.post_attention_layernorm.float().cpu(),
+                            q_norm=l.q_norm.float().cpu(), k_norm=l.k_norm.float().cpu()) for l in w.layers]
+    return O.OracleWeights(w.fc.float().cpu(), w.hidden_norm.float().cpu(), w.norm.float().cpu(),
+                           lm.float().cpu(), layers)
+
+
+def cpu_step_time(cfgd, dense, noise, th, max_steps, budget_s):
+    """Time full fp32 draft steps of the CPU oracle (forward + lm_head + argmax)."""
+    import torch
+    from oracle import dflash_oracle as O
+    torch.set_num_threads(os.cpu_count())
+    ocfg = O.OracleConfig(**cfgd)
+    nz, tt = noise.float().cpu(), th.float().cpu()
+    times = []
+    t_start = time.perf_counter()
+    with torch.no_grad():
+        while len(times) < max_steps:
+            t0 = time.perf_counter()
+            hid = O.draft_forward(ocfg, dense, nz, tt)
+            O.greedy(O.draft_logits(dense, hid, cfgd["block_size"]))
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    return times
+
+
+def run_reference_arm(args, cfgd, rank, world):
+    import torch
+    pkg = _pkg()
+    if rank != 0:
+        return
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    cfg = pkg.DFlashConfig(**cfgd)
+    cfg.target_layer_ids = list(range(F))
+    w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+    noise, th = synth_inputs(cfgd, args.ctx, args.batch, dev, 0)
+    dense = cpu_oracle_weights(w, lm)
+    del w, lm
+    times = cpu_step_time(cfgd, dense, noise, th, max_steps=max(1, min(args.steps, 3)), budget_s=90)
+    if args.warmup > 0 and len(times) > 1:
+        times = times[1:]  # first call warms the allocator / threads
+    t = statistics.mean(times)
+    toks = args.batch * (cfgd["block_size"] - 1)
+    val = toks / t
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "draft tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, cfgd),
+            "cpu_baseline": {"value": val, "unit": "draft tok/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"{len(times)} full draft step(s) of the fp32 CPU restatement "
+                                       f"(oracle/dflash_oracle.py; MLX unavailable) on the same config, "
+                                       f"torch CPU with {os.cpu_count()} threads"},
+            "e2e": {"value": val, "unit": "draft tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, cfgd):
+    return {"workload": f"{args.config}: DFlash draft step, W8A16, hidden {cfgd['hidden_size']}, "
+                        f"{cfgd['num_attention_heads']}/{cfgd['num_key_value_heads']} heads, FFN "
+                        f"{cfgd['intermediate_size']}, {cfgd['num_hidden_layers']} layers, vocab "
+                        f"{cfgd['vocab_size']}, block {cfgd['block_size']}, ctx {args.ctx}, batch "
+                        f"{args.batch} per GPU",
+            "ctx": args.ctx, "block": cfgd["block_size"], "batch_per_gpu": args.batch,
+            "accept_p": 0.9, "l2": "no flush: every step streams ~3.7 GB of weights/inputs (> 126 MB L2)",
+            "parallelism": f"batch-sharded x{args.gpus}, no collectives"}
+
+
+def _pkg():
+    import importlib
+    pkg = importlib.import_module("mirror-sd_b200")
+    sys.modules.setdefault("mirror_sd_b200", pkg)
+    return pkg
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["c3", "c2"], default="c3")
+    ap.add_argument("--ctx", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfgd = dict(CFG_27B if args.config == "c3" else CFG_8B)
+    if args.ctx is None:
+        args.ctx = 4096 if args.config == "c3" else 2048
+    if args.warmup < 3:
+        args.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        run_reference_arm(args, cfgd, rank, world)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    pkg = _pkg()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg, w, lm, model = build_model(pkg, cfgd, args.ctx, args.batch, dev, seed=0)
+    noise, th = synth_inputs(cfgd, args.ctx, args.batch, dev, rank)
+    B = cfgd["block_size"]
+    out_h = torch.empty((args.batch, B, cfgd["hidden_size"]), dtype=torch.bfloat16, device=dev)
+    out_t = torch.empty((args.batch, B - 1), dtype=torch.int32, device=dev)
+    acc = torch.empty((args.batch,), dtype=torch.int32, device=dev)
+    cor = torch.empty((args.batch,), dtype=torch.int32, device=dev)
+    _, toks, _, _ = model.draft_step(noise, th, want_hidden=False)
+    target = synth_targets(toks, cfgd["vocab_size"], 0.9, rank)
+
+    def step(events=None):
+        model.draft_step(noise, th, target_tokens=target, out_hidden=out_h, out_tokens=out_t,
+                         acc_len=acc, correction=cor, phase_events=events)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    launches_per_step = model._lib.dflash_last_launch_count(model._handle)
+
+    # per-step phase events (recorded by the library on the launch stream)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(args.steps)]
+    for es in ev:
+        for e in es:
+            e.record()
+    torch.cuda.synchronize(dev)
+    props = torch.cuda.get_device_properties(dev)
+    gpu_id = getattr(props, "uuid", None)
+    sampler = ClockSampler(f"GPU-{gpu_id}" if gpu_id is not None else local) if rank == 0 else None
+    time.sleep(0.6 if sampler else 0)
+    for _ in range(3):
+        step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    start.record()
+    for i in range(args.steps):
+        step(ev[i])
+    end.record()
+    torch.cuda.synchronize(dev)
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    phases = {}
+    names = pkg._native.PHASE_NAMES
+    for k in range(1, 8):
+        phases[names[k]] = statistics.mean(ev[i][k - 1].elapsed_time(ev[i][k]) for i in range(args.steps))
+    t_ms = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
+    ms_max = float(t_ms.item())
+    acc_mean = float(acc.float().mean().item())
+
+    # end-to-end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        noise_h = noise.cpu().pin_memory()
+        th_h = th.cpu().pin_memory()
+        tgt_h = target.cpu().pin_memory()
+        tok_h = torch.empty((args.batch, B - 1), dtype=torch.int32).pin_memory()
+        acc_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
+        cor_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
+        nd, td, tg = torch.empty_like(noise), torch.empty_like(th), torch.empty_like(target)
+        k2 = max(5, min(args.steps, 50))
+
+        def e2e_step():
+            nd.copy_(noise_h, non_blocking=True)
+            td.copy_(th_h, non_blocking=True)
+            tg.copy_(tgt_h, non_blocking=True)
+            model.draft_step(nd, td, target_tokens=tg, want_hidden=False, out_tokens=out_t,
+                             acc_len=acc, correction=cor)
+            tok_h.copy_(out_t, non_blocking=True)
+            acc_h.copy_(acc, non_blocking=True)
+            cor_h.copy_(cor, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record()
+        for _ in range(k2):
+            e2e_step()
+        e2.record()
+        torch.cuda.synchronize(dev)
+        ms_e2e = torch.tensor([s2.elapsed_time(e2) / k2], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+        h2d = noise.numel() * 2 + th.numel() * 2 + target.numel() * 4
+        d2h = out_t.numel() * 4 + acc.numel() * 4 + cor.numel() * 4
+        e2e = {"value": world * args.batch * (B - 1) / (float(ms_e2e.item()) / 1e3), "unit": "draft tok/s",
+               "ms_per_step": float(ms_e2e.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "steps": k2, "api": "DFlashDraftModel.draft_step on pinned host tensors"}
+
+    if sampler:
+        sampler.stop()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    hbm, tf_burst, tf_sust, src = peaks()
+    nbytes = step_bytes(cfgd, args.ctx, args.batch)
+    nflops = step_flops(cfgd, args.ctx, args.batch)
+    fc_flops = 2.0 * args.batch * args.ctx * F * cfgd["hidden_size"] * cfgd["hidden_size"]
+    t_fc = phases["fc_gemm"] / 1e3
+    fc_tfs = fc_flops / t_fc / 1e12 if t_fc > 0 else None
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get(f"fc_gemm_{args.config}_ctx{args.ctx}")
+    t_step = ms_max / 1e3
+    line = {
+        "metric": METRIC, "value": world * args.batch * (B - 1) / t_step, "unit": "draft tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+        "us_per_step": ms_max * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "w8a16: int8 weights, bf16/f16 activations, fp32 accumulate", "data": "synthetic",
+        "config": workload_config(args, cfgd),
+        "roofline": {"bound": "tensor", "kernel": "fc GEMM (tcgen05, bf16)", "achieved": fc_tfs,
+                     "peak": tf_sust, "unit": "TFLOP/s", "frac": (fc_tfs / tf_sust) if fc_tfs else None,
+                     "peak_source": f"{src} bf16_tflops_sustained", "traffic": traffic,
+                     "flops_per_launch": fc_flops, "launch_ms": phases["fc_gemm"]},
+        "step_roofline": {"bytes": nbytes, "flops": nflops,
+                          "hbm_floor_ms": nbytes / (hbm * 1e9) * 1e3,
+                          "tensor_floor_ms": nflops / (tf_sust * 1e12) * 1e3,
+                          "frac_of_max_floor": max(nbytes / (hbm * 1e9), nflops / (tf_sust * 1e12)) / t_step,
+                          "hbm_frac": nbytes / t_step / (hbm * 1e9)},
+        "phases_ms": phases, "accept_len_mean": acc_mean,
+        "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step,
+        "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
+        "e2e": e2e,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        dense = cpu_oracle_weights(w, lm)
+        times = cpu_step_time(cfgd, dense, noise, th, max_steps=2, budget_s=30)
+        t = min(times)
+        line["cpu_baseline"] = {"value": args.batch * (B - 1) / t, "unit": "draft tok/s",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{len(times)} full fp32 draft step(s) (oracle/dflash_oracle.py, "
+                                          f"the reference's MLX being unavailable), best of them"}
+    print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -228,31 +228,44 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
   }
 }
 
-// merge split partials -> out [b*B, NQ*128] f16 (row = bi*B + j, col = head*128 + d)
+// merge split partials -> out [b*B, NQ*128] f16 (row = bi*B + j, col = head*128 + d);
+// one warp per (batch, head, block row), lanes split the splits for the
+// max / denominator and the head dims for the weighted sum.
 __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out) {
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
-  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   const int bi = blockIdx.y;
-  const int rows_per_b = p.nq * p.block;
-  if (warp_global >= rows_per_b) return;
-  const int head = warp_global / p.block, j = warp_global % p.block;
+  if (row >= p.nq * p.block) return;
+  const int head = row / p.block, j = row % p.block;
   const int kvh = head / G;
   const int r = (head - kvh * G) * p.block + j;
   const size_t base = (((size_t)bi * p.nkv + kvh) * p.splits) * (size_t)R + r;
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, p.mpart[base + (size_t)s * R]);
+  for (int s = lane; s < p.splits; s += 32) M = fmaxf(M, p.mpart[base + (size_t)s * R]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float Ms = (M == -INFINITY) ? 0.f : M;
   float L = 0.f;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < p.splits; ++s) {
-    const size_t idx = base + (size_t)s * R;
-    const float w = exp2f(p.mpart[idx] - Ms);
-    L += p.lpart[idx] * w;
-    const float4 ov = *reinterpret_cast<const float4*>(p.opart + idx * 128 + lane * 4);
-    acc[0] += ov.x * w; acc[1] += ov.y * w; acc[2] += ov.z * w; acc[3] += ov.w * w;
+  for (int s0 = 0; s0 < p.splits; s0 += 32) {
+    const int s = s0 + lane;
+    float w = 0.f;
+    if (s < p.splits) {
+      const size_t idx = base + (size_t)s * R;
+      w = exp2f(p.mpart[idx] - Ms);
+      L += p.lpart[idx] * w;
+    }
+    const int n = min(32, p.splits - s0);
+#pragma unroll 4
+    for (int t = 0; t < n; ++t) {
+      const float wt = __shfl_sync(0xffffffffu, w, t);
+      const float4 ov = *reinterpret_cast<const float4*>(p.opart + (base + (size_t)(s0 + t) * R) * 128 + lane * 4);
+      acc[0] += ov.x * wt; acc[1] += ov.y * wt; acc[2] += ov.z * wt; acc[3] += ov.w * wt;
+    }
   }
+  L = warp_sum(L);
   const float inv = 1.0f / L;
   uint2 pk;
   pk.x = pack_f16x2(acc[0] * inv, acc[1] * inv);
@@ -267,10 +280,10 @@ size_t attn_smem_bytes(int nq, int nkv, int block) {
   return ((size_t)RP * AT_LD + (size_t)4 * AT_TK * AT_LD) * 2;
 }
 
-// choose the KV split so that b * NKV * splits covers the SMs about twice
+// choose the KV split so that b * NKV * splits covers the SMs about once
 void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits) {
   const int per = batch * nkv;
-  int s = (2 * num_sms + per - 1) / per;
+  int s = (num_sms + per - 1) / per;
   const int max_s = (kv_len + AT_TK - 1) / AT_TK;
   if (s > max_s) s = max_s;
   if (s < 1) s = 1;

@@ -68,7 +68,7 @@ struct Layer {
 struct Handle {
   int device = 0;
   int num_sms = 148;
-  int max_splits = 16;
+  int max_splits = 8;
   DFlashDims d{};
   Arena arena;
   std::mutex mu;
@@ -87,6 +87,7 @@ struct Handle {
   float* ctx_part = nullptr;
   __half* ctx_n = nullptr;
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
+  __half* xn = nullptr;             // RMSNorm'd block rows (f16) feeding q|k|v and gate|up
   float *opart = nullptr, *mpart = nullptr, *lpart = nullptr;
   size_t attn_part_rows = 0;
   __nv_bfloat16* hn = nullptr;
@@ -208,22 +209,22 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(A.alloc(&ly.w_qkv, (size_t)nqkv * H));
     CKC(A.alloc(&ly.s_qkv, nqkv));
     CKC(w8_repack_launch(lw.wq, NQ * 128, H, ly.w_qkv, big, 0, 0, st));
-    CKC(w8_repack_launch(lw.wk, NKV * 128, H, ly.w_qkv, big, 0, NQ * 8, st));
-    CKC(w8_repack_launch(lw.wv, NKV * 128, H, ly.w_qkv, big, 0, (NQ + NKV) * 8, st));
+    CKC(w8_repack_launch(lw.wk, NKV * 128, H, ly.w_qkv, big, 0, NQ * 128, st));
+    CKC(w8_repack_launch(lw.wv, NKV * 128, H, ly.w_qkv, big, 0, (NQ + NKV) * 128, st));
     CKC(w8_scale_launch((const __half*)lw.sq, NQ * 128, ly.s_qkv, big, 0, 0, st));
-    CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, ly.s_qkv, big, 0, NQ * 8, st));
-    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, ly.s_qkv, big, 0, (NQ + NKV) * 8, st));
+    CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, ly.s_qkv, big, 0, NQ * 128, st));
+    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, ly.s_qkv, big, 0, (NQ + NKV) * 128, st));
     CKC(A.alloc(&ly.w_o, (size_t)H * NQ * 128));
     CKC(A.alloc(&ly.s_o, H));
     CKC(w8_repack_launch(lw.wo, H, NQ * 128, ly.w_o, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.so, H, ly.s_o, big, 0, 0, st));
-    // gate/up interleaved per 256-channel tile: 8 gate row-blocks then 8 up row-blocks
+    // gate/up interleaved per 128-channel tile: 64 gate channels then the 64 matching up channels
     CKC(A.alloc(&ly.w_gu, (size_t)2 * I * H));
     CKC(A.alloc(&ly.s_gu, 2 * I));
-    CKC(w8_repack_launch(lw.wg, I, H, ly.w_gu, 8, 16, 0, st));
-    CKC(w8_repack_launch(lw.wu, I, H, ly.w_gu, 8, 16, 8, st));
-    CKC(w8_scale_launch((const __half*)lw.sg, I, ly.s_gu, 8, 16, 0, st));
-    CKC(w8_scale_launch((const __half*)lw.su, I, ly.s_gu, 8, 16, 8, st));
+    CKC(w8_repack_launch(lw.wg, I, H, ly.w_gu, 64, 128, 0, st));
+    CKC(w8_repack_launch(lw.wu, I, H, ly.w_gu, 64, 128, 64, st));
+    CKC(w8_scale_launch((const __half*)lw.sg, I, ly.s_gu, 64, 128, 0, st));
+    CKC(w8_scale_launch((const __half*)lw.su, I, ly.s_gu, 64, 128, 64, st));
     CKC(A.alloc(&ly.w_d, (size_t)H * I));
     CKC(A.alloc(&ly.s_d, H));
     CKC(w8_repack_launch(lw.wd, H, I, ly.w_d, big, 0, 0, st));
@@ -240,7 +241,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(i8_to_f16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
     CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
     CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, 0, st));
-    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 8, st));
+    CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 128, st));
     hd->layers.push_back(ly);
   }
   // ---- workspace
@@ -262,13 +263,14 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->Q, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->attn_out, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->act, (size_t)Mx * I));
+  CKC(A.alloc(&hd->xn, (size_t)Mx * H));
   hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, kvcap, hd->num_sms);
   CKC(A.alloc(&hd->opart, hd->attn_part_rows * 128));
   CKC(A.alloc(&hd->mpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->lpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->hn, (size_t)Mx * H));
-  CKC(A.alloc(&hd->lm_val, (size_t)hd->num_sms * Mx));
-  CKC(A.alloc(&hd->lm_idx, (size_t)hd->num_sms * Mx));
+  CKC(A.alloc(&hd->lm_val, (size_t)2 * hd->num_sms * Mx));
+  CKC(A.alloc(&hd->lm_idx, (size_t)2 * hd->num_sms * Mx));
   CKC(A.alloc(&hd->dev_err, 1));
   CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
   CKC(cudaDeviceSynchronize());
@@ -371,14 +373,15 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     __half* Kl = hd->K + l * layer_stride;
     __half* Vl = hd->V + l * layer_stride;
     // q | k | v of the block rows: input RMSNorm fused into the activation load
+    CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xn, st));
     W8Params p{};
     p.w = ly.w_qkv; p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
-    p.h = hd->h; p.hstat = hd->hstat; p.hparts = hparts; p.norm_w = ly.in_norm; p.eps = d.rms_norm_eps;
+    p.x = hd->xn; p.eps = d.rms_norm_eps;
     p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
     p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.kv_rows = kv_cap;
-    p.kv_row0 = C; p.err = hd->dev_err;
+    p.kv_row0 = C;
     p.splits = w8_pick_splits(p.N, p.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(p, kQKV, kXHNorm, st));
+    CK(w8_gemm_launch(p, kQKV, st));
     // attention over [context ; block]
     AttnParams ap{};
     ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kv_cap;
@@ -390,24 +393,24 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     // o_proj + residual
     W8Params o{};
     o.w = ly.w_o; o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
-    o.h_out = hd->h; o.hstat_out = hd->hstat; o.err = hd->dev_err;
+    o.h_out = hd->h; o.hstat_out = hd->hstat;
     o.splits = w8_pick_splits(o.N, o.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(o, kResid, kXF16, st));
+    CK(w8_gemm_launch(o, kResid, st));
     hparts = H / 128;
     // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
+    CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xn, st));
     W8Params gu{};
     gu.w = ly.w_gu; gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
-    gu.h = hd->h; gu.hstat = hd->hstat; gu.hparts = hparts; gu.norm_w = ly.post_norm;
-    gu.eps = d.rms_norm_eps; gu.act = hd->act; gu.err = hd->dev_err;
+    gu.x = hd->xn; gu.act = hd->act;
     gu.splits = w8_pick_splits(gu.N, gu.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(gu, kSiluMul, kXHNorm, st));
+    CK(w8_gemm_launch(gu, kSiluMul, st));
     // down + residual
     W8Params dn{};
     dn.w = ly.w_d; dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
-    dn.h_out = hd->h; dn.hstat_out = hd->hstat; dn.err = hd->dev_err;
+    dn.h_out = hd->h; dn.hstat_out = hd->hstat;
     dn.splits = w8_pick_splits(dn.N, dn.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(dn, kResid, kXF16, st));
-    launches += 6;  // qkv, attention partial + combine, o, gate|up, down
+    CK(w8_gemm_launch(dn, kResid, st));
+    launches += 8;  // 2 norms, qkv, attention partial + combine, o, gate|up, down
   }
   CK(mark(5));
   CK(final_norm_launch(hd->h, hd->hstat, hparts, M, H, hd->norm, d.rms_norm_eps, hd->hn,
@@ -418,8 +421,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     LmParams lp{};
     lp.E = hd->lm_head; lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
     lp.best_val = hd->lm_val; lp.best_idx = hd->lm_idx;
-    CK(lm_argmax_launch(lp, hd->num_sms, st));
-    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, hd->num_sms, M, B, b, a->out_tokens,
+    CK(lm_argmax_launch(lp, 2 * hd->num_sms, st));
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, 2 * hd->num_sms, M, B, b, a->out_tokens,
                             a->target_tokens, a->acc_len, a->correction, st));
     launches += 2;
   }
@@ -467,8 +470,8 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   W8Params p{};
   p.w = wp; p.scale = sp; p.N = N; p.K = K; p.M = M;
   p.x = reinterpret_cast<const __half*>(x); p.y = reinterpret_cast<__half*>(y);
-  p.splits = w8_pick_splits(N, K, M, sms, 16);
-  cudaError_t e = w8_gemm_launch(p, kStore, kXF16, st);
+  p.splits = w8_pick_splits(N, K, M, sms, 8);
+  cudaError_t e = w8_gemm_launch(p, kStore, st);
   cudaFreeAsync(wp, st);
   cudaFreeAsync(sp, st);
   CK(e);
@@ -564,7 +567,7 @@ size_t dflash_lm_head_workspace_size(int batch, int block) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (size_t)sms * batch * block * 8 + 256;
+  return (size_t)2 * sms * batch * block * 8 + 256;
 }
 
 int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H, int V,
@@ -586,9 +589,9 @@ int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int 
   p.hn = reinterpret_cast<const __nv_bfloat16*>(hn);
   p.V = V; p.H = H; p.M = M;
   p.best_val = static_cast<float*>(workspace);
-  p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)sms * M);
-  CK(lm_argmax_launch(p, sms, st));
-  CK(argmax_accept_launch(p.best_val, p.best_idx, sms, M, block, batch, tokens, target, acc_len,
+  p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)2 * sms * M);
+  CK(lm_argmax_launch(p, 2 * sms, st));
+  CK(argmax_accept_launch(p.best_val, p.best_idx, 2 * sms, M, block, batch, tokens, target, acc_len,
                           correction, st));
   return DFLASH_OK;
 }

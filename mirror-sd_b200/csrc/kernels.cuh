@@ -50,7 +50,9 @@ struct LmParams {
 };
 
 // ---- host launchers (return cudaErrorInvalidValue on unsupported shapes)
-cudaError_t w8_gemm_launch(const W8Params& p, int mode, int xsrc, cudaStream_t st);
+cudaError_t w8_gemm_launch(const W8Params& p, int mode, cudaStream_t st);
+cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
+                               const float* w, float eps, __half* x, cudaStream_t st);
 int w8_pick_splits(int N, int K, int M, int num_sms, int max_splits);
 size_t w8_smem_bytes(const W8Params& p);
 cudaError_t w8_repack_launch(const int8_t* src, int n_src, int K, uint8_t* dst, int grp,

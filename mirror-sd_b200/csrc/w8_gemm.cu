@@ -20,6 +20,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   return v;
 }
 
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
 // lane holds channels 4*lane .. 4*lane+3 of one 128-wide head; rotate
 // (split-half neox: pairs d and d+64 live in lanes l and l^16).
 __device__ __forceinline__ void rope_lane(float (&y)[4], int lane,
@@ -38,8 +44,8 @@ __device__ __forceinline__ void rope_lane(float (&y)[4], int lane,
   }
 }
 
-template <int MT, int MODE, int XSRC>
-__global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p) {
+template <int MT, int MODE>
+__global__ void __launch_bounds__(W8_WARPS * 32, (MT >= 8 ? 2 : 3)) w8_gemm_kernel(const W8Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int MP = MT * 8;
   const int S = p.splits;
@@ -51,67 +57,37 @@ __global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p
   const int kb0 = split * nkb_all / S;
   const int nkb = (split + 1) * nkb_all / S - kb0;
   const int kslice = nkb * 64;
-  const int xstride = kslice + 8;  // halves; +16 B per row keeps ldmatrix-style reads conflict free
-  __half* xs = reinterpret_cast<__half*>(smem);
-  float* rstd_s = reinterpret_cast<float*>(smem + (size_t)MP * xstride * 2);
+  const int nchunks = (kslice + W8_CHK - 1) / W8_CHK;
+  __half* ring = reinterpret_cast<__half*>(smem);
 
   // 1) start streaming this warp's weights before touching activations
-  const int rb0 = (tile * W8_NT + warp * 32) >> 4;
-  const uint8_t* wp0 = p.w + w8_packed_offset(rb0, kb0, 0, lane, p.K);
-  const uint8_t* wp1 = p.w + w8_packed_offset(rb0 + 1, kb0, 0, lane, p.K);
+  const uint8_t* wp = p.w + w8_packed_offset(tile, kb0, warp, 0, 0, lane, p.K);
+  constexpr size_t KB_STRIDE = (size_t)W8_WARPS * 2048;  // bytes between consecutive k64 blocks
   uint4 wb[W8_PD][4];
 #pragma unroll
-  for (int j = 0; j < W8_PD; ++j) {
-    if (j < nkb) {
-      wb[j][0] = ldg_stream(wp0 + (size_t)j * 1024);
-      wb[j][1] = ldg_stream(wp0 + (size_t)j * 1024 + 512);
-      wb[j][2] = ldg_stream(wp1 + (size_t)j * 1024);
-      wb[j][3] = ldg_stream(wp1 + (size_t)j * 1024 + 512);
-    }
-  }
+  for (int j = 0; j < W8_PD; ++j)
+    if (j < nkb)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) wb[j][r] = ldg_stream(wp + j * KB_STRIDE + r * 512);
 
-  // 2) activations -> shared (f16), rows >= M are zero
-  if (XSRC == kXHNorm) {
-    if (threadIdx.x < MP) {
-      const int m = threadIdx.x;
-      float r = 0.f;
-      if (m < p.M) {
-        float ss = 0.f;
-        for (int q = 0; q < p.hparts; ++q) ss += p.hstat[(size_t)q * p.M + m];
-        r = rsqrtf(ss / static_cast<float>(p.K) + p.eps);
+  // 2) activation ring: chunk q holds X[0..MP)[kb0*64 + q*CHK, +CHK)
+  auto load_chunk = [&](int q) {
+    if (q < nchunks) {
+      __half* st = ring + (size_t)(q % W8_NST) * MP * W8_XLD;
+      const int k0 = q * W8_CHK;
+      const int cpr = min(W8_CHK, kslice - k0) / 8;
+      for (int idx = threadIdx.x; idx < MP * cpr; idx += W8_WARPS * 32) {
+        const int m = idx / cpr, kk = (idx - m * cpr) * 8;
+        const bool ok = m < p.M;
+        const __half* src = p.x + (size_t)(ok ? m : 0) * p.K + (size_t)kb0 * 64 + k0 + kk;
+        cp_async16_zfill(smem_u32(st + m * W8_XLD + kk), src, ok);
       }
-      rstd_s[m] = r;
     }
-    __syncthreads();
-  }
-  {
-    const int cpr = kslice / 8;  // 16-byte chunks per row
-    for (int idx = threadIdx.x; idx < MP * cpr; idx += blockDim.x) {
-      const int m = idx / cpr;
-      const int kk = (idx - m * cpr) * 8;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (m < p.M) {
-        const size_t gk = (size_t)kb0 * 64 + kk;
-        if (XSRC == kXF16) {
-          val = *reinterpret_cast<const uint4*>(p.x + (size_t)m * p.K + gk);
-        } else {
-          const float4 a = *reinterpret_cast<const float4*>(p.h + (size_t)m * p.K + gk);
-          const float4 b = *reinterpret_cast<const float4*>(p.h + (size_t)m * p.K + gk + 4);
-          const float4 wa = *reinterpret_cast<const float4*>(p.norm_w + gk);
-          const float4 wb4 = *reinterpret_cast<const float4*>(p.norm_w + gk + 4);
-          const float r = rstd_s[m];
-          val.x = pack_f16x2(a.x * r * wa.x, a.y * r * wa.y);
-          val.y = pack_f16x2(a.z * r * wa.z, a.w * r * wa.w);
-          val.z = pack_f16x2(b.x * r * wb4.x, b.y * r * wb4.y);
-          val.w = pack_f16x2(b.z * r * wb4.z, b.w * r * wb4.w);
-        }
-      }
-      *reinterpret_cast<uint4*>(xs + (size_t)m * xstride + kk) = val;
-    }
-  }
-  __syncthreads();
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int q = 0; q < W8_NST - 1; ++q) load_chunk(q);
 
-  // 3) main loop over this CTA's K slice, k64 blocks
   float acc[2][MT][4];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
@@ -120,51 +96,57 @@ __global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[r][t][e] = 0.f;
 
-  const uint32_t xs_base = smem_u32(xs) + (uint32_t)((g * xstride + c * 16) * 2);
-  for (int kbb = 0; kbb < nkb; kbb += W8_PD) {
+  // 3) main loop over k64 blocks; a new ring chunk starts every CHK/64 blocks
+  //    (the condition is uniform across the CTA, so the barrier is too)
+  constexpr int KB_PER_CHUNK = W8_CHK / 64;
+  const uint32_t ring_base = smem_u32(ring) + (uint32_t)((g * W8_XLD + c * 16) * 2);
+  for (int kb = 0; kb < nkb; kb += W8_PD) {
 #pragma unroll
     for (int j = 0; j < W8_PD; ++j) {
-      const int kb = kbb + j;
-      if (kb < nkb) {
+      const int k = kb + j;
+      if (k < nkb) {
+        if (k % KB_PER_CHUNK == 0) {
+          cp_async_wait<W8_NST - 2>();
+          __syncthreads();
+          load_chunk(k / KB_PER_CHUNK + W8_NST - 1);
+        }
         const uint4 cur0 = wb[j][0], cur1 = wb[j][1], cur2 = wb[j][2], cur3 = wb[j][3];
-        const int kn = kb + W8_PD;
-        if (kn < nkb) {
-          wb[j][0] = ldg_stream(wp0 + (size_t)kn * 1024);
-          wb[j][1] = ldg_stream(wp0 + (size_t)kn * 1024 + 512);
-          wb[j][2] = ldg_stream(wp1 + (size_t)kn * 1024);
-          wb[j][3] = ldg_stream(wp1 + (size_t)kn * 1024 + 512);
-        }
-        uint4 xa[MT], xb[MT];
+        if (k + W8_PD < nkb)
 #pragma unroll
-        for (int t = 0; t < MT; ++t) {
-          const uint32_t a = xs_base + (uint32_t)((t * 8 * xstride + kb * 64) * 2);
-          xa[t] = lds128(a);
-          xb[t] = lds128(a + 16);
-        }
+          for (int r = 0; r < 4; ++r) wb[j][r] = ldg_stream(wp + (size_t)(k + W8_PD) * KB_STRIDE + r * 512);
+        const uint32_t kaddr = ring_base +
+            (uint32_t)((((k / KB_PER_CHUNK) % W8_NST) * MP * W8_XLD + (k % KB_PER_CHUNK) * 64) * 2);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t r0a0 = u8x2_to_f16x2(word_of(cur0, i), 0x5140);
-          const uint32_t r0a2 = u8x2_to_f16x2(word_of(cur0, i), 0x5342);
-          const uint32_t r0a1 = u8x2_to_f16x2(word_of(cur1, i), 0x5140);
-          const uint32_t r0a3 = u8x2_to_f16x2(word_of(cur1, i), 0x5342);
-          const uint32_t r1a0 = u8x2_to_f16x2(word_of(cur2, i), 0x5140);
-          const uint32_t r1a2 = u8x2_to_f16x2(word_of(cur2, i), 0x5342);
-          const uint32_t r1a1 = u8x2_to_f16x2(word_of(cur3, i), 0x5140);
-          const uint32_t r1a3 = u8x2_to_f16x2(word_of(cur3, i), 0x5342);
+        for (int ih = 0; ih < 2; ++ih) {
+          // activation row t*8+g, k = 16c + 8ih .. +7 : halves for MMAs i = 2ih, 2ih+1
+          uint4 xq[MT];
 #pragma unroll
-          for (int t = 0; t < MT; ++t) {
-            const uint4& xv = (i < 2) ? xa[t] : xb[t];
-            const uint32_t b0 = (i & 1) ? xv.z : xv.x;
-            const uint32_t b1 = (i & 1) ? xv.w : xv.y;
-            mma_f16_16816(acc[0][t], r0a0, r0a1, r0a2, r0a3, b0, b1);
-            mma_f16_16816(acc[1][t], r1a0, r1a1, r1a2, r1a3, b0, b1);
+          for (int t = 0; t < MT; ++t) xq[t] = lds128(kaddr + (uint32_t)(t * 8 * W8_XLD * 2 + ih * 16));
+#pragma unroll
+          for (int i = 2 * ih; i < 2 * ih + 2; ++i) {
+            const uint32_t r0a0 = u8x2_to_f16x2(word_of(cur0, i), 0x5140);
+            const uint32_t r0a2 = u8x2_to_f16x2(word_of(cur0, i), 0x5342);
+            const uint32_t r0a1 = u8x2_to_f16x2(word_of(cur1, i), 0x5140);
+            const uint32_t r0a3 = u8x2_to_f16x2(word_of(cur1, i), 0x5342);
+            const uint32_t r1a0 = u8x2_to_f16x2(word_of(cur2, i), 0x5140);
+            const uint32_t r1a2 = u8x2_to_f16x2(word_of(cur2, i), 0x5342);
+            const uint32_t r1a1 = u8x2_to_f16x2(word_of(cur3, i), 0x5140);
+            const uint32_t r1a3 = u8x2_to_f16x2(word_of(cur3, i), 0x5342);
+#pragma unroll
+            for (int t = 0; t < MT; ++t) {
+              const uint32_t b0 = (i & 1) ? xq[t].z : xq[t].x;
+              const uint32_t b1 = (i & 1) ? xq[t].w : xq[t].y;
+              mma_f16_16816(acc[0][t], r0a0, r0a1, r0a2, r0a3, b0, b1);
+              mma_f16_16816(acc[1][t], r1a0, r1a1, r1a2, r1a3, b0, b1);
+            }
           }
         }
       }
     }
   }
+  cp_async_wait<0>();
 
-  // 4) partial tile -> shared (aliases the activation tile)
+  // 4) partial tile -> shared (aliases the ring)
   constexpr int RS = MP + 1;
   float* red = reinterpret_cast<float*>(smem);
   __syncthreads();
@@ -182,29 +164,26 @@ __global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p
   cg::cluster_group cluster = cg::this_cluster();
   if (S > 1) cluster.sync(); else __syncthreads();
 
-  // 5) epilogue: items are (row, 128-channel group); a warp owns an item,
-  //    a lane owns 4 consecutive channels.  Rank r of the cluster takes items
-  //    r, r+S, ... and sums the S partials in rank order.
-  const int groups = (MODE == kSiluMul) ? 1 : 2;
-  const int items = p.M * groups;
-  for (int it = split + S * warp; it < items; it += S * W8_WARPS) {
-    const int m = it / groups;
-    const int grp = it - m * groups;
+  // 5) epilogue: one item per activation row (the whole 128-channel tile); a
+  //    warp owns an item; rank r of the cluster takes rows r, r+S, ...; the S
+  //    partials are summed in rank order.
+  constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;  // outputs per lane
+  for (int m = split + S * warp; m < p.M; m += S * W8_WARPS) {
     float v[4], u[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) { v[e] = 0.f; u[e] = 0.f; }
-    const int ch0 = grp * 128 + lane * 4;
+    const int ch0 = lane * EPC;
     for (int s = 0; s < S; ++s) {
       const float* rr = (S > 1) ? cluster.map_shared_rank(red, s) : red;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < EPC; ++e) {
         v[e] += rr[(ch0 + e) * RS + m];
-        if (MODE == kSiluMul) u[e] += rr[(ch0 + 128 + e) * RS + m];
+        if (MODE == kSiluMul) u[e] += rr[(ch0 + 64 + e) * RS + m];
       }
     }
     const int gch = tile * W8_NT + ch0;  // global output channel of v[0]
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] *= __ldg(p.scale + gch + e);
+    for (int e = 0; e < EPC; ++e) v[e] *= __ldg(p.scale + gch + e);
 
     if (MODE == kStore) {
       uint2 o;
@@ -218,21 +197,19 @@ __global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p
       *hp = hv;
       float ss = hv.x * hv.x + hv.y * hv.y + hv.z * hv.z + hv.w * hv.w;
       ss = warp_sum(ss);
-      if (lane == 0) p.hstat_out[(size_t)(gch / 128) * p.M + m] = ss;
+      if (lane == 0) p.hstat_out[(size_t)tile * p.M + m] = ss;
     } else if (MODE == kSiluMul) {
-      float o[4];
+      float o[2];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 2; ++e) {
         const float gv = v[e];
-        const float uv = u[e] * __ldg(p.scale + gch + 128 + e);
+        const float uv = u[e] * __ldg(p.scale + gch + 64 + e);
         o[e] = (gv / (1.0f + expf(-gv))) * uv;
       }
-      uint2 pk;
-      pk.x = pack_f16x2(o[0], o[1]);
-      pk.y = pack_f16x2(o[2], o[3]);
-      *reinterpret_cast<uint2*>(p.act + (size_t)m * (p.N / 2) + tile * 128 + lane * 4) = pk;
-    } else {  // kQKV
-      const int head = gch / 128;
+      *reinterpret_cast<uint32_t*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) =
+          pack_f16x2(o[0], o[1]);
+    } else {  // kQKV: the tile is one head
+      const int head = tile;
       const int bi = m / p.block, j = m - bi * p.block;
       const bool is_q = head < p.n_q_heads;
       const bool is_k = !is_q && head < p.n_q_heads + p.n_kv_heads;
@@ -263,34 +240,71 @@ __global__ void __launch_bounds__(W8_WARPS * 32) w8_gemm_kernel(const W8Params p
   if (S > 1) cluster.sync();
 }
 
+// ------------------------------------------------------------------ RMSNorm rows
+// x[m, k] = f16(h[m, k] * rsqrt(sum_p hstat[p, m] / K + eps) * w[k]); one CTA per row
+__global__ void rmsnorm_f16_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
+                                   int hparts, int M, int K, const float* __restrict__ w, float eps,
+                                   __half* __restrict__ x) {
+  const int m = blockIdx.x;
+  __shared__ float part[32];
+  float ss = 0.f;
+  for (int q = threadIdx.x; q < hparts; q += blockDim.x) ss += hstat[(size_t)q * M + m];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) part[0] = rsqrtf(t / static_cast<float>(K) + eps);
+  }
+  __syncthreads();
+  const float r = part[0];
+  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+    const float4 a = *reinterpret_cast<const float4*>(h + (size_t)m * K + k);
+    const float4 b = *reinterpret_cast<const float4*>(h + (size_t)m * K + k + 4);
+    const float4 wa = *reinterpret_cast<const float4*>(w + k);
+    const float4 wb = *reinterpret_cast<const float4*>(w + k + 4);
+    uint4 o;
+    o.x = pack_f16x2(a.x * r * wa.x, a.y * r * wa.y);
+    o.y = pack_f16x2(a.z * r * wa.z, a.w * r * wa.w);
+    o.z = pack_f16x2(b.x * r * wb.x, b.y * r * wb.y);
+    o.w = pack_f16x2(b.z * r * wb.z, b.w * r * wb.w);
+    *reinterpret_cast<uint4*>(x + (size_t)m * K + k) = o;
+  }
+}
+
 // ------------------------------------------------------------------ repack
-// dst row-block = (src_rb / grp) * gstride + src_rb % grp + base
+// Source channel r lands on output channel d = (r / grp) * gstride + r % grp + base
+// (plain copy: grp >= n_src; gate/up interleave: grp 64, gstride 128, base 0 / 64).
+__device__ __forceinline__ int w8_dst_channel(int r, int grp, int gstride, int base) {
+  return (r / grp) * gstride + r % grp + base;
+}
+
 __global__ void w8_repack_kernel(const int8_t* __restrict__ src, int n_src, int K,
                                  uint8_t* __restrict__ dst, int grp, int gstride, int base) {
-  const size_t nchunks = (size_t)(n_src / 16) * (K / 64) * 64;
-  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < nchunks;
+  const int nkb = K / 64;
+  const size_t total = (size_t)n_src * nkb * 4;  // 16-byte pieces
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
-    const int lane = idx & 31;
-    const int half = (idx >> 5) & 1;
-    const size_t rest = idx >> 6;
-    const int kb = rest % (K / 64);
-    const int rb = rest / (K / 64);
-    const int row = rb * 16 + (lane >> 2) + half * 8;
-    const int col = kb * 64 + 16 * (lane & 3);
-    uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)row * K + col);
+    const int c = idx & 3;
+    const size_t rest = idx >> 2;
+    const int kb = rest % nkb;
+    const int r = rest / nkb;
+    uint4 v = *reinterpret_cast<const uint4*>(src + (size_t)r * K + kb * 64 + 16 * c);
     v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
-    const int drb = (rb / grp) * gstride + rb % grp + base;
-    *reinterpret_cast<uint4*>(dst + w8_packed_offset(drb, kb, half, lane, K)) = v;
+    const int d = w8_dst_channel(r, grp, gstride, base);
+    const int tile = d / W8_NT, in_tile = d % W8_NT;
+    const int warp = in_tile / 32, rb = (in_tile % 32) / 16, within = in_tile % 16;
+    const int lane = 4 * (within % 8) + c, half = within / 8;
+    *reinterpret_cast<uint4*>(dst + w8_packed_offset(tile, kb, warp, rb, half, lane, K)) = v;
   }
 }
 
 __global__ void w8_scale_kernel(const __half* __restrict__ s, int n_src, float* __restrict__ dst,
                                 int grp, int gstride, int base) {
-  const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-  if (ch >= n_src) return;
-  const int rb = ch >> 4;
-  const int drb = (rb / grp) * gstride + rb % grp + base;
-  dst[drb * 16 + (ch & 15)] = __half2float(s[ch]);
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n_src) return;
+  dst[w8_dst_channel(r, grp, gstride, base)] = __half2float(s[r]);
 }
 
 // ------------------------------------------------------------------ quantiser
@@ -323,15 +337,11 @@ __global__ void quantize_q8_kernel(const float* __restrict__ w, int ic, int8_t* 
 }
 
 // ------------------------------------------------------------------ host
-template <int MT, int MODE, int XSRC>
+template <int MT, int MODE>
 static cudaError_t launch_mt(const W8Params& p, size_t smem, cudaStream_t st) {
-  auto kern = w8_gemm_kernel<MT, MODE, XSRC>;
+  auto kern = w8_gemm_kernel<MT, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  if (p.splits > 8) {
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((p.N / W8_NT) * p.splits);
   cfg.blockDim = dim3(W8_WARPS * 32);
@@ -347,66 +357,62 @@ static cudaError_t launch_mt(const W8Params& p, size_t smem, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int MODE, int XSRC>
+template <int MODE>
 static cudaError_t launch_mode(const W8Params& p, size_t smem, cudaStream_t st) {
-  if (p.M <= 8) return launch_mt<1, MODE, XSRC>(p, smem, st);
-  if (p.M <= 16) return launch_mt<2, MODE, XSRC>(p, smem, st);
-  if (p.M <= 32) return launch_mt<4, MODE, XSRC>(p, smem, st);
-  return launch_mt<8, MODE, XSRC>(p, smem, st);
+  if (p.M <= 8) return launch_mt<1, MODE>(p, smem, st);
+  if (p.M <= 16) return launch_mt<2, MODE>(p, smem, st);
+  if (p.M <= 32) return launch_mt<4, MODE>(p, smem, st);
+  return launch_mt<8, MODE>(p, smem, st);
 }
 
+// K-split (= cluster size, power of two, <= 8): the largest split whose grid
+// still fits in one wave of three CTAs per SM, keeping >= 2 k64 blocks per CTA.
 int w8_pick_splits(int N, int K, int M, int num_sms, int max_splits) {
   const int tiles = N / W8_NT;
   const int nkb = K / 64;
-  const int mp = M <= 8 ? 8 : (M <= 16 ? 16 : (M <= 32 ? 32 : 64));
+  const int per_sm = M > 32 ? 2 : 3;
   int s = 1;
-  // grow the cluster until the grid covers two CTAs per SM and the activation
-  // slice stays small enough for two CTAs per SM
-  while (s < max_splits && nkb / (s * 2) >= 2 &&
-         (tiles * s < 2 * num_sms || (size_t)mp * (nkb / s * 64 + 8) * 2 > 96 * 1024))
-    s *= 2;
+  while (s * 2 <= max_splits && nkb / (s * 2) >= 2 && tiles * s * 2 <= per_sm * num_sms) s *= 2;
   return s;
 }
 
 size_t w8_smem_bytes(const W8Params& p) {
   const int mp = p.M <= 8 ? 8 : (p.M <= 16 ? 16 : (p.M <= 32 ? 32 : 64));
-  const int nkb_all = p.K / 64;
-  int max_nkb = 0;
-  for (int s = 0; s < p.splits; ++s) {
-    const int n = (s + 1) * nkb_all / p.splits - s * nkb_all / p.splits;
-    if (n > max_nkb) max_nkb = n;
-  }
-  const size_t xs = (size_t)mp * (max_nkb * 64 + 8) * 2 + mp * 4;
+  const size_t ring = (size_t)W8_NST * mp * W8_XLD * 2;
   const size_t red = (size_t)W8_NT * (mp + 1) * 4;
-  return xs > red ? xs : red;
+  return ring > red ? ring : red;
 }
 
-static cudaError_t w8_gemm_launch_once(const W8Params& p, int mode, int xsrc, cudaStream_t st) {
+static cudaError_t w8_gemm_launch_once(const W8Params& p, int mode, cudaStream_t st) {
   const size_t smem = w8_smem_bytes(p);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  if (mode == kQKV && xsrc == kXHNorm) return launch_mode<kQKV, kXHNorm>(p, smem, st);
-  if (mode == kResid && xsrc == kXF16) return launch_mode<kResid, kXF16>(p, smem, st);
-  if (mode == kSiluMul && xsrc == kXHNorm) return launch_mode<kSiluMul, kXHNorm>(p, smem, st);
-  if (mode == kStore && xsrc == kXF16) return launch_mode<kStore, kXF16>(p, smem, st);
-  if (mode == kStore && xsrc == kXHNorm) return launch_mode<kStore, kXHNorm>(p, smem, st);
+  if (mode == kQKV) return launch_mode<kQKV>(p, smem, st);
+  if (mode == kResid) return launch_mode<kResid>(p, smem, st);
+  if (mode == kSiluMul) return launch_mode<kSiluMul>(p, smem, st);
+  if (mode == kStore) return launch_mode<kStore>(p, smem, st);
   return cudaErrorInvalidValue;
 }
 
-cudaError_t w8_gemm_launch(const W8Params& p, int mode, int xsrc, cudaStream_t st) {
-  if (p.M < 1 || p.M > 64 || p.N % W8_NT || p.K % 64 || p.splits < 1 || p.splits > 16 ||
+cudaError_t w8_gemm_launch(const W8Params& p, int mode, cudaStream_t st) {
+  if (p.M < 1 || p.M > 64 || p.N % W8_NT || p.K % 64 || p.splits < 1 || p.splits > 8 ||
       p.K / 64 < p.splits)
     return cudaErrorInvalidValue;
-  // a cluster that cannot be scheduled (too large for a GPC at this
-  // footprint) is retried with half the split
+  // a cluster that cannot be scheduled at this footprint is retried with half the split
   W8Params q = p;
   for (;;) {
-    cudaError_t e = w8_gemm_launch_once(q, mode, xsrc, st);
+    cudaError_t e = w8_gemm_launch_once(q, mode, st);
     if (e == cudaSuccess || q.splits == 1 ||
         (e != cudaErrorInvalidClusterSize && e != cudaErrorLaunchOutOfResources))
       return e;
     (void)cudaGetLastError();
     q.splits /= 2;
   }
+}
+
+cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
+                               const float* w, float eps, __half* x, cudaStream_t st) {
+  if (K % 8 || M < 1) return cudaErrorInvalidValue;
+  rmsnorm_f16_kernel<<<M, 256, 0, st>>>(h, hstat, hparts, M, K, w, eps, x);
+  return cudaGetLastError();
 }
 
 cudaError_t w8_repack_launch(const int8_t* src, int n_src, int K, uint8_t* dst, int grp,
