@@ -86,8 +86,8 @@ typedef struct DFlashWeightsView {
   const uint16_t* fc;          /* bf16 [H, F*H]; copied */
   const float* hidden_norm;    /* [H]; copied */
   const float* norm;           /* [H]; copied */
-  const uint16_t* lm_head;     /* bf16 [V, H]: the target's (tied) embedding,
-                                  referenced, NOT copied; must outlive the handle */
+  const uint16_t* lm_head;     /* bf16 [V, H]: the target's (tied) embedding; copied
+                                  into 128-row swizzled tiles (the caller may free it) */
   const DFlashLayerWeights* layers; /* HOST array of num_hidden_layers entries */
 } DFlashWeightsView;
 

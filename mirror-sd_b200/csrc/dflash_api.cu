@@ -58,10 +58,10 @@ struct Arena {
 };
 
 struct Layer {
-  uint8_t* w_qkv; float* s_qkv;
-  uint8_t* w_o; float* s_o;
-  uint8_t* w_gu; float* s_gu;
-  uint8_t* w_d; float* s_d;
+  int8_t* w_qkv; float* s_qkv;   // tile-packed int8, channels [q heads | k heads | v heads]
+  int8_t* w_o; float* s_o;
+  int8_t* w_gu; float* s_gu;     // per 128-row tile: 64 gate rows then the matching 64 up rows
+  int8_t* w_d; float* s_d;
   float *in_norm, *post_norm, *q_norm;
 };
 
@@ -74,7 +74,7 @@ struct Handle {
   std::mutex mu;
   // weights
   __nv_bfloat16* fc = nullptr;
-  const __nv_bfloat16* lm_head = nullptr;
+  uint8_t* lm_tiles = nullptr;      // lm_head packed by lm_pack_launch (128-row swizzled tiles)
   float *hidden_norm = nullptr, *norm = nullptr, *inv_freq = nullptr;
   float* k_norm_all = nullptr;     // [L, 128]
   __half* w_kv_ctx = nullptr;      // [L*2*NKV*128, H] exact f16 of the int8 K|V weights
@@ -186,7 +186,8 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   const size_t fc_elems = (size_t)H * F * H;
   CKC(A.alloc(&hd->fc, fc_elems));
   CKC(cudaMemcpyAsync(hd->fc, w->fc, fc_elems * 2, cudaMemcpyDeviceToDevice, st));
-  hd->lm_head = reinterpret_cast<const __nv_bfloat16*>(w->lm_head);
+  CKC(A.alloc(&hd->lm_tiles, lm_pack_bytes(d.vocab_size, H)));
+  CKC(lm_pack_launch(reinterpret_cast<const __nv_bfloat16*>(w->lm_head), d.vocab_size, H, hd->lm_tiles, st));
   CKC(A.alloc(&hd->hidden_norm, H));
   CKC(A.alloc(&hd->norm, H));
   CKC(cudaMemcpyAsync(hd->hidden_norm, w->hidden_norm, H * 4, cudaMemcpyDeviceToDevice, st));
@@ -208,26 +209,26 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     Layer ly{};
     CKC(A.alloc(&ly.w_qkv, (size_t)nqkv * H));
     CKC(A.alloc(&ly.s_qkv, nqkv));
-    CKC(w8_repack_launch(lw.wq, NQ * 128, H, ly.w_qkv, big, 0, 0, st));
-    CKC(w8_repack_launch(lw.wk, NKV * 128, H, ly.w_qkv, big, 0, NQ * 128, st));
-    CKC(w8_repack_launch(lw.wv, NKV * 128, H, ly.w_qkv, big, 0, (NQ + NKV) * 128, st));
+    CKC(w8_tilepack_launch(lw.wq, NQ * 128, H, ly.w_qkv, big, 0, 0, st));
+    CKC(w8_tilepack_launch(lw.wk, NKV * 128, H, ly.w_qkv, big, 0, NQ * 128, st));
+    CKC(w8_tilepack_launch(lw.wv, NKV * 128, H, ly.w_qkv, big, 0, (NQ + NKV) * 128, st));
     CKC(w8_scale_launch((const __half*)lw.sq, NQ * 128, ly.s_qkv, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, ly.s_qkv, big, 0, NQ * 128, st));
     CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, ly.s_qkv, big, 0, (NQ + NKV) * 128, st));
     CKC(A.alloc(&ly.w_o, (size_t)H * NQ * 128));
     CKC(A.alloc(&ly.s_o, H));
-    CKC(w8_repack_launch(lw.wo, H, NQ * 128, ly.w_o, big, 0, 0, st));
+    CKC(w8_tilepack_launch(lw.wo, H, NQ * 128, ly.w_o, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.so, H, ly.s_o, big, 0, 0, st));
     // gate/up interleaved per 128-channel tile: 64 gate channels then the 64 matching up channels
     CKC(A.alloc(&ly.w_gu, (size_t)2 * I * H));
     CKC(A.alloc(&ly.s_gu, 2 * I));
-    CKC(w8_repack_launch(lw.wg, I, H, ly.w_gu, 64, 128, 0, st));
-    CKC(w8_repack_launch(lw.wu, I, H, ly.w_gu, 64, 128, 64, st));
+    CKC(w8_tilepack_launch(lw.wg, I, H, ly.w_gu, 64, 128, 0, st));
+    CKC(w8_tilepack_launch(lw.wu, I, H, ly.w_gu, 64, 128, 64, st));
     CKC(w8_scale_launch((const __half*)lw.sg, I, ly.s_gu, 64, 128, 0, st));
     CKC(w8_scale_launch((const __half*)lw.su, I, ly.s_gu, 64, 128, 64, st));
     CKC(A.alloc(&ly.w_d, (size_t)H * I));
     CKC(A.alloc(&ly.s_d, H));
-    CKC(w8_repack_launch(lw.wd, H, I, ly.w_d, big, 0, 0, st));
+    CKC(w8_tilepack_launch(lw.wd, H, I, ly.w_d, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.sd, H, ly.s_d, big, 0, 0, st));
     CKC(A.alloc(&ly.in_norm, H));
     CKC(A.alloc(&ly.post_norm, H));
@@ -269,8 +270,8 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->mpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->lpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->hn, (size_t)Mx * H));
-  CKC(A.alloc(&hd->lm_val, (size_t)2 * hd->num_sms * Mx));
-  CKC(A.alloc(&hd->lm_idx, (size_t)2 * hd->num_sms * Mx));
+  CKC(A.alloc(&hd->lm_val, (size_t)hd->num_sms * Mx));
+  CKC(A.alloc(&hd->lm_idx, (size_t)hd->num_sms * Mx));
   CKC(A.alloc(&hd->dev_err, 1));
   CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
   CKC(cudaDeviceSynchronize());
@@ -375,13 +376,13 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     // q | k | v of the block rows: input RMSNorm fused into the activation load
     CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xn, st));
     W8Params p{};
-    p.w = ly.w_qkv; p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
+    p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
     p.x = hd->xn; p.eps = d.rms_norm_eps;
     p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
     p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.kv_rows = kv_cap;
     p.kv_row0 = C;
-    p.splits = w8_pick_splits(p.N, p.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(p, kQKV, st));
+    p.splits = w8tc_pick_splits(p.N, p.K, hd->num_sms);
+    CK(w8tc_launch(ly.w_qkv, p, kQKV, hd->dev_err, st));
     // attention over [context ; block]
     AttnParams ap{};
     ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kv_cap;
@@ -392,24 +393,24 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     CK(attn_launch(ap, b, hd->attn_out, st));
     // o_proj + residual
     W8Params o{};
-    o.w = ly.w_o; o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
+    o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
     o.h_out = hd->h; o.hstat_out = hd->hstat;
-    o.splits = w8_pick_splits(o.N, o.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(o, kResid, st));
+    o.splits = w8tc_pick_splits(o.N, o.K, hd->num_sms);
+    CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, st));
     hparts = H / 128;
     // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
     CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xn, st));
     W8Params gu{};
-    gu.w = ly.w_gu; gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
+    gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
     gu.x = hd->xn; gu.act = hd->act;
-    gu.splits = w8_pick_splits(gu.N, gu.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(gu, kSiluMul, st));
+    gu.splits = w8tc_pick_splits(gu.N, gu.K, hd->num_sms);
+    CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, st));
     // down + residual
     W8Params dn{};
-    dn.w = ly.w_d; dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
+    dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
     dn.h_out = hd->h; dn.hstat_out = hd->hstat;
-    dn.splits = w8_pick_splits(dn.N, dn.K, M, hd->num_sms, hd->max_splits);
-    CK(w8_gemm_launch(dn, kResid, st));
+    dn.splits = w8tc_pick_splits(dn.N, dn.K, hd->num_sms);
+    CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, st));
     launches += 8;  // 2 norms, qkv, attention partial + combine, o, gate|up, down
   }
   CK(mark(5));
@@ -419,10 +420,11 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   CK(mark(6));
   if (a->out_tokens || a->target_tokens) {
     LmParams lp{};
-    lp.E = hd->lm_head; lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
+    lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
     lp.best_val = hd->lm_val; lp.best_idx = hd->lm_idx;
-    CK(lm_argmax_launch(lp, 2 * hd->num_sms, st));
-    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, 2 * hd->num_sms, M, B, b, a->out_tokens,
+    int grid = 0;
+    CK(lm_argmax_launch(lp, hd->lm_tiles, hd->num_sms, hd->dev_err, &grid, st));
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, M, B, b, a->out_tokens,
                             a->target_tokens, a->acc_len, a->correction, st));
     launches += 2;
   }
@@ -455,26 +457,36 @@ int dflash_quantize_q8(const float* w, int oc, int ic, int8_t* q, uint16_t* s, v
 int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uint16_t* x, int M,
                      uint16_t* y, void* stream) {
   if (!q || !s || !x || !y) return fail(DFLASH_ERR_INVALID, "NULL pointer");
-  if (N % 256 || K % 64 || M < 1 || M > 64)
-    return fail(DFLASH_ERR_INVALID, "need N %% 256 == 0, K %% 64 == 0, 1 <= M <= 64");
+  if (N % 128 || K % 64 || K < 128 || M < 1 || M > 64)
+    return fail(DFLASH_ERR_INVALID, "need N %% 128 == 0, K %% 64 == 0, K >= 128, 1 <= M <= 64");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  uint8_t* wp = nullptr;
   float* sp = nullptr;
-  CK(cudaMallocAsync(&wp, (size_t)N * K, st));
+  int* err = nullptr;
   CK(cudaMallocAsync(&sp, (size_t)N * 4, st));
-  CK(w8_repack_launch(q, N, K, wp, 1 << 30, 0, 0, st));
+  CK(cudaMallocAsync(&err, sizeof(int), st));
+  CK(cudaMemsetAsync(err, 0, sizeof(int), st));
   CK(w8_scale_launch(reinterpret_cast<const __half*>(s), N, sp, 1 << 30, 0, 0, st));
+  int8_t* wt = nullptr;
+  CK(cudaMallocAsync(&wt, (size_t)N * K, st));
+  CK(w8_tilepack_launch(q, N, K, wt, 1 << 30, 0, 0, st));
   W8Params p{};
-  p.w = wp; p.scale = sp; p.N = N; p.K = K; p.M = M;
+  p.scale = sp; p.N = N; p.K = K; p.M = M;
   p.x = reinterpret_cast<const __half*>(x); p.y = reinterpret_cast<__half*>(y);
-  p.splits = w8_pick_splits(N, K, M, sms, 8);
-  cudaError_t e = w8_gemm_launch(p, kStore, st);
-  cudaFreeAsync(wp, st);
+  p.splits = w8tc_pick_splits(N, K, sms);
+  cudaError_t e = w8tc_launch(wt, p, kStore, err, st);
+  int hv = 0;
+  if (e == cudaSuccess) {
+    cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    e = cudaStreamSynchronize(st);
+  }
   cudaFreeAsync(sp, st);
+  cudaFreeAsync(wt, st);
+  cudaFreeAsync(err, st);
   CK(e);
+  if (hv) return fail(DFLASH_ERR_DEVICE, "W8A16 kernel gave up on a bounded wait (code %d)", hv);
   return DFLASH_OK;
 }
 
@@ -567,14 +579,14 @@ size_t dflash_lm_head_workspace_size(int batch, int block) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (size_t)2 * sms * batch * block * 8 + 256;
+  return (size_t)sms * batch * block * 8 + 256;
 }
 
 int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H, int V,
                           int32_t* tokens, const int32_t* target, int32_t* acc_len, int32_t* correction,
                           void* workspace, size_t ws_bytes, void* stream) {
   if (!hn || !E || !workspace) return fail(DFLASH_ERR_INVALID, "NULL pointer");
-  if (batch < 1 || block < 2 || batch * block > 64 || H % 32 || V < 1)
+  if (batch < 1 || block < 2 || batch * block > 64 || H % 64 || V < 1)
     return fail(DFLASH_ERR_INVALID, "bad lm_head shape");
   if (target && (!acc_len || !correction)) return fail(DFLASH_ERR_INVALID, "acc_len/correction required");
   if (ws_bytes < dflash_lm_head_workspace_size(batch, block))
@@ -584,15 +596,25 @@ int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int 
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int M = batch * block;
+  uint8_t* et = nullptr;
+  int* err = nullptr;
+  CK(cudaMallocAsync(&et, lm_pack_bytes(V, H), st));
+  CK(cudaMallocAsync(&err, sizeof(int), st));
+  CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  CK(lm_pack_launch(reinterpret_cast<const __nv_bfloat16*>(E), V, H, et, st));
   LmParams p{};
-  p.E = reinterpret_cast<const __nv_bfloat16*>(E);
   p.hn = reinterpret_cast<const __nv_bfloat16*>(hn);
   p.V = V; p.H = H; p.M = M;
   p.best_val = static_cast<float*>(workspace);
-  p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)2 * sms * M);
-  CK(lm_argmax_launch(p, 2 * sms, st));
-  CK(argmax_accept_launch(p.best_val, p.best_idx, 2 * sms, M, block, batch, tokens, target, acc_len,
-                          correction, st));
+  p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)sms * M);
+  int grid = 0;
+  cudaError_t e = lm_argmax_launch(p, et, sms, err, &grid, st);
+  if (e == cudaSuccess)
+    e = argmax_accept_launch(p.best_val, p.best_idx, grid, M, block, batch, tokens, target, acc_len,
+                             correction, st);
+  cudaFreeAsync(et, st);
+  cudaFreeAsync(err, st);
+  CK(e);
   return DFLASH_OK;
 }
 

@@ -54,6 +54,12 @@ cudaError_t w8_gemm_launch(const W8Params& p, int mode, cudaStream_t st);
 cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
                                const float* w, float eps, __half* x, cudaStream_t st);
 int w8_pick_splits(int N, int K, int M, int num_sms, int max_splits);
+// tcgen05 W8A16 path (w8_tc.cu): w_tiles is the int8 weight packed by
+// w8_tilepack_launch ([N/128][K/64][128][64 B])
+int w8tc_pick_splits(int N, int K, int num_sms);
+cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int* err, cudaStream_t st);
+cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst, int grp, int gstride,
+                               int base, cudaStream_t st);
 size_t w8_smem_bytes(const W8Params& p);
 cudaError_t w8_repack_launch(const int8_t* src, int n_src, int K, uint8_t* dst, int grp,
                              int gstride, int base, cudaStream_t st);
@@ -69,7 +75,11 @@ cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_
 cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
                            cudaStream_t st);
 
-cudaError_t lm_argmax_launch(const LmParams& p, int grid, cudaStream_t st);
+int lm_grid(int V, int num_sms);
+size_t lm_pack_bytes(int V, int H);
+cudaError_t lm_pack_launch(const __nv_bfloat16* E, int V, int H, uint8_t* out, cudaStream_t st);
+cudaError_t lm_argmax_launch(const LmParams& p, const uint8_t* e_tiles, int num_sms, int* err,
+                             int* grid_out, cudaStream_t st);
 cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int M, int block,
                                  int batch, int32_t* out_tokens, const int32_t* target,
                                  int32_t* acc_len, int32_t* correction, cudaStream_t st);

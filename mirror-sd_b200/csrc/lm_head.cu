@@ -26,170 +26,188 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return (v > bv) || (v == bv && i < bi);
 }
 
-constexpr int LM_PD = 3;          // k32 blocks of E in flight per warp
-constexpr int LM_CHK = 256;       // hn k per ring stage
-constexpr int LM_NST = 3;
-constexpr int LM_LD = LM_CHK + 32;  // bf16 per staged row (+64 B: conflict-free 16-byte reads)
+// ---------------------------------------------------------------- tcgen05 path
+// E is repacked once (lm_pack) into 128-row vocabulary tiles whose k64 blocks
+// are contiguous 16 KB runs already laid out in the UMMA's 128-byte swizzle:
+// [V/128][H/64][128 rows][128 B], rows >= V zero.  A CTA owns a contiguous
+// range of vocabulary tiles.  warp 0 streams E blocks (cp.async.bulk) and the
+// matching hn tile (TMA, 128-byte swizzle); warp 1 issues
+// tcgen05.mma M=128 (vocab) x N=MP (block rows) x K=16 into one of two TMEM
+// accumulators; warps 2..5 take the argmax of the other accumulator while
+// the next tile streams in.
+constexpr int LT_NS = 6;
+constexpr int LT_THREADS = 192;
+constexpr int LT_E_BYTES = 128 * 128;
 
-template <int MT>
-__global__ void __launch_bounds__(LM_WARPS * 32, 2) lm_argmax_kernel(const LmParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int MP = MT * 8;
-  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem);
+template <int MP>
+__global__ void __launch_bounds__(LT_THREADS, 1)
+    lm_tc_kernel(const __grid_constant__ CUtensorMap map_h, const LmParams p, const uint8_t* e_tiles,
+                 int tiles_per_cta, int* err) {
+  constexpr int H_BYTES = MP * 128;
+  constexpr int STAGE = LT_E_BYTES + H_BYTES;
+  static_assert(STAGE % 1024 == 0, "stage alignment");
+  constexpr uint32_t ACC_COLS = MP <= 32 ? 32 : 64;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + LT_NS * STAGE);
+  uint64_t* empty = full + LT_NS;
+  uint64_t* acc_full = empty + LT_NS;   // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red_v = reinterpret_cast<float*>(tmem_slot + 4);   // [4][64]
+  int* red_i = reinterpret_cast<int*>(red_v + 4 * 64);       // [4][64]
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int units = (p.V + 31) / 32;  // 32 vocab rows per warp-unit
-  const int u0 = (int)((long long)blockIdx.x * units / gridDim.x);
-  const int u1 = (int)((long long)(blockIdx.x + 1) * units / gridDim.x);
-  const int rounds = (u1 - u0 + LM_WARPS - 1) / LM_WARPS;
-  const int nk32 = p.H / 32;
-  const int nchunks = (p.H + LM_CHK - 1) / LM_CHK;
-  const int total_chunks = rounds * nchunks;
+  const int VT = (p.V + 127) / 128;
+  const int nkb = p.H / 64;
+  const int t0 = blockIdx.x * tiles_per_cta;
+  const int t1 = min(VT, t0 + tiles_per_cta);
+  const int ntile = max(0, t1 - t0);
 
-  // hn ring: global chunk gq = round * nchunks + q holds hn[0..MP)[q*CHK, +CHK)
-  auto load_chunk = [&](int gq) {
-    if (gq < total_chunks) {
-      __nv_bfloat16* st = ring + (size_t)(gq % LM_NST) * MP * LM_LD;
-      const int k0 = (gq % nchunks) * LM_CHK;
-      const int cpr = min(LM_CHK, p.H - k0) / 8;
-      for (int idx = threadIdx.x; idx < MP * cpr; idx += LM_WARPS * 32) {
-        const int m = idx / cpr, kk = (idx - m * cpr) * 8;
-        const bool ok = m < p.M;
-        cp_async16_zfill(smem_u32(st + m * LM_LD + kk), p.hn + (size_t)(ok ? m : 0) * p.H + k0 + kk, ok);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < LT_NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&map_h);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int ti = 0; ti < ntile; ++ti) {
+        const uint8_t* eb = e_tiles + (size_t)(t0 + ti) * nkb * LT_E_BYTES;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % LT_NS;
+          const uint32_t ph = (it / LT_NS) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, err, abort_flag)) { ti = ntile; break; }
+          uint8_t* st = smem + s * STAGE;
+          mbar_arrive_expect_tx(&full[s], STAGE);
+          bulk_load(st, eb + (size_t)kb * LT_E_BYTES, LT_E_BYTES, &full[s]);
+          tma_load_2d(st + LT_E_BYTES, &map_h, &full[s], kb * 64, 0);
+        }
       }
     }
-    cp_async_commit();
-  };
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(128, MP, 1);
+      int it = 0;
+      bool ok = true;
+      for (int ti = 0; ti < ntile && ok; ++ti) {
+        const int b = ti & 1;
+        if (!mbar_wait(&acc_empty[b], ((ti >> 1) & 1) ^ 1, err, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * ACC_COLS;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % LT_NS;
+          const uint32_t ph = (it / LT_NS) & 1;
+          if (!mbar_wait(&full[s], ph, err, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE);
+          const uint64_t adesc = umma_desc_sw128(sa);
+          const uint64_t bdesc = umma_desc_sw128(sa + LT_E_BYTES);
 #pragma unroll
-  for (int q = 0; q < LM_NST - 1; ++q) load_chunk(q);
-
-  // running best for columns (t*8 + 2c + e), identical in the 8 lanes of a column quad
-  float bv[MT][2];
-  int bi[MT][2];
-#pragma unroll
-  for (int t = 0; t < MT; ++t)
-#pragma unroll
-    for (int e = 0; e < 2; ++e) { bv[t][e] = -INFINITY; bi[t][e] = 0x7fffffff; }
-
-  const uint32_t ring_lane = smem_u32(ring) + (uint32_t)((g * LM_LD + 8 * c) * 2);
-  constexpr int K32_PER_CHUNK = LM_CHK / 32;
-  for (int rd = 0; rd < rounds; ++rd) {
-    const int u = u0 + rd * LM_WARPS + warp;
-    const bool active = u < u1;
-    const int vbase = u * 32;
-    // rows vbase + {g, g+8, 16+g, 24+g}; rows >= V clamp to V-1 (masked below)
-    const __nv_bfloat16* er[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      int v = vbase + (r >> 1) * 16 + (r & 1) * 8 + g;
-      v = v < p.V ? v : p.V - 1;
-      er[r] = p.E + (size_t)v * p.H + 8 * c;
+          for (int k = 0; k < 4; ++k) umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);
+      }
     }
-    float acc[2][MT][4];
+  } else {
+    const int q = warp & 3;
+    // running best: lane c owns columns c and c + 32
+    float bv[2] = {-INFINITY, -INFINITY};
+    int bi[2] = {0x7fffffff, 0x7fffffff};
+    for (int ti = 0; ti < ntile; ++ti) {
+      const int b = ti & 1;
+      if (!mbar_wait(&acc_full[b], (ti >> 1) & 1, err, abort_flag)) break;
+      tc_fence_after();
+      const int vrow = (t0 + ti) * 128 + q * 32 + lane;
+      const bool vok = vrow < p.V;
 #pragma unroll
-    for (int r = 0; r < 2; ++r)
+      for (int c0 = 0; c0 < MP; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + b * ACC_COLS + ((uint32_t)(q * 32) << 16) + c0, r);
+        tmem_ld_wait();
+        if (c0 + 32 >= MP) {  // last chunk: hand the accumulator back before the shuffles
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
 #pragma unroll
-      for (int t = 0; t < MT; ++t)
+        for (int c = 0; c < 32; ++c) {
+          if (c0 + c < MP) {
+            float v = __uint_as_float(r[c]);
+            int idx = vrow;
+            if (!vok || v != v) { v = -INFINITY; idx = 0x7fffffff; }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[r][t][e] = 0.f;
-    uint4 wb[LM_PD][4];
-    if (active) {
-#pragma unroll
-      for (int j = 0; j < LM_PD; ++j)
-        if (j < nk32)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) wb[j][r] = ldg_stream(er[r] + j * 32);
-    }
-    for (int kb = 0; kb < nk32; kb += LM_PD) {
-#pragma unroll
-      for (int j = 0; j < LM_PD; ++j) {
-        const int k = kb + j;
-        if (k < nk32) {
-          if (k % K32_PER_CHUNK == 0) {  // uniform across the CTA
-            cp_async_wait<LM_NST - 2>();
-            __syncthreads();
-            load_chunk(rd * nchunks + k / K32_PER_CHUNK + LM_NST - 1);
-          }
-          if (active) {
-            uint4 cur[4];
-#pragma unroll
-            for (int r = 0; r < 4; ++r) cur[r] = wb[j][r];
-            if (k + LM_PD < nk32)
-#pragma unroll
-              for (int r = 0; r < 4; ++r) wb[j][r] = ldg_stream(er[r] + (k + LM_PD) * 32);
-            const int gq = rd * nchunks + k / K32_PER_CHUNK;
-            const uint32_t kaddr = ring_lane +
-                (uint32_t)(((gq % LM_NST) * MP * LM_LD + (k % K32_PER_CHUNK) * 32) * 2);
-#pragma unroll
-            for (int t = 0; t < MT; ++t) {
-              uint4 hv;
-              asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                           : "=r"(hv.x), "=r"(hv.y), "=r"(hv.z), "=r"(hv.w)
-                           : "r"(kaddr + (uint32_t)(t * 8 * LM_LD * 2)));
-              // MMA 0: phys k 8c..8c+3 ; MMA 1: 8c+4..8c+7
-#pragma unroll
-              for (int r = 0; r < 2; ++r) {
-                mma_bf16_16816(acc[r][t], cur[2 * r].x, cur[2 * r + 1].x, cur[2 * r].y,
-                               cur[2 * r + 1].y, hv.x, hv.y);
-                mma_bf16_16816(acc[r][t], cur[2 * r].z, cur[2 * r + 1].z, cur[2 * r].w,
-                               cur[2 * r + 1].w, hv.z, hv.w);
-              }
+            for (int o = 16; o > 0; o >>= 1) {
+              const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+              const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+              if (better(ov, oi, v, idx)) { v = ov; idx = oi; }
+            }
+            if (lane == c && better(v, idx, bv[c0 / 32], bi[c0 / 32])) {
+              bv[c0 / 32] = v;
+              bi[c0 / 32] = idx;
             }
           }
         }
       }
     }
-    if (active) {
-      // candidates of this unit -> running best
-#pragma unroll
-      for (int t = 0; t < MT; ++t) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float v = -INFINITY;
-          int idx = 0x7fffffff;
-#pragma unroll
-          for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int hgh = 0; hgh < 2; ++hgh) {
-              const int vi = vbase + r * 16 + hgh * 8 + g;
-              float x = acc[r][t][hgh * 2 + e];
-              if (x != x) x = -INFINITY;
-              if (vi < p.V && better(x, vi, v, idx)) { v = x; idx = vi; }
-            }
-#pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-            if (better(ov, oi, v, idx)) { v = ov; idx = oi; }
-          }
-          if (better(v, idx, bv[t][e], bi[t][e])) { bv[t][e] = v; bi[t][e] = idx; }
-        }
-      }
-    }
+    red_v[q * 64 + lane] = bv[0];
+    red_i[q * 64 + lane] = bi[0];
+    red_v[q * 64 + 32 + lane] = bv[1];
+    red_i[q * 64 + 32 + lane] = bi[1];
   }
-  cp_async_wait<0>();
+  tc_fence_before();
   __syncthreads();
-
-  // CTA reduction across warps (reuses the ring)
-  float* sv = reinterpret_cast<float*>(smem);
-  int* si = reinterpret_cast<int*>(sv + LM_WARPS * MP);
-  if (g == 0) {
-#pragma unroll
-    for (int t = 0; t < MT; ++t)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        sv[warp * MP + t * 8 + 2 * c + e] = bv[t][e];
-        si[warp * MP + t * 8 + 2 * c + e] = bi[t][e];
-      }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
   }
-  __syncthreads();
-  for (int m = threadIdx.x; m < p.M; m += blockDim.x) {
+  for (int m = threadIdx.x; m < p.M; m += LT_THREADS) {
     float v = -INFINITY;
     int idx = 0x7fffffff;
-    for (int w = 0; w < LM_WARPS; ++w)
-      if (better(sv[w * MP + m], si[w * MP + m], v, idx)) { v = sv[w * MP + m]; idx = si[w * MP + m]; }
+    for (int w = 0; w < 4; ++w)
+      if (better(red_v[w * 64 + m], red_i[w * 64 + m], v, idx)) { v = red_v[w * 64 + m]; idx = red_i[w * 64 + m]; }
     p.best_val[(size_t)blockIdx.x * p.M + m] = v;
     p.best_idx[(size_t)blockIdx.x * p.M + m] = idx;
+  }
+}
+
+// E [V, H] bf16 row-major -> [ceil(V/128)][H/64][128 rows][128 B] in the
+// 128-byte swizzle (16-byte chunk j of row r stored at chunk j ^ (r % 8)).
+__global__ void lm_pack_kernel(const __nv_bfloat16* __restrict__ E, int V, int H, uint8_t* __restrict__ out) {
+  const int nkb = H / 64;
+  const int VT = (V + 127) / 128;
+  const size_t total = (size_t)VT * nkb * 128 * 8;  // 16-byte chunks
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (size_t)gridDim.x * blockDim.x) {
+    const int j = idx & 7;
+    const int r = (idx >> 3) & 127;
+    const size_t rest = idx >> 10;
+    const int kb = rest % nkb;
+    const int vt = rest / nkb;
+    const int v = vt * 128 + r;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (v < V) val = *reinterpret_cast<const uint4*>(E + (size_t)v * H + kb * 64 + j * 8);
+    *reinterpret_cast<uint4*>(out + (((size_t)vt * nkb + kb) * 128 + r) * 128 + ((j ^ (r & 7)) << 4)) = val;
   }
 }
 
@@ -249,25 +267,70 @@ __global__ void accept_kernel(const int32_t* __restrict__ draft, const int32_t* 
   correction[b] = t[a];
 }
 
-template <int MT>
-static cudaError_t lm_launch_t(const LmParams& p, int grid, cudaStream_t st) {
-  const size_t ring = (size_t)LM_NST * MT * 8 * LM_LD * 2;
-  const size_t red = (size_t)LM_WARPS * MT * 8 * 8;
-  const size_t smem = ring > red ? ring : red;
-  cudaError_t e = cudaFuncSetAttribute(lm_argmax_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)smem);
+typedef CUresult (*EncodeTiledFn3)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static bool map_rows_sw128(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
+  static EncodeTiledFn3 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    fn = reinterpret_cast<EncodeTiledFn3>(ptr);
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int lm_grid(int V, int num_sms) {
+  const int VT = (V + 127) / 128;
+  const int per = (VT + num_sms - 1) / num_sms;
+  return (VT + per - 1) / per;
+}
+
+template <int MP>
+static cudaError_t lm_tc_t(const CUtensorMap& mh, const LmParams& p, const uint8_t* et, int grid,
+                           int per, int* err, cudaStream_t st) {
+  const size_t smem = (size_t)LT_NS * (LT_E_BYTES + MP * 128) + 1024 + 256 + 8 * 64 * 4;
+  cudaError_t e = cudaFuncSetAttribute(lm_tc_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  lm_argmax_kernel<MT><<<grid, LM_WARPS * 32, smem, st>>>(p);
+  lm_tc_kernel<MP><<<grid, LT_THREADS, smem, st>>>(mh, p, et, per, err);
   return cudaGetLastError();
 }
 
-cudaError_t lm_argmax_launch(const LmParams& p, int grid, cudaStream_t st) {
-  if (p.H % 32 || p.M < 1 || p.M > 64 || p.V < 1) return cudaErrorInvalidValue;
-  const int mt = (p.M + 7) / 8;
-  if (mt == 1) return lm_launch_t<1>(p, grid, st);
-  if (mt == 2) return lm_launch_t<2>(p, grid, st);
-  if (mt <= 4) return lm_launch_t<4>(p, grid, st);
-  return lm_launch_t<8>(p, grid, st);
+// returns the grid used (partials written for that many CTAs) via *grid_out
+cudaError_t lm_argmax_launch(const LmParams& p, const uint8_t* e_tiles, int num_sms, int* err,
+                             int* grid_out, cudaStream_t st) {
+  if (p.H % 64 || p.M < 1 || p.M > 64 || p.V < 1) return cudaErrorInvalidValue;
+  const int VT = (p.V + 127) / 128;
+  const int grid = lm_grid(p.V, num_sms);
+  const int per = (VT + grid - 1) / grid;
+  *grid_out = grid;
+  const int mp = (p.M + 15) / 16 * 16;
+  CUtensorMap mh;
+  if (!map_rows_sw128(&mh, p.hn, p.H, p.M, mp)) return cudaErrorInvalidValue;
+  if (mp == 16) return lm_tc_t<16>(mh, p, e_tiles, grid, per, err, st);
+  if (mp == 32) return lm_tc_t<32>(mh, p, e_tiles, grid, per, err, st);
+  if (mp == 48) return lm_tc_t<48>(mh, p, e_tiles, grid, per, err, st);
+  return lm_tc_t<64>(mh, p, e_tiles, grid, per, err, st);
+}
+
+size_t lm_pack_bytes(int V, int H) { return (size_t)((V + 127) / 128) * 128 * H * 2; }
+
+cudaError_t lm_pack_launch(const __nv_bfloat16* E, int V, int H, uint8_t* out, cudaStream_t st) {
+  if (H % 64 || V < 1) return cudaErrorInvalidValue;
+  lm_pack_kernel<<<2048, 256, 0, st>>>(E, V, H, out);
+  return cudaGetLastError();
 }
 
 cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int M, int block,

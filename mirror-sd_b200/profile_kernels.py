@@ -1,0 +1,83 @@
+"""Run one hot-path kernel of the draft step on a named case, for timing and
+for ncu captures that stay small (each case holds < 2 GB on the device and
+streams more than the 126 MB L2 per launch).
+
+    python mirror-sd_b200/profile_kernels.py <case> [--iters N] [--warmup W]
+
+Cases (27B-class draft dims, 32 block rows):
+  w8_gu    gate|up W8A16 projection   N=34816 K=5120   (178 MB int8)
+  w8_down  down W8A16 projection      N=5120  K=17408  (89 MB)
+  w8_qkv   fused q|k|v projection     N=7168  K=5120   (37 MB)
+  lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
+  attn     block attention            40/8 heads, 32 queries, kv 4128
+  fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
+Prints the mean launch time measured with CUDA events and the achieved
+bandwidth (or TFLOP/s for fc).
+"""
+import argparse
+import importlib
+import os
+import sys
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args()
+    importlib.import_module("mirror-sd_b200")
+    K = importlib.import_module("mirror-sd_b200.kernels")
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    M = 32
+    if a.case.startswith("w8_"):
+        N, Kd = {"w8_gu": (34816, 5120), "w8_down": (5120, 17408), "w8_qkv": (7168, 5120)}[a.case]
+        q = torch.randint(-127, 128, (N, Kd), generator=g, device=dev, dtype=torch.int8)
+        s = (torch.rand(N, generator=g, device=dev) * 1e-3).to(torch.float16)
+        x = torch.randn(M, Kd, generator=g, device=dev).to(torch.float16)
+        fn = lambda: K.w8_linear(q, s, x)
+        nbytes, flops = N * Kd, 2 * M * N * Kd
+    elif a.case == "lm_head":
+        V, H = 151936, 5120
+        E = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        hn = torch.randn(1, M, H, generator=g, device=dev).to(torch.bfloat16)
+        ws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
+        fn = lambda: K.lm_head_argmax(hn, E, workspace=ws)
+        nbytes, flops = V * H * 2, 2 * (M - 1) * V * H
+    elif a.case == "attn":
+        L = 4128
+        qq = torch.randn(1, 40, M, 128, generator=g, device=dev).to(torch.float16)
+        kk = torch.randn(1, 8, L, 128, generator=g, device=dev).to(torch.float16)
+        vv = torch.randn(1, 8, L, 128, generator=g, device=dev).to(torch.float16)
+        ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+        fn = lambda: K.attention(qq, kk, vv, workspace=ws)
+        nbytes, flops = 2 * 8 * L * 128 * 2, 4 * 40 * M * L * 128
+    elif a.case == "fc":
+        Mr, Kd, N = 4096, 25600, 5120
+        A = torch.randn(Mr, Kd, generator=g, device=dev).to(torch.bfloat16)
+        B = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        fn = lambda: K.tc_gemm(A, B)
+        nbytes, flops = (Mr + N) * Kd * 2, 2 * Mr * N * Kd
+    else:
+        raise SystemExit(f"unknown case {a.case}")
+    for _ in range(a.warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / a.iters
+    print(f"{a.case}: {ms * 1e3:.1f} us/call  {nbytes / ms / 1e6:.0f} GB/s  {flops / ms / 1e9:.1f} TFLOP/s")
+
+
+if __name__ == "__main__":
+    main()

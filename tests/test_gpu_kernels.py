@@ -39,7 +39,7 @@ def test_quantizer_bit_exact_random(pkg):
     assert np.array_equal(s.cpu().numpy().view(np.uint16), sr.view(np.uint16))
 
 
-@pytest.mark.parametrize("M,N,Kd", [(1, 256, 64), (8, 512, 640), (16, 1024, 4096), (32, 768, 5120),
+@pytest.mark.parametrize("M,N,Kd", [(1, 256, 128), (8, 384, 640), (16, 1024, 4096), (32, 768, 5120),
                                     (31, 256, 17408), (64, 512, 1024)])
 def test_w8_linear_vs_fp32(K, M, N, Kd):
     g = torch.Generator().manual_seed(M * 7 + N)
