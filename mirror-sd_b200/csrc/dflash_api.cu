@@ -94,6 +94,9 @@ struct Handle {
   float* lm_val = nullptr;
   int* lm_idx = nullptr;
   int* dev_err = nullptr;
+  float* w8_part = nullptr;          // split-K partials of the W8A16 projections
+  size_t w8_part_floats = 0;
+  int* w8_cnt = nullptr;             // per-tile arrival counters (zero between launches)
   int last_launches = 0;
 };
 
@@ -272,6 +275,18 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->hn, (size_t)Mx * H));
   CKC(A.alloc(&hd->lm_val, (size_t)hd->num_sms * Mx));
   CKC(A.alloc(&hd->lm_idx, (size_t)hd->num_sms * Mx));
+  {
+    const int shapes[4][2] = {{(NQ + 2 * NKV) * 128, H}, {H, NQ * 128}, {2 * I, H}, {H, I}};
+    int max_tiles = 0;
+    for (auto& sh : shapes) {
+      const size_t f = w8tc_part_floats(sh[0], sh[1], Mx, hd->num_sms);
+      if (f > hd->w8_part_floats) hd->w8_part_floats = f;
+      if (sh[0] / 128 > max_tiles) max_tiles = sh[0] / 128;
+    }
+    CKC(A.alloc(&hd->w8_part, hd->w8_part_floats));
+    CKC(A.alloc(&hd->w8_cnt, (size_t)max_tiles));
+    CKC(cudaMemset(hd->w8_cnt, 0, (size_t)max_tiles * sizeof(int)));
+  }
   CKC(A.alloc(&hd->dev_err, 1));
   CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
   CKC(cudaDeviceSynchronize());
@@ -381,8 +396,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
     p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.kv_rows = kv_cap;
     p.kv_row0 = C;
-    p.splits = w8tc_pick_splits(p.N, p.K, hd->num_sms);
-    CK(w8tc_launch(ly.w_qkv, p, kQKV, hd->dev_err, st));
+    CK(w8tc_launch(ly.w_qkv, p, kQKV, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     // attention over [context ; block]
     AttnParams ap{};
     ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kv_cap;
@@ -395,22 +409,19 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     W8Params o{};
     o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
     o.h_out = hd->h; o.hstat_out = hd->hstat;
-    o.splits = w8tc_pick_splits(o.N, o.K, hd->num_sms);
-    CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, st));
+    CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     hparts = H / 128;
     // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
     CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xn, st));
     W8Params gu{};
     gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
     gu.x = hd->xn; gu.act = hd->act;
-    gu.splits = w8tc_pick_splits(gu.N, gu.K, hd->num_sms);
-    CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, st));
+    CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     // down + residual
     W8Params dn{};
     dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
     dn.h_out = hd->h; dn.hstat_out = hd->hstat;
-    dn.splits = w8tc_pick_splits(dn.N, dn.K, hd->num_sms);
-    CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, st));
+    CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     launches += 8;  // 2 norms, qkv, attention partial + combine, o, gate|up, down
   }
   CK(mark(5));
@@ -457,8 +468,8 @@ int dflash_quantize_q8(const float* w, int oc, int ic, int8_t* q, uint16_t* s, v
 int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uint16_t* x, int M,
                      uint16_t* y, void* stream) {
   if (!q || !s || !x || !y) return fail(DFLASH_ERR_INVALID, "NULL pointer");
-  if (N % 128 || K % 64 || K < 128 || M < 1 || M > 64)
-    return fail(DFLASH_ERR_INVALID, "need N %% 128 == 0, K %% 64 == 0, K >= 128, 1 <= M <= 64");
+  if (N % 128 || K % 128 || M < 1 || M > 64)
+    return fail(DFLASH_ERR_INVALID, "need N %% 128 == 0, K %% 128 == 0, 1 <= M <= 64");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
@@ -475,8 +486,13 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   W8Params p{};
   p.scale = sp; p.N = N; p.K = K; p.M = M;
   p.x = reinterpret_cast<const __half*>(x); p.y = reinterpret_cast<__half*>(y);
-  p.splits = w8tc_pick_splits(N, K, sms);
-  cudaError_t e = w8tc_launch(wt, p, kStore, err, st);
+  const size_t pf = w8tc_part_floats(N, K, M, sms);
+  float* part = nullptr;
+  int* cnt = nullptr;
+  CK(cudaMallocAsync(&part, (pf > 0 ? pf : 1) * sizeof(float), st));
+  CK(cudaMallocAsync(&cnt, (size_t)(N / 128) * sizeof(int), st));
+  CK(cudaMemsetAsync(cnt, 0, (size_t)(N / 128) * sizeof(int), st));
+  cudaError_t e = w8tc_launch(wt, p, kStore, err, part, pf, cnt, sms, st);
   int hv = 0;
   if (e == cudaSuccess) {
     cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
@@ -484,6 +500,8 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   }
   cudaFreeAsync(sp, st);
   cudaFreeAsync(wt, st);
+  cudaFreeAsync(part, st);
+  cudaFreeAsync(cnt, st);
   cudaFreeAsync(err, st);
   CK(e);
   if (hv) return fail(DFLASH_ERR_DEVICE, "W8A16 kernel gave up on a bounded wait (code %d)", hv);

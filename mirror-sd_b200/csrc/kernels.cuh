@@ -55,9 +55,12 @@ cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, i
                                const float* w, float eps, __half* x, cudaStream_t st);
 int w8_pick_splits(int N, int K, int M, int num_sms, int max_splits);
 // tcgen05 W8A16 path (w8_tc.cu): w_tiles is the int8 weight packed by
-// w8_tilepack_launch ([N/128][K/64][128][64 B])
-int w8tc_pick_splits(int N, int K, int num_sms);
-cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int* err, cudaStream_t st);
+// w8_tilepack_launch ([N/128][K/64][128][64 B]); part / counters are the
+// split-K scratch (w8tc_part_floats floats; counters zero, one per tile).
+void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups);
+size_t w8tc_part_floats(int N, int K, int M, int num_sms);
+cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int* err, float* part,
+                        size_t part_floats, int* counters, int num_sms, cudaStream_t st);
 cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst, int grp, int gstride,
                                int base, cudaStream_t st);
 size_t w8_smem_bytes(const W8Params& p);
