@@ -162,6 +162,34 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
                      const float* k_norm, float rope_theta, int q_pos0, int k_pos0, float eps,
                      uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same attention without any device allocation and without a caller
+ * workspace.  It has no counterpart in the reference.  It is for callers that
+ * cannot call cudaMalloc: a host runtime that has reserved the device's memory
+ * up front for its own pool and forbids side allocations, or a binding that
+ * has no way to pass a workspace buffer.
+ *
+ * Scratch: the split-KV partials and the RoPE table live in one static device
+ * array of DFLASH_ATTN_STATIC_SCRATCH_BYTES.  Every GPU that loads this library
+ * holds that array until the process exits.  A shape whose
+ * dflash_attention_workspace_size() exceeds the array is rejected with
+ * DFLASH_ERR_INVALID.
+ *
+ * First call per device: it looks up the array's device address, once per
+ * device, while that device is current.  Make that first call outside any
+ * stream capture.
+ *
+ * Sharing: all calls on a device share the one array, and it keeps whatever
+ * the last call left in it.  Every byte a call reads is written earlier in
+ * that call, so nothing needs clearing.  Two calls whose kernels overlap on
+ * the GPU (different streams, no ordering between them) race on the array.
+ * Serialise them on one stream, or use dflash_attention with separate
+ * workspaces. */
+#define DFLASH_ATTN_STATIC_SCRATCH_BYTES ((size_t)16 << 20)
+int dflash_attention_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v, int batch,
+                             int nq, int nkv, int block, int kv_len, int normrope,
+                             const float* q_norm, const float* k_norm, float rope_theta,
+                             int q_pos0, int k_pos0, float eps, uint16_t* out, void* stream);
+
 /* Tied lm_head + greedy argmax (+ acceptance when target != NULL) on
  * final-normed hidden rows: hn [batch, block, H] bf16, E [V, H] bf16; writes
  * tokens [batch, block-1] for rows 1..block-1 (generate.py:604-606, :722-728).

@@ -79,6 +79,10 @@ EXPORTS = {
                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                    c_void_p, c_void_p, c_float, ctypes.c_int, ctypes.c_int,
                                    c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "dflash_attention_noalloc": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_int,
+                                           ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                           ctypes.c_int, c_void_p, c_void_p, c_float, ctypes.c_int,
+                                           ctypes.c_int, c_float, c_void_p, c_void_p]),
     "dflash_lm_head_workspace_size": (c_size_t, [ctypes.c_int, ctypes.c_int]),
     "dflash_lm_head_argmax": (c_int32, [c_void_p, c_void_p, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, c_void_p, c_void_p, c_void_p,

@@ -637,3 +637,62 @@ int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int 
 }
 
 }  // extern "C"
+
+// ---- attention over a static scratch array -------------------------------
+//
+// dflash_attention_noalloc serves callers that cannot call cudaMalloc: a host
+// runtime that has reserved the device's memory for its own pool, or a binding
+// that cannot pass a workspace buffer.  It runs the same kernels as
+// dflash_attention.  Its workspace is the array below: fixed size, one per
+// device that loads the library, held until the process exits.
+//
+// `g_attn_scratch` is a host-side stand-in for the array.  The device address
+// comes from cudaGetSymbolAddress, looked up on a device's first call while
+// that device is current.  Calls on a device share the array, so calls that
+// overlap on the GPU race.  The array keeps the last call's contents.  The
+// partial kernel writes every (split, row) partial and the table rows it reads
+// before anything reads them, so nothing needs clearing between calls.
+
+static __device__ __align__(256) unsigned char g_attn_scratch[DFLASH_ATTN_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kScratchMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_dev[kScratchMaxDevices] = {};
+
+// device address of g_attn_scratch on the current device, looked up once
+int attn_scratch_ptr(void** out) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kScratchMaxDevices)
+    return fail(DFLASH_ERR_INVALID, "device ordinal %d beyond the %d supported", dev,
+                kScratchMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_dev[dev]) {
+    void* p = nullptr;
+    CK(cudaGetSymbolAddress(&p, g_attn_scratch));
+    g_scratch_dev[dev] = p;
+  }
+  *out = g_scratch_dev[dev];
+  return DFLASH_OK;
+}
+}  // namespace
+
+extern "C" int dflash_attention_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                        int batch, int nq, int nkv, int block, int kv_len,
+                                        int normrope, const float* q_norm, const float* k_norm,
+                                        float rope_theta, int q_pos0, int k_pos0, float eps,
+                                        uint16_t* out, void* stream) {
+  const size_t need = dflash_attention_workspace_size(batch, nq, nkv, block, kv_len);
+  if (need > DFLASH_ATTN_STATIC_SCRATCH_BYTES)
+    return fail(DFLASH_ERR_INVALID,
+                "dflash_attention_noalloc: this shape needs %zu bytes of scratch, more than the "
+                "%zu-byte static array; use dflash_attention with a caller workspace",
+                need, (size_t)DFLASH_ATTN_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = attn_scratch_ptr(&scratch);
+  if (rc != DFLASH_OK) return rc;
+  return dflash_attention(q, k, v, batch, nq, nkv, block, kv_len, normrope, q_norm, k_norm,
+                          rope_theta, q_pos0, k_pos0, eps, out, scratch,
+                          DFLASH_ATTN_STATIC_SCRATCH_BYTES, stream);
+}
