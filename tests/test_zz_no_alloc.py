@@ -41,7 +41,7 @@ def _inputs(seed, b, nq, nkv, B, L):
 def test_noalloc_matches_workspace_entry_on_consecutive_calls(pkg):
     import importlib
     K = importlib.import_module("mirror-sd_b200.kernels")
-    # call 1: the 27B attention shape (32/8 heads, block 32, ctx 4096), raw Q/K with
+    # call 1: 32 query / 8 kv heads, block 32, ctx 4096, raw Q/K with
     # the fused per-head RMSNorm + RoPE; call 2: a smaller ragged shape, plain Q/K
     q1, k1, v1, qn1, kn1 = _inputs(1, 1, 32, 8, 32, 4096 + 32)
     q2, k2, v2, _, _ = _inputs(2, 2, 8, 2, 16, 300)
