@@ -29,6 +29,11 @@
  *   dflash_accept    the longest-prefix acceptance loop (generate.py:722-728)
  *   dflash_quantize_q8  ANEDraftModel._quantize_weight_q8 (ane_model.py:265-279)
  *   dflash_destroy   drop of the native kernels / buffers (wrapper.rs)
+ *   dflash_cache_*   DFlashKVCache and DFlashDraftModel.make_cache
+ *                    (mirror_sd/dflash.py:139-212, :405-406): the append with
+ *                    sink + window eviction happens inside dflash_forward
+ *                    (update_and_fetch, dflash.py:168-193); trim / offset /
+ *                    keys are the cache object's own methods
  */
 #ifndef DFLASH_B200_H
 #define DFLASH_B200_H
@@ -91,17 +96,24 @@ typedef struct DFlashWeightsView {
   const DFlashLayerWeights* layers; /* HOST array of num_hidden_layers entries */
 } DFlashWeightsView;
 
-/* One stateless draft step (cache=None in dflash.py): RoPE positions are
- * rope_offset + row for the ctx_len context rows and rope_offset + ctx_len + j
- * for the block rows (dflash.py:299-305). */
+/* One draft step.  Sequence s brings C_s new context rows (ctx_lens[s], or
+ * ctx_len for every sequence when ctx_lens is NULL) and `block` noise rows.
+ * Without a cache (cache=None in dflash.py) the step attends to exactly those
+ * C_s + block rows, at RoPE positions off_s + row (rope_offsets[s], or
+ * rope_offset), and keeps nothing.  With a cache (dflash_cache_create) the new
+ * rows are appended to sequence s of the cache at positions offset_s + row,
+ * sink + window eviction is applied, and the step attends to everything the
+ * cache then holds (dflash.py:287-317); afterwards the caller trims the block
+ * rows with dflash_cache_trim, as generate.py:608-609 does. */
 typedef struct DFlashForwardArgs {
   int32_t batch;
   int32_t block;          /* block_size, 2..max_block, batch*block <= 64 */
-  int32_t ctx_len;        /* context rows per sequence, 0..max_ctx */
-  int32_t rope_offset;
+  int32_t ctx_len;        /* context rows per sequence, 0..max_ctx (when ctx_lens is NULL) */
+  int32_t rope_offset;    /* without a cache: position of row 0 (when rope_offsets is NULL) */
   int32_t num_layers;     /* 1..num_hidden_layers (DFlashDraftModel.num_draft_layers) */
   const uint16_t* noise;          /* bf16 [batch, block, H] */
-  const uint16_t* target_hidden;  /* bf16 [batch, ctx_len, F*H] */
+  const uint16_t* target_hidden;  /* bf16 context rows of all sequences packed in order:
+                                     [sum_s C_s, F*H] ([batch, ctx_len, F*H] when uniform) */
   void* out_hidden;               /* [batch, block, H] final-normed hidden states, or NULL:
                                      bf16, or fp32 when out_hidden_fp32 != 0 */
   int32_t out_hidden_fp32;
@@ -116,6 +128,9 @@ typedef struct DFlashForwardArgs {
    * layers, 6 after the final norm, 7 after lm_head + argmax (+ accept). */
   void* const* phase_events;
   int32_t n_phase_events;
+  const int32_t* ctx_lens;        /* HOST array [batch] of C_s, or NULL */
+  const int32_t* rope_offsets;    /* HOST array [batch], or NULL; not used with a cache */
+  void* cache;                    /* from dflash_cache_create, or NULL (cache=None) */
 } DFlashForwardArgs;
 
 #define DFLASH_PHASES 8
@@ -135,6 +150,31 @@ int dflash_destroy(void* handle);
 int dflash_last_launch_count(void* handle);
 int dflash_last_error(char* buf, size_t len);
 int dflash_version(void);
+
+/* ---- draft KV cache (dflash.py:139-212) ---------------------------------
+ * K/V rows of every layer and sequence stay on the device in
+ * [layer][sequence][kv head][slot][128] f16 rings.  Eviction of the middle rows
+ * moves a ring start, trim shortens the list: no row is ever copied.  Eviction
+ * is on when sink_size > 0 and window_size > 0 (dflash.py:180-181); the cache
+ * then holds sink_size + window_size + max_ctx + max_block slots per sequence.
+ * Without eviction it holds max_len slots and a step that would overflow them
+ * is rejected.  Offsets and lengths are host-side state: the cache ops below
+ * enqueue no device work (dflash_cache_read excepted). */
+int dflash_cache_create(void* handle, int num_layers, int max_batch, int sink_size, int window_size,
+                        int max_len, void** cache);
+/* DFlashKVCache.trim(n) (dflash.py:195-207) on one layer, or on every layer
+ * when layer < 0, for every sequence: length -> max(length - n, 0),
+ * offset -> offset - n.  n <= 0 does nothing. */
+int dflash_cache_trim(void* cache, int layer, int n);
+/* Empty every sequence (offset 0).  Device contents are not touched. */
+int dflash_cache_reset(void* cache);
+/* DFlashKVCache.offset and keys.shape[2] of one layer and sequence. */
+int dflash_cache_state(void* cache, int layer, int seq, int32_t* offset, int32_t* length);
+/* DFlashKVCache.keys / .values of one layer and sequence, in logical order, as
+ * f16 [NKV, length, 128] into caller buffers (either may be NULL). */
+int dflash_cache_read(void* cache, int layer, int seq, uint16_t* keys, uint16_t* values,
+                      void* stream);
+int dflash_cache_destroy(void* cache);
 
 /* ---- kernel-level entry points (one hot-path kernel each) ---------------- */
 

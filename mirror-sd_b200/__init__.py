@@ -5,10 +5,10 @@ carries a hyphen).  The compute path is the CUDA library ``lib/libdflash_b200.so
 (C ABI: ``include/dflash_b200.h``), built by ``build.py``.
 """
 from . import _native
-from .dflash import (DFlashConfig, DFlashDraftModel, DFlashKVCache, DFlashWeightsQ8, Q8Layer,
+from .dflash import (DFlashCache, DFlashConfig, DFlashDraftModel, DFlashKVCache, DFlashWeightsQ8, Q8Layer,
                      accept, build_target_layer_ids, extract_context_feature, quantize_q8, sample)
 from .weights import synth_weights_q8, weights_from_q8_numpy
 
-__all__ = ["DFlashConfig", "DFlashDraftModel", "DFlashKVCache", "DFlashWeightsQ8", "Q8Layer",
+__all__ = ["DFlashCache", "DFlashConfig", "DFlashDraftModel", "DFlashKVCache", "DFlashWeightsQ8", "Q8Layer",
            "accept", "build_target_layer_ids", "extract_context_feature", "quantize_q8", "sample",
            "synth_weights_q8", "weights_from_q8_numpy"]

@@ -49,7 +49,9 @@ class DFlashForwardArgs(ctypes.Structure):
                 ("noise", c_void_p), ("target_hidden", c_void_p), ("out_hidden", c_void_p),
                 ("out_hidden_fp32", c_int32), ("out_tokens", c_void_p), ("target_tokens", c_void_p),
                 ("acc_len", c_void_p), ("correction", c_void_p),
-                ("phase_events", ctypes.POINTER(c_void_p)), ("n_phase_events", c_int32)]
+                ("phase_events", ctypes.POINTER(c_void_p)), ("n_phase_events", c_int32),
+                ("ctx_lens", ctypes.POINTER(c_int32)), ("rope_offsets", ctypes.POINTER(c_int32)),
+                ("cache", c_void_p)]
 
 
 DFLASH_PHASES = 8
@@ -66,6 +68,15 @@ EXPORTS = {
     "dflash_quantize_q8": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, c_void_p, c_void_p,
                                      c_void_p]),
     "dflash_device_status": (c_int32, [c_void_p, c_void_p]),
+    "dflash_cache_create": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, ctypes.POINTER(c_void_p)]),
+    "dflash_cache_trim": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int]),
+    "dflash_cache_reset": (c_int32, [c_void_p]),
+    "dflash_cache_state": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(c_int32),
+                                     ctypes.POINTER(c_int32)]),
+    "dflash_cache_read": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, c_void_p, c_void_p,
+                                    c_void_p]),
+    "dflash_cache_destroy": (c_int32, [c_void_p]),
     "dflash_destroy": (c_int32, [c_void_p]),
     "dflash_last_launch_count": (c_int32, [c_void_p]),
     "dflash_last_error": (c_int32, [ctypes.c_char_p, c_size_t]),

@@ -12,6 +12,10 @@
 // RoPE of dflash.py:291-305 to the raw Q and K rows as they land in shared
 // memory (the attention-only configuration); in the draft forward both are
 // already applied by the projection epilogues.
+//
+// In the draft forward K/V rows are read through the KvMap of kernels.cuh:
+// each sequence attends to its own logical rows [0, n_att), wherever the
+// cache ring holds them.
 #include "kernels.cuh"
 
 namespace dfl {
@@ -60,9 +64,13 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
   __half* ks = qs + (size_t)RP * AT_LD;               // [2][TK][LD]
   __half* vs = ks + (size_t)2 * AT_TK * AT_LD;        // [2][TK][LD]
 
+  // logical kv rows of this sequence; with a KvMap they sit at ring slots
+  const bool mapped = p.kv.nseq > 0;
+  const int kv_len = mapped ? p.kv.n_att[bi] : p.kv_len;
+  const int rs = mapped ? p.kv.rs_post[bi] : 0;
   const int kv0 = split * p.chunk;
-  const int kv1 = min(p.kv_len, kv0 + p.chunk);
-  const int ntiles = (kv1 - kv0 + AT_TK - 1) / AT_TK;
+  const int kv1 = min(kv_len, kv0 + p.chunk);
+  const int ntiles = kv1 > kv0 ? (kv1 - kv0 + AT_TK - 1) / AT_TK : 0;
 
   const __half* qg = p.q + ((size_t)bi * p.nq + (size_t)kvh * G) * p.block * 128;
   const __half* kg = p.k + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
@@ -80,7 +88,8 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
       const int r = idx >> 4, cc = (idx & 15) * 8;
       const int row = base + r;
       const bool ok = row < kv1;
-      const size_t off = (size_t)min(row, p.kv_len - 1) * 128 + cc;
+      const int lrow = ok ? row : 0;  // a valid address even when nothing is read
+      const size_t off = (size_t)(mapped ? kv_slot(p.kv, lrow, rs) : lrow) * 128 + cc;
       cp_async16_zfill(smem_u32(ks + ((size_t)buf * AT_TK + r) * AT_LD + cc), kg + off, ok);
       cp_async16_zfill(smem_u32(vs + ((size_t)buf * AT_TK + r) * AT_LD + cc), vg + off, ok);
     }

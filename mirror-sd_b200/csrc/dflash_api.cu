@@ -1,5 +1,6 @@
 // C ABI (include/dflash_b200.h): handle with device-resident weights and
 // workspace, the stateless draft step, and the kernel-level entry points.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -98,6 +99,33 @@ struct Handle {
   size_t w8_part_floats = 0;
   int* w8_cnt = nullptr;             // per-tile arrival counters (zero between launches)
   int last_launches = 0;
+};
+
+// Draft KV cache (dflash.py:139-212).  Per layer and sequence the host keeps
+// the logical state; the device holds the rows in the KvMap ring layout of
+// kernels.cuh ([layer][sequence][kv head][slot][128] f16).
+struct SeqState {
+  int offset = 0;  // positions processed (RoPE offset), dflash.py:172
+  int hl = 0;      // rows in the sink slots
+  int rs = 0;      // ring start
+  int rl = 0;      // rows in the ring
+  bool operator==(const SeqState& o) const {
+    return offset == o.offset && hl == o.hl && rs == o.rs && rl == o.rl;
+  }
+};
+
+struct Cache {
+  const Handle* owner = nullptr;    // compared, never dereferenced: the cache may outlive it
+  int device = 0, nkv = 0;
+  std::mutex mu;                    // host state; dflash_forward takes it after the handle's
+  int layers = 0, max_batch = 0;
+  int sink_size = 0, window_size = 0;
+  bool evict = false;               // sink_size > 0 && window_size > 0 (dflash.py:180-181)
+  int sink = 0, ring = 0, slots = 0;
+  __half *K = nullptr, *V = nullptr;
+  size_t layer_stride = 0;          // halves
+  std::vector<SeqState> st;         // [layers][max_batch]
+  SeqState& at(int l, int s) { return st[(size_t)l * max_batch + s]; }
 };
 
 int check_dims(const DFlashDims* d) {
@@ -253,7 +281,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   const int Cx = d.max_batch * d.max_ctx;
   const int kvcap = d.max_ctx + d.max_block;
   const int G = NQ / NKV;
-  CKC(A.alloc(&hd->rope, (size_t)kvcap * 64));
+  CKC(A.alloc(&hd->rope, (size_t)(Cx + Mx) * 64));
   CKC(A.alloc(&hd->h, (size_t)Mx * H));
   CKC(A.alloc(&hd->hstat, (size_t)(H / 128) * Mx));
   if (Cx > 0) {
@@ -268,7 +296,9 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->attn_out, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->act, (size_t)Mx * I));
   CKC(A.alloc(&hd->xn, (size_t)Mx * H));
-  hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, kvcap, hd->num_sms);
+  // the split count never exceeds what the longest rows give, and a cache can
+  // make rows longer than max_ctx + max_block: size for any length
+  hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, 1 << 28, hd->num_sms);
   CKC(A.alloc(&hd->opart, hd->attn_part_rows * 128));
   CKC(A.alloc(&hd->mpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->lpart, hd->attn_part_rows));
@@ -326,24 +356,95 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   const DFlashDims& d = hd->d;
   const int H = d.hidden_size, I = d.intermediate_size, NQ = d.num_attention_heads,
             NKV = d.num_key_value_heads, F = d.num_target_features;
-  const int b = a->batch, B = a->block, C = a->ctx_len, nl = a->num_layers;
+  const int b = a->batch, B = a->block, nl = a->num_layers;
   if (b < 1 || b > d.max_batch) return fail(DFLASH_ERR_INVALID, "batch %d outside [1, %d]", b, d.max_batch);
   if (B < 2 || B > d.max_block) return fail(DFLASH_ERR_INVALID, "block %d outside [2, %d]", B, d.max_block);
-  if (C < 0 || C > d.max_ctx) return fail(DFLASH_ERR_INVALID, "ctx_len %d outside [0, %d]", C, d.max_ctx);
   if (nl < 1 || nl > d.num_hidden_layers)
     return fail(DFLASH_ERR_INVALID, "num_layers %d outside [1, %d]", nl, d.num_hidden_layers);
-  if (a->rope_offset < 0) return fail(DFLASH_ERR_INVALID, "rope_offset must be >= 0");
-  if (!a->noise || (C > 0 && !a->target_hidden))
+  if (b > kKvMaxSeq) return fail(DFLASH_ERR_INVALID, "batch %d above %d", b, kKvMaxSeq);
+  // per-sequence context rows, packed in sequence order
+  KvMap m{};
+  m.nseq = b;
+  int cmax = 0;
+  for (int s = 0; s < b; ++s) {
+    const int c = a->ctx_lens ? a->ctx_lens[s] : a->ctx_len;
+    if (c < 0 || c > d.max_ctx)
+      return fail(DFLASH_ERR_INVALID, "ctx_len %d of sequence %d outside [0, %d]", c, s, d.max_ctx);
+    m.ctx_start[s + 1] = m.ctx_start[s] + c;
+    cmax = std::max(cmax, c);
+  }
+  const int Ctot = m.ctx_start[b];
+  if (!a->noise || (Ctot > 0 && !a->target_hidden))
     return fail(DFLASH_ERR_INVALID, "noise / target_hidden must not be NULL");
   if (a->target_tokens && (!a->acc_len || !a->correction))
     return fail(DFLASH_ERR_INVALID, "acc_len and correction are required with target_tokens");
+  Cache* cc = static_cast<Cache*>(a->cache);
+  if (cc && cc->owner != hd) return fail(DFLASH_ERR_INVALID, "the cache belongs to another handle");
+  if (cc && b > cc->max_batch)
+    return fail(DFLASH_ERR_INVALID, "batch %d above the cache's %d sequences", b, cc->max_batch);
+  if (cc && nl != cc->layers)
+    return fail(DFLASH_ERR_INVALID, "num_layers %d differs from the cache's %d layers", nl, cc->layers);
   std::lock_guard<std::mutex> lock(hd->mu);
+  std::unique_lock<std::mutex> cache_lock;
+  if (cc) cache_lock = std::unique_lock<std::mutex>(cc->mu);
+
+  // where this step's K/V rows go and which rows attention reads
+  __half *Kbase, *Vbase;
+  size_t layer_stride;
+  std::vector<SeqState> next;
+  if (cc) {
+    // update_and_fetch (dflash.py:168-193): append C_s + B rows, then keep
+    // the sink and the last window rows when the list outgrows them
+    m.sink = cc->sink; m.ring = cc->ring; m.slots = cc->slots;
+    next.resize(b);
+    for (int s = 0; s < b; ++s) {
+      const SeqState s0 = cc->at(0, s);
+      for (int l = 1; l < nl; ++l)
+        if (!(cc->at(l, s) == s0))
+          return fail(DFLASH_ERR_INVALID,
+                      "cache layers hold different rows for sequence %d (trim every layer alike)", s);
+      const int app = m.ctx_start[s + 1] - m.ctx_start[s] + B;
+      const int to_sink = s0.hl < cc->sink ? std::min(app, cc->sink - s0.hl) : 0;
+      SeqState n1 = s0;
+      n1.hl = s0.hl + to_sink;
+      n1.rl = s0.rl + app - to_sink;
+      if (n1.rl > cc->ring)
+        return fail(DFLASH_ERR_INVALID, "cache full: sequence %d would hold %d rows, capacity %d", s,
+                    n1.hl + n1.rl, cc->slots);
+      if (cc->evict && n1.hl + n1.rl > cc->sink_size + cc->window_size) {
+        n1.rs = (s0.rs + n1.rl - cc->window_size) % cc->ring;
+        n1.rl = cc->window_size;
+      }
+      n1.offset = s0.offset + app;
+      m.n0[s] = s0.hl + s0.rl;
+      m.rs_pre[s] = s0.rs;
+      m.rs_post[s] = n1.rs;
+      m.n_att[s] = n1.hl + n1.rl;
+      m.pos0[s] = s0.offset;
+      next[s] = n1;
+    }
+    Kbase = cc->K; Vbase = cc->V;
+    layer_stride = cc->layer_stride;
+  } else {
+    // cache=None: the step's own C_s + B rows, nothing kept
+    m.sink = 0; m.ring = m.slots = cmax + B;
+    for (int s = 0; s < b; ++s) {
+      const int off = a->rope_offsets ? a->rope_offsets[s] : a->rope_offset;
+      if (off < 0) return fail(DFLASH_ERR_INVALID, "rope offsets must be >= 0");
+      m.n0[s] = 0; m.rs_pre[s] = 0; m.rs_post[s] = 0;
+      m.n_att[s] = m.ctx_start[s + 1] - m.ctx_start[s] + B;
+      m.pos0[s] = off;
+    }
+    Kbase = hd->K; Vbase = hd->V;
+    layer_stride = (size_t)b * NKV * m.slots * 128;
+  }
+  int kvmax = 0;
+  for (int s = 0; s < b; ++s) kvmax = std::max(kvmax, m.n_att[s]);
+
   CK(cudaSetDevice(hd->device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int M = b * B;
-  const int kv_cap = C + B;
   const int G = NQ / NKV;
-  const size_t layer_stride = (size_t)b * NKV * kv_cap * 128;
   const bool timing = a->phase_events && a->n_phase_events >= DFLASH_PHASES;
   auto mark = [&](int k) -> cudaError_t {
     return timing ? cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[k]), st) : cudaSuccess;
@@ -351,25 +452,25 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   int launches = 0;
 
   CK(mark(0));
-  CK(rope_table_launch(a->rope_offset, kv_cap, hd->inv_freq, hd->rope, st));
+  CK(rope_table_map_launch(m, B, hd->inv_freq, hd->rope, st));
   CK(init_h_launch(reinterpret_cast<const __nv_bfloat16*>(a->noise), M, H, hd->h, hd->hstat, st));
   launches += 2;
   CK(mark(1));
 
-  if (C > 0) {
+  if (Ctot > 0) {
     TcParams fp{};
-    fp.M = b * C; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
+    fp.M = Ctot; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
     fp.out_f32 = hd->ctx_raw; fp.sumsq_part = hd->ctx_part;
     CK(tc_gemm_launch(a->target_hidden, hd->fc, true, kTcFc, fp, st));
     CK(mark(2));
-    CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, b * C, H, hd->hidden_norm, d.rms_norm_eps,
+    CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, Ctot, H, hd->hidden_norm, d.rms_norm_eps,
                        hd->ctx_n, st));
     CK(mark(3));
     TcParams kp{};
-    kp.M = b * C; kp.N = nl * 2 * NKV * 128; kp.K = H; kp.err = hd->dev_err;
+    kp.M = Ctot; kp.N = nl * 2 * NKV * 128; kp.K = H; kp.err = hd->dev_err;
     kp.scale = hd->s_kv_ctx; kp.k_norm = hd->k_norm_all; kp.rope = hd->rope;
-    kp.k_out = hd->K; kp.v_out = hd->V; kp.layer_stride = layer_stride;
-    kp.nkv = NKV; kp.rows_per_seq = C; kp.kv_cap = kv_cap; kp.kv_row0 = 0; kp.eps = d.rms_norm_eps;
+    kp.k_out = Kbase; kp.v_out = Vbase; kp.layer_stride = layer_stride;
+    kp.nkv = NKV; kp.eps = d.rms_norm_eps; kp.kv = m;
     CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, false, kTcCtxKV, kp, st));
     CK(mark(4));
     launches += 3;
@@ -380,30 +481,31 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   }
 
   int chunk, splits;
-  attn_pick_split(b, NKV, kv_cap, hd->num_sms, &chunk, &splits);
+  attn_pick_split(b, NKV, kvmax, hd->num_sms, &chunk, &splits);
   if ((size_t)b * NKV * splits * G * B > hd->attn_part_rows)
     return fail(DFLASH_ERR_INVALID, "attention workspace too small");
   int hparts = 1;
   for (int l = 0; l < nl; ++l) {
     const Layer& ly = hd->layers[l];
-    __half* Kl = hd->K + l * layer_stride;
-    __half* Vl = hd->V + l * layer_stride;
+    __half* Kl = Kbase + l * layer_stride;
+    __half* Vl = Vbase + l * layer_stride;
     // q | k | v of the block rows: input RMSNorm fused into the activation load
     CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xn, st));
     W8Params p{};
     p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
     p.x = hd->xn; p.eps = d.rms_norm_eps;
     p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
-    p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.kv_rows = kv_cap;
-    p.kv_row0 = C;
+    p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.rope_blk0 = Ctot;
+    p.kv = m;
     CK(w8tc_launch(ly.w_qkv, p, kQKV, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
-    // attention over [context ; block]
+    // attention over each sequence's stored rows
     AttnParams ap{};
-    ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kv_cap;
-    ap.kv_cap = kv_cap; ap.chunk = chunk; ap.splits = splits; ap.opart = hd->opart;
+    ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kvmax;
+    ap.kv_cap = m.slots; ap.chunk = chunk; ap.splits = splits; ap.opart = hd->opart;
     ap.mpart = hd->mpart; ap.lpart = hd->lpart;
     ap.scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
     ap.normrope = 0;
+    ap.kv = m;
     CK(attn_launch(ap, b, hd->attn_out, st));
     // o_proj + residual
     W8Params o{};
@@ -440,7 +542,141 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     launches += 2;
   }
   CK(mark(7));
+  if (cc)
+    for (int l = 0; l < nl; ++l)
+      for (int s = 0; s < b; ++s) cc->at(l, s) = next[s];
   hd->last_launches = launches;
+  return DFLASH_OK;
+}
+
+// ---------------------------------------------------------------- KV cache
+int dflash_cache_create(void* handle, int num_layers, int max_batch, int sink_size, int window_size,
+                        int max_len, void** out) {
+  if (!handle || !out) return fail(DFLASH_ERR_INVALID, "NULL handle or output");
+  Handle* hd = static_cast<Handle*>(handle);
+  const DFlashDims& d = hd->d;
+  if (num_layers < 1 || num_layers > d.num_hidden_layers)
+    return fail(DFLASH_ERR_INVALID, "num_layers %d outside [1, %d]", num_layers, d.num_hidden_layers);
+  if (max_batch < 1 || max_batch > d.max_batch)
+    return fail(DFLASH_ERR_INVALID, "max_batch %d outside [1, %d]", max_batch, d.max_batch);
+  Cache* c = new Cache();
+  c->owner = hd;
+  c->device = hd->device;
+  c->nkv = d.num_key_value_heads;
+  c->layers = num_layers;
+  c->max_batch = max_batch;
+  c->sink_size = sink_size;
+  c->window_size = window_size;
+  c->evict = sink_size > 0 && window_size > 0;
+  if (c->evict) {
+    // before eviction a step holds at most window + (max_ctx + max_block) ring rows
+    c->sink = sink_size;
+    c->ring = window_size + d.max_ctx + d.max_block;
+  } else {
+    if (max_len < 1) {
+      delete c;
+      return fail(DFLASH_ERR_INVALID, "a cache without eviction needs max_len >= 1 (got %d)", max_len);
+    }
+    c->sink = 0;
+    c->ring = max_len;
+  }
+  c->slots = c->sink + c->ring;
+  c->layer_stride = (size_t)max_batch * d.num_key_value_heads * c->slots * 128;
+  c->st.assign((size_t)num_layers * max_batch, SeqState{});
+  const size_t elems = c->layer_stride * num_layers;
+  cudaError_t e = cudaSetDevice(hd->device);
+  if (e == cudaSuccess) e = cudaMalloc(&c->K, elems * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&c->V, elems * 2);
+  if (e != cudaSuccess) {
+    if (c->K) cudaFree(c->K);
+    delete c;
+    return fail(e == cudaErrorMemoryAllocation ? DFLASH_ERR_OOM : DFLASH_ERR_CUDA,
+                "cache allocation of 2 x %zu bytes: %s", elems * 2, cudaGetErrorString(e));
+  }
+  *out = c;
+  return DFLASH_OK;
+}
+
+int dflash_cache_trim(void* cache, int layer, int n) {
+  if (!cache) return fail(DFLASH_ERR_INVALID, "NULL cache");
+  Cache* c = static_cast<Cache*>(cache);
+  if (layer >= c->layers) return fail(DFLASH_ERR_INVALID, "layer %d outside [0, %d)", layer, c->layers);
+  if (n <= 0) return DFLASH_OK;
+  std::lock_guard<std::mutex> lock(c->mu);
+  const int l0 = layer < 0 ? 0 : layer, l1 = layer < 0 ? c->layers : layer + 1;
+  for (int l = l0; l < l1; ++l)
+    for (int s = 0; s < c->max_batch; ++s) {
+      SeqState& q = c->at(l, s);
+      const int len = std::max(q.hl + q.rl - n, 0);  // dflash.py:204
+      if (len >= q.hl) {
+        q.rl = len - q.hl;
+      } else {
+        q.rl = 0;
+        q.hl = len;
+      }
+      q.offset -= n;                                 // dflash.py:207
+    }
+  return DFLASH_OK;
+}
+
+int dflash_cache_reset(void* cache) {
+  if (!cache) return fail(DFLASH_ERR_INVALID, "NULL cache");
+  Cache* c = static_cast<Cache*>(cache);
+  std::lock_guard<std::mutex> lock(c->mu);
+  for (auto& q : c->st) q = SeqState{};
+  return DFLASH_OK;
+}
+
+int dflash_cache_state(void* cache, int layer, int seq, int32_t* offset, int32_t* length) {
+  if (!cache) return fail(DFLASH_ERR_INVALID, "NULL cache");
+  Cache* c = static_cast<Cache*>(cache);
+  if (layer < 0 || layer >= c->layers || seq < 0 || seq >= c->max_batch)
+    return fail(DFLASH_ERR_INVALID, "layer %d / sequence %d out of range", layer, seq);
+  std::lock_guard<std::mutex> lock(c->mu);
+  const SeqState& q = c->at(layer, seq);
+  if (offset) *offset = q.offset;
+  if (length) *length = q.hl + q.rl;
+  return DFLASH_OK;
+}
+
+int dflash_cache_read(void* cache, int layer, int seq, uint16_t* keys, uint16_t* values, void* stream) {
+  if (!cache) return fail(DFLASH_ERR_INVALID, "NULL cache");
+  Cache* c = static_cast<Cache*>(cache);
+  if (layer < 0 || layer >= c->layers || seq < 0 || seq >= c->max_batch)
+    return fail(DFLASH_ERR_INVALID, "layer %d / sequence %d out of range", layer, seq);
+  std::lock_guard<std::mutex> lock(c->mu);
+  const SeqState q = c->at(layer, seq);
+  const int NKV = c->nkv;
+  const int len = q.hl + q.rl;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CK(cudaSetDevice(c->device));
+  // logical rows: sink slots [0, hl), then ring rows from rs (wrapping once)
+  const int first = std::min(q.rl, c->ring - q.rs);
+  const struct { int dst, src, n; } runs[3] = {
+      {0, 0, q.hl}, {q.hl, c->sink + q.rs, first}, {q.hl + first, c->sink, q.rl - first}};
+  for (int which = 0; which < 2; ++which) {
+    uint16_t* dst = which ? values : keys;
+    if (!dst) continue;
+    const __half* base = (which ? c->V : c->K) + layer * c->layer_stride +
+                         (size_t)seq * NKV * c->slots * 128;
+    for (int h = 0; h < NKV; ++h)
+      for (const auto& r : runs)
+        if (r.n > 0)
+          CK(cudaMemcpyAsync(dst + ((size_t)h * len + r.dst) * 128,
+                             base + ((size_t)h * c->slots + r.src) * 128, (size_t)r.n * 128 * 2,
+                             cudaMemcpyDeviceToDevice, st));
+  }
+  return DFLASH_OK;
+}
+
+int dflash_cache_destroy(void* cache) {
+  if (!cache) return fail(DFLASH_ERR_INVALID, "NULL cache");
+  Cache* c = static_cast<Cache*>(cache);
+  cudaSetDevice(c->device);
+  cudaDeviceSynchronize();
+  cudaFree(c->K);
+  cudaFree(c->V);
+  delete c;
   return DFLASH_OK;
 }
 

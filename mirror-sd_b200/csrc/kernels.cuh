@@ -1,14 +1,91 @@
 // Host/device parameter blocks and host launch functions of every kernel.
 #pragma once
-#include "w8_gemm.cuh"
+#include "common.cuh"
 
 namespace dfl {
 
+// ---- where K/V rows live ----------------------------------------------------
+//
+// Every K/V store is [layer][sequence][kv head][slots][128] f16.  A sequence's
+// stored rows form the logical list of the reference cache
+// (dflash.py:139-212): the first `sink` logical rows sit in slots [0, sink);
+// the rest live in a ring of `ring` slots after them, logical row p >= sink
+// at slot sink + (rs + p - sink) mod ring.  Eviction of the middle rows moves
+// the ring start `rs` only, trim shortens the list: no K/V row is ever copied.
+// The stateless forward (cache=None) is the case sink = 0, rs = 0, n0 = 0.
+//
+// One forward appends each sequence's new context rows and then its block
+// rows; appended row i of sequence s is logical row n0[s] + i, at RoPE
+// position pos0[s] + i.  Context rows are packed across sequences
+// ([ctx_start[s], ctx_start[s+1]) in the fc / context GEMMs); the RoPE table
+// holds the packed context rows first and then the nseq * block block rows.
+constexpr int kKvMaxSeq = 32;
+
+struct KvMap {
+  int nseq;                        // 0: plain [seq][kv head][slots] layout, rows 0..kv_len-1
+  int sink, ring, slots;           // slots = sink + ring
+  int ctx_start[kKvMaxSeq + 1];    // packed context rows of sequence s
+  int n0[kKvMaxSeq];               // logical rows stored before this forward
+  int rs_pre[kKvMaxSeq];           // ring start while appending
+  int rs_post[kKvMaxSeq];          // ring start after eviction (what attention reads)
+  int n_att[kKvMaxSeq];            // logical rows attention reads
+  int pos0[kKvMaxSeq];             // RoPE position of appended row 0
+};
+
+__host__ __device__ __forceinline__ int kv_slot(const KvMap& m, int p, int rs) {
+  if (p < m.sink) return p;
+  int j = rs + (p - m.sink);
+  if (j >= m.ring) j -= m.ring;
+  return m.sink + j;
+}
+
+// sequence owning packed context row `row` (the last s with ctx_start[s] <= row)
+__host__ __device__ __forceinline__ int kv_seq_of_ctx_row(const KvMap& m, int row) {
+  int lo = 0, hi = m.nseq - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (m.ctx_start[mid] <= row) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// W8A16 projection epilogues (w8_tc.cu):
+//   kStore   : Y as f16
+//   kQKV     : per-head RMSNorm + neox RoPE for q and k heads, plain v, written
+//              into the attention layouts (dflash.py:290-305)
+//   kResid   : h += Y (fp32 residual stream) and per-128-channel sum of h^2
+//              partials for the next RMSNorm (dflash.py:356, :361)
+//   kSiluMul : each 128-channel tile holds 64 gate and the 64 matching up
+//              channels -> silu(g) * u (dflash.py:330)
+enum W8Mode : int { kStore = 0, kQKV = 1, kResid = 2, kSiluMul = 3 };
+
+struct W8Params {
+  const float* scale;     // [N] fp32 per-output-channel scale (from the fp16 scale)
+  int N, K, M;            // M = activation rows (batch * block)
+  int splits;             // K splits (set by w8tc_launch)
+  const __half* x;        // [M, K] f16 activations
+  // outputs
+  __half* y;              // kStore: [M, N]
+  float* h_out;           // kResid: [M, N] (in place residual)
+  float* hstat_out;       // kResid: [N/128, M]
+  __half* act;            // kSiluMul: [M, N/2]
+  // kQKV
+  __half* q_out;          // [b, NQ, B, 128]
+  __half* k_out;          // this layer's K store [seq][NKV][kv.slots][128] (KvMap)
+  __half* v_out;
+  const float* q_norm;    // [128]
+  const float* k_norm;    // [128]
+  const float2* rope;     // (cos, sin) table; block row m = s * block + j uses row rope_blk0 + m
+  float eps;
+  int n_q_heads, n_kv_heads, block, rope_blk0;
+  KvMap kv;               // block row j of sequence s is logical row n0[s] + ctx_s + j
+};
+
 struct AttnParams {
   const __half* q;      // [b, NQ, B, 128]
-  const __half* k;      // [b, NKV, kv_cap, 128]
-  const __half* v;      // [b, NKV, kv_cap, 128]
-  int nq, nkv, block, kv_len, kv_cap;
+  const __half* k;      // [b, NKV, kv_cap, 128] (kv_cap = kv.slots when kv.nseq > 0)
+  const __half* v;
+  int nq, nkv, block, kv_len, kv_cap;  // kv_len: longest logical row count
   int chunk, splits;    // kv rows per CTA (multiple of 64), CTAs per (b, kv head)
   float* opart;         // [b, NKV, splits, R, 128]
   float* mpart;         // [b, NKV, splits, R]  (base-2 logits)
@@ -20,6 +97,7 @@ struct AttnParams {
   const float2* rope;   // [rows, 64] (cos, sin) table
   float eps;
   int q_row0, k_row0;   // table rows: q row j -> q_row0 + j, k row i -> k_row0 + i
+  KvMap kv;             // nseq > 0: sequence s reads logical rows [0, n_att[s]) at rs_post[s]
 };
 
 enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2 };
@@ -33,12 +111,13 @@ struct TcParams {
   // kTcCtxKV
   const float* scale;       // [N]
   const float* k_norm;      // [L, 128]
-  const float2* rope;       // [rows, 64] (cos, sin) by kv row
-  __half* k_out;            // layer l base = k_out + l * layer_stride
+  const float2* rope;       // (cos, sin) table, row = packed context row
+  __half* k_out;            // layer l base = k_out + l * layer_stride, [seq][NKV][kv.slots][128]
   __half* v_out;
   size_t layer_stride;      // halves
-  int nkv, rows_per_seq, kv_cap, kv_row0;
+  int nkv;
   float eps;
+  KvMap kv;                 // packed context row -> (sequence, logical row, slot)
 };
 
 struct LmParams {
@@ -50,10 +129,8 @@ struct LmParams {
 };
 
 // ---- host launchers (return cudaErrorInvalidValue on unsupported shapes)
-cudaError_t w8_gemm_launch(const W8Params& p, int mode, cudaStream_t st);
 cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
                                const float* w, float eps, __half* x, cudaStream_t st);
-int w8_pick_splits(int N, int K, int M, int num_sms, int max_splits);
 // tcgen05 W8A16 path (w8_tc.cu): w_tiles is the int8 weight packed by
 // w8_tilepack_launch ([N/128][K/64][128][64 B]); part / counters are the
 // split-K scratch (w8tc_part_floats floats; counters zero, one per tile).
@@ -63,9 +140,6 @@ cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int*
                         size_t part_floats, int* counters, int num_sms, cudaStream_t st);
 cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst, int grp, int gstride,
                                int base, cudaStream_t st);
-size_t w8_smem_bytes(const W8Params& p);
-cudaError_t w8_repack_launch(const int8_t* src, int n_src, int K, uint8_t* dst, int grp,
-                             int gstride, int base, cudaStream_t st);
 cudaError_t w8_scale_launch(const __half* s, int n_src, float* dst, int grp, int gstride,
                             int base, cudaStream_t st);
 cudaError_t quantize_q8_launch(const float* w, int oc, int ic, int8_t* q, __half* s,
@@ -90,6 +164,9 @@ cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch
                           int32_t* acc_len, int32_t* correction, cudaStream_t st);
 
 cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st);
+// table rows of one forward: packed context rows, then nseq * block block rows (KvMap)
+cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
+                                  cudaStream_t st);
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
                           cudaStream_t st);
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,

@@ -1,11 +1,13 @@
 // Small bandwidth kernels around the projections:
-//   rope_table   : (cos, sin) of (offset + row) * inv_freq, once per forward
-//                  (the ANE host precomputes the same tables, ane_model.py:484-527)
+//   rope_table   : (cos, sin) of position * inv_freq for the rows of one
+//                  forward (the ANE host precomputes the same tables,
+//                  ane_model.py:484-527)
 //   init_h       : residual stream h = noise (fp32) and its sum-of-squares
 //   ctx_norm     : hidden_norm of the fc output (dflash.py:392) -> f16 rows
 //   final_norm   : final RMSNorm (dflash.py:403) -> bf16 for the lm_head and
 //                  the optional hidden-state output
 //   i8_to_f16    : exact f16 copy of int8 weights (context K/V GEMM operand)
+//   rmsnorm_f16  : RMSNorm of the block rows before a projection -> f16
 #include "kernels.cuh"
 
 namespace dfl {
@@ -19,6 +21,28 @@ __global__ void rope_table_kernel(int pos0, int rows, const float* __restrict__ 
   float s, c;
   sincosf(ang, &s, &c);
   out[idx] = make_float2(c, s);
+}
+
+// rows of one forward: packed context rows (sequence s: positions pos0[s] + i),
+// then block row m = s * block + j at pos0[s] + ctx_s + j
+__global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
+                                      const float* __restrict__ inv_freq, float2* __restrict__ out) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * 64) return;
+  const int r = idx >> 6, i = idx & 63;
+  const int nctx = m.ctx_start[m.nseq];
+  int pos;
+  if (r < nctx) {
+    const int s = kv_seq_of_ctx_row(m, r);
+    pos = m.pos0[s] + (r - m.ctx_start[s]);
+  } else {
+    const int s = (r - nctx) / block, j = (r - nctx) - s * block;
+    pos = m.pos0[s] + (m.ctx_start[s + 1] - m.ctx_start[s]) + j;
+  }
+  const float ang = static_cast<float>(pos) * inv_freq[i];
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  out[idx] = make_float2(cs, sn);
 }
 
 // one warp per row
@@ -125,6 +149,14 @@ cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2*
   rope_table_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(pos0, rows, inv_freq, out);
   return cudaGetLastError();
 }
+
+cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
+                                  cudaStream_t st) {
+  if (m.nseq < 1 || m.nseq > kKvMaxSeq || block < 1) return cudaErrorInvalidValue;
+  const int rows = m.ctx_start[m.nseq] + m.nseq * block;
+  rope_table_map_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(m, block, rows, inv_freq, out);
+  return cudaGetLastError();
+}
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
                           cudaStream_t st) {
   if (H % 8) return cudaErrorInvalidValue;
@@ -153,6 +185,46 @@ cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStrea
 }
 cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st) {
   f16_to_f32_kernel<<<256, 256, 0, st>>>(src, n, dst);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ RMSNorm rows
+// x[m, k] = f16(h[m, k] * rsqrt(sum_p hstat[p, m] / K + eps) * w[k]); one CTA per row
+__global__ void rmsnorm_f16_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
+                                   int hparts, int M, int K, const float* __restrict__ w, float eps,
+                                   __half* __restrict__ x) {
+  const int m = blockIdx.x;
+  __shared__ float part[32];
+  float ss = 0.f;
+  for (int q = threadIdx.x; q < hparts; q += blockDim.x) ss += hstat[(size_t)q * M + m];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) part[0] = rsqrtf(t / static_cast<float>(K) + eps);
+  }
+  __syncthreads();
+  const float r = part[0];
+  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
+    const float4 a = *reinterpret_cast<const float4*>(h + (size_t)m * K + k);
+    const float4 b = *reinterpret_cast<const float4*>(h + (size_t)m * K + k + 4);
+    const float4 wa = *reinterpret_cast<const float4*>(w + k);
+    const float4 wb = *reinterpret_cast<const float4*>(w + k + 4);
+    uint4 o;
+    o.x = pack_f16x2(a.x * r * wa.x, a.y * r * wa.y);
+    o.y = pack_f16x2(a.z * r * wa.z, a.w * r * wa.w);
+    o.z = pack_f16x2(b.x * r * wb.x, b.y * r * wb.y);
+    o.w = pack_f16x2(b.z * r * wb.z, b.w * r * wb.w);
+    *reinterpret_cast<uint4*>(x + (size_t)m * K + k) = o;
+  }
+}
+
+cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
+                               const float* w, float eps, __half* x, cudaStream_t st) {
+  if (K % 8 || M < 1) return cudaErrorInvalidValue;
+  rmsnorm_f16_kernel<<<M, 256, 0, st>>>(h, hstat, hparts, M, K, w, eps, x);
   return cudaGetLastError();
 }
 

@@ -132,8 +132,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         if (MODE == kTcFc && row_ok) p.sumsq_part[(size_t)blockIdx.x * p.M + row] = ss;
       } else {  // kTcCtxKV: two 128-wide heads per tile
-        const int bi = row / p.rows_per_seq;
-        const int i = row - bi * p.rows_per_seq;  // context row inside its sequence
+        // sequence and slot of this packed context row (rows >= M are never stored)
+        const int crow = row_ok ? row : 0;
+        const int bi = kv_seq_of_ctx_row(p.kv, crow);
+        const int slot = kv_slot(p.kv, p.kv.n0[bi] + crow - p.kv.ctx_start[bi], p.kv.rs_pre[bi]);
         const int per_layer = 2 * p.nkv * 128;
 #pragma unroll 1
         for (int hh = 0; hh < 2; ++hh) {
@@ -160,9 +162,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             rstd = rsqrtf(ss / 128.0f + p.eps);
           }
           __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
-                        (((size_t)bi * p.nkv + kvh) * p.kv_cap + p.kv_row0 + i) * 128;
+                        (((size_t)bi * p.nkv + kvh) * p.kv.slots + slot) * 128;
           const float* kn = p.k_norm + layer * 128;
-          const float2* cs = p.rope + (size_t)(p.kv_row0 + i) * 64;
+          const float2* cs = p.rope + (size_t)crow * 64;
 #pragma unroll 1
           for (int half = 0; half < 2; ++half) {
             uint32_t r1[32], r2[32];

@@ -24,7 +24,7 @@
 //              S > 1 each CTA writes its fp32 partial to global scratch and
 //              the last CTA of the tile (per-tile arrival counter) sums the S
 //              partials in split order (deterministic) and runs the fused
-//              epilogue of w8_gemm.cuh (kStore / kQKV / kResid / kSiluMul).
+//              epilogue of kernels.cuh (kStore / kQKV / kResid / kSiluMul).
 // The fp16 per-channel scale is applied in the epilogue (int8 values are exact
 // in f16, so the product is the reference's q * s up to fp32 rounding).
 // Every mbarrier wait is bounded; a timeout raises the device error word and
@@ -145,7 +145,7 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
       const float r = rsqrtf(ss / 128.0f + p.eps);
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[e] = v[e] * r * __ldg(nw + lane * 4 + e);
-      rope_lane_t(v, lane, p.rope + (size_t)(p.kv_row0 + j) * 64);
+      rope_lane_t(v, lane, p.rope + (size_t)(p.rope_blk0 + m) * 64);
     }
     uint2 o;
     o.x = pack_f16x2(v[0], v[1]);
@@ -156,7 +156,9 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
     } else {
       const int kvh = is_k ? head - p.n_q_heads : head - p.n_q_heads - p.n_kv_heads;
       __half* base = is_k ? p.k_out : p.v_out;
-      dstp = base + (((size_t)bi * p.n_kv_heads + kvh) * p.kv_rows + p.kv_row0 + j) * 128;
+      const int lrow = p.kv.n0[bi] + (p.kv.ctx_start[bi + 1] - p.kv.ctx_start[bi]) + j;
+      const int slot = kv_slot(p.kv, lrow, p.kv.rs_pre[bi]);
+      dstp = base + (((size_t)bi * p.n_kv_heads + kvh) * p.kv.slots + slot) * 128;
     }
     *reinterpret_cast<uint2*>(dstp + lane * 4) = o;
   }

@@ -157,29 +157,114 @@ def quantize_q8(w: torch.Tensor):
 
 
 # ----------------------------------------------------------------------------
-# KV cache bookkeeping (dflash.py:139-212)
+# draft KV cache (dflash.py:139-212)
 # ----------------------------------------------------------------------------
-class DFlashKVCache:
-    """Offset / trim bookkeeping of the reference's draft cache.  The stateless
-    draft step (cache=None) is what this build runs on the device; a cache
-    that already holds keys is rejected by ``DFlashDraftModel.__call__``."""
+class _CacheStore:
+    """The device cache behind one ``make_cache()`` list: K/V rows of every
+    layer and sequence in device rings (include/dflash_b200.h, dflash_cache_*)."""
 
-    def __init__(self, sink_size: int = 0, window_size: int = 0):
-        self.keys = None
-        self.values = None
-        self.offset = 0
+    def __init__(self, model, num_layers, sink_size, window_size, max_len, max_batch):
+        self._lib = model._lib
+        self.model = model          # keeps the handle alive while the cache exists
+        self.num_layers = num_layers
+        self.batch = 1              # sequences of the last forward
+        ptr = ctypes.c_void_p()
+        N.check(self._lib.dflash_cache_create(model._handle, num_layers, max_batch, int(sink_size),
+                                              int(window_size), int(max_len), ctypes.byref(ptr)),
+                "dflash_cache_create")
+        self.ptr = ptr
+
+    def close(self):
+        if getattr(self, "ptr", None) is not None and self.ptr.value:
+            N.check(self._lib.dflash_cache_destroy(self.ptr), "dflash_cache_destroy")
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def state(self, layer, seq=0):
+        off, ln = ctypes.c_int32(), ctypes.c_int32()
+        N.check(self._lib.dflash_cache_state(self.ptr, layer, seq, ctypes.byref(off), ctypes.byref(ln)),
+                "dflash_cache_state")
+        return off.value, ln.value
+
+    def trim(self, layer, n):
+        N.check(self._lib.dflash_cache_trim(self.ptr, layer, int(n)), "dflash_cache_trim")
+
+    def reset(self):
+        N.check(self._lib.dflash_cache_reset(self.ptr), "dflash_cache_reset")
+
+    def read(self, layer):
+        """(keys, values) f16 [b, NKV, len, 128] in logical order, or a list of
+        per-sequence [NKV, len_s, 128] tensors when the lengths differ."""
+        cfg = self.model.config
+        ks, vs = [], []
+        st = torch.cuda.current_stream(self.model.device)
+        for seq in range(self.batch):
+            ln = self.state(layer, seq)[1]
+            k = torch.empty((cfg.num_key_value_heads, ln, cfg.head_dim), dtype=torch.float16,
+                            device=self.model.device)
+            v = torch.empty_like(k)
+            N.check(self._lib.dflash_cache_read(self.ptr, layer, seq, N.ptr(k), N.ptr(v),
+                                                ctypes.c_void_p(st.cuda_stream)), "dflash_cache_read")
+            ks.append(k)
+            vs.append(v)
+        if len({k.shape[1] for k in ks}) == 1:
+            return torch.stack(ks), torch.stack(vs)
+        return ks, vs
+
+
+class DFlashKVCache:
+    """One layer of the draft cache (dflash.py:139-212): ``offset``, ``keys`` /
+    ``values`` and ``trim(n)`` with the reference's meaning.  Appending, with
+    the sink + window eviction of ``update_and_fetch``, happens inside the
+    draft forward on the device."""
+
+    def __init__(self, store: _CacheStore, layer: int, sink_size: int, window_size: int):
+        self._store = store
+        self.layer = layer
         self.sink_size = int(sink_size)
         self.window_size = int(window_size)
 
+    @property
+    def offset(self) -> int:
+        return self._store.state(self.layer, 0)[0]
+
+    def _kv(self):
+        if all(self._store.state(self.layer, s)[1] == 0 for s in range(self._store.batch)):
+            return None, None
+        return self._store.read(self.layer)
+
+    @property
+    def keys(self):
+        return self._kv()[0]
+
+    @property
+    def values(self):
+        return self._kv()[1]
+
     def trim(self, n: int):
-        if self.keys is not None and n > 0:
-            keep = max(self.keys.shape[2] - n, 0)
-            self.keys = self.keys[..., :keep, :]
-            self.values = self.values[..., :keep, :]
-            self.offset -= n
+        self._store.trim(self.layer, n)
 
     def state(self):
-        return [] if self.keys is None else [self.keys, self.values]
+        k, v = self._kv()
+        return [] if k is None else [k, v]
+
+
+class DFlashCache(list):
+    """``make_cache()`` result: one ``DFlashKVCache`` per draft layer over one
+    device store (``generate.py`` trims each entry after every draft step)."""
+
+    def __init__(self, store: _CacheStore, sink_size: int, window_size: int):
+        super().__init__(DFlashKVCache(store, l, sink_size, window_size)
+                         for l in range(store.num_layers))
+        self.store = store
+
+    def reset(self):
+        self.store.reset()
 
 
 # ----------------------------------------------------------------------------
@@ -266,9 +351,16 @@ class DFlashDraftModel:
         except Exception:
             pass
 
-    def make_cache(self, sink_size: int = 64, window_size: int = 1024) -> list:
-        return [DFlashKVCache(sink_size=sink_size, window_size=window_size)
-                for _ in range(self.num_draft_layers)]
+    def make_cache(self, sink_size: int = 64, window_size: int = 1024,
+                   max_len: Optional[int] = None, max_batch: Optional[int] = None) -> "DFlashCache":
+        """Per-layer draft caches (dflash.py:405-406).  Eviction runs when both
+        sink_size and window_size are positive; otherwise the cache holds up to
+        ``max_len`` rows per sequence (default: 4 * (max_ctx + max_block))."""
+        if max_len is None:
+            max_len = 4 * (self.max_ctx + self.max_block)
+        store = _CacheStore(self, self.num_draft_layers, sink_size, window_size, max_len,
+                            max_batch or self.max_batch)
+        return DFlashCache(store, sink_size, window_size)
 
     def set_block_size(self, new_block: int) -> None:
         """Change the active block size (ane_model.py:611-630: ValueError
@@ -290,19 +382,50 @@ class DFlashDraftModel:
     def draft_step(self, noise_embedding, target_hidden, rope_offset: int = 0,
                    target_tokens=None, want_hidden: bool = True, want_tokens: bool = True,
                    out_hidden=None, out_tokens=None, acc_len=None, correction=None,
-                   hidden_fp32: bool = False, phase_events=None):
-        """One stateless draft step on the device: final-normed hidden states
-        (bf16, or fp32 with ``hidden_fp32``), greedy draft ids for rows 1..q-1
-        and, given the verifier's posterior ``target_tokens`` [b, q], the
-        accepted length and correction token.  ``phase_events``: optional list
-        of 8 ``torch.cuda.Event`` recorded at the phase boundaries."""
+                   hidden_fp32: bool = False, phase_events=None, cache=None, ctx_lens=None,
+                   rope_offsets=None):
+        """One draft step on the device: final-normed hidden states (bf16, or
+        fp32 with ``hidden_fp32``), greedy draft ids for rows 1..q-1 and, given
+        the verifier's posterior ``target_tokens`` [b, q], the accepted length
+        and correction token.
+
+        ``target_hidden`` is [b, ctx, F*H], or with ``ctx_lens`` (one count per
+        sequence) the packed rows [sum(ctx_lens), F*H].  With ``cache`` (from
+        ``make_cache``) the rows are appended to it and the step attends to
+        everything it holds; without, positions start at ``rope_offset`` (or
+        ``rope_offsets`` per sequence).  ``phase_events``: optional list of 8
+        ``torch.cuda.Event`` recorded at the phase boundaries."""
         noise = self._as_dev(noise_embedding, torch.bfloat16)
         th = self._as_dev(target_hidden, torch.bfloat16)
-        if noise.dim() != 3 or th.dim() != 3 or noise.shape[0] != th.shape[0]:
-            raise ValueError("noise_embedding [b, q, H] and target_hidden [b, ctx, F*H] expected")
+        if noise.dim() != 3:
+            raise ValueError("noise_embedding [b, q, H] expected")
         b, q, H = noise.shape
-        if H != self.config.hidden_size or th.shape[2] != len(self.config.target_layer_ids) * H:
+        F = len(self.config.target_layer_ids)
+        lens_arr = offs_arr = None
+        if ctx_lens is not None:
+            lens = [int(c) for c in ctx_lens]
+            if len(lens) != b:
+                raise ValueError(f"ctx_lens needs {b} entries")
+            th = th.reshape(-1, th.shape[-1])
+            if th.shape[0] != sum(lens):
+                raise ValueError(f"packed target_hidden has {th.shape[0]} rows, ctx_lens sum to {sum(lens)}")
+            lens_arr = (ctypes.c_int32 * b)(*lens)
+            ctx_len = max(lens) if lens else 0
+        else:
+            if th.dim() != 3 or th.shape[0] != b:
+                raise ValueError("noise_embedding [b, q, H] and target_hidden [b, ctx, F*H] expected")
+            ctx_len = th.shape[1]
+        if H != self.config.hidden_size or th.shape[-1] != F * H:
             raise ValueError("hidden size mismatch")
+        if rope_offsets is not None:
+            if len(rope_offsets) != b:
+                raise ValueError(f"rope_offsets needs {b} entries")
+            offs_arr = (ctypes.c_int32 * b)(*[int(o) for o in rope_offsets])
+        store = None
+        if cache is not None:
+            store = getattr(cache, "store", None)
+            if not isinstance(store, _CacheStore):
+                raise ValueError("cache must come from this model's make_cache()")
         if want_hidden and out_hidden is None:
             out_hidden = torch.empty((b, q, H), dtype=torch.float32 if hidden_fp32 else torch.bfloat16,
                                      device=self.device)
@@ -318,7 +441,7 @@ class DFlashDraftModel:
             if correction is None:
                 correction = torch.empty((b,), dtype=torch.int32, device=self.device)
         args = N.DFlashForwardArgs(
-            batch=b, block=q, ctx_len=th.shape[1], rope_offset=int(rope_offset),
+            batch=b, block=q, ctx_len=ctx_len, rope_offset=int(rope_offset),
             num_layers=int(self.num_draft_layers),
             noise=noise.data_ptr(), target_hidden=th.data_ptr() if th.numel() else None,
             out_hidden=out_hidden.data_ptr() if out_hidden is not None else None,
@@ -326,7 +449,8 @@ class DFlashDraftModel:
             out_tokens=out_tokens.data_ptr() if out_tokens is not None else None,
             target_tokens=tt.data_ptr() if tt is not None else None,
             acc_len=acc_len.data_ptr() if acc_len is not None else None,
-            correction=correction.data_ptr() if correction is not None else None)
+            correction=correction.data_ptr() if correction is not None else None,
+            ctx_lens=lens_arr, rope_offsets=offs_arr, cache=store.ptr if store is not None else None)
         if phase_events is not None:
             if len(phase_events) < N.DFLASH_PHASES:
                 raise ValueError(f"phase_events needs {N.DFLASH_PHASES} events")
@@ -335,6 +459,8 @@ class DFlashDraftModel:
             args.n_phase_events = len(phase_events)
         N.check(self._lib.dflash_forward(self._handle, ctypes.byref(args), self._stream()),
                 "dflash_forward")
+        if store is not None:
+            store.batch = b
         return out_hidden, out_tokens, acc_len, correction
 
     def __call__(self, noise_embedding, target_hidden, mask=None, cache=None, **kwargs):
@@ -342,35 +468,28 @@ class DFlashDraftModel:
         final-normed hidden states [b, q, H] (bf16)."""
         if mask is not None:
             raise ValueError("the DFlash draft attention is non-causal; mask must be None")
-        rope_offset = 0
-        if cache is not None:
-            if any(c.keys is not None for c in cache):
-                raise NotImplementedError("a draft KV cache that already holds keys is not supported;"
-                                          " call with cache=None (stateless draft step)")
-            rope_offset = cache[0].offset if len(cache) else 0
-        hidden, _, _, _ = self.draft_step(noise_embedding, target_hidden, rope_offset,
+        hidden, _, _, _ = self.draft_step(noise_embedding, target_hidden, cache=cache,
                                           want_hidden=True, want_tokens=False)
         return hidden
 
-    def draft_tokens(self, noise_embedding, target_hidden, rope_offset: int = 0):
+    def draft_tokens(self, noise_embedding, target_hidden, rope_offset: int = 0, cache=None):
         """lm_head + greedy argmax fused on the device: ids [b, q-1] for rows
         1..q-1 (generate.py:604-606)."""
         _, toks, _, _ = self.draft_step(noise_embedding, target_hidden, rope_offset,
-                                        want_hidden=False, want_tokens=True)
+                                        want_hidden=False, want_tokens=True, cache=cache)
         return toks
 
     # -- ANE-style split API (ane_model.py:538-604) ---------------------------
     def prepare_forward(self, noise_embedding, precomputed_context, cache, target_hidden):
         if precomputed_context is not None:
             raise ValueError("precomputed_context is not used: fc + hidden_norm run on the device")
-        off = cache[0].offset if cache is not None and len(cache) and cache[0].offset > 0 else 0
-        self._pending = (noise_embedding, target_hidden, off)
+        self._pending = (noise_embedding, target_hidden, cache)
 
     def run_kernels(self):
         if self._pending is None:
             raise RuntimeError("prepare_forward() must be called first")
-        noise, th, off = self._pending
-        self._out_hidden, self._out_tokens, _, _ = self.draft_step(noise, th, off)
+        noise, th, cache = self._pending
+        self._out_hidden, self._out_tokens, _, _ = self.draft_step(noise, th, cache=cache)
         self._pending = None
 
     def read_output(self):
