@@ -18,6 +18,7 @@ value = sum over ranks of drafted tokens / max over ranks of the step time.
 CPU restatement in oracle/, MLX being unavailable) on rank 0 only.
 """
 import argparse
+import importlib
 import json
 import os
 import statistics
@@ -259,11 +260,14 @@ def main():
         return
 
     pkg = _pkg()
+    shard = importlib.import_module("mirror-sd_b200.shard")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg, w, lm, model = build_model(pkg, cfgd, args.ctx, args.batch, dev, seed=0)
-    noise, th = synth_inputs(cfgd, args.ctx, args.batch, dev, rank)
     B = cfgd["block_size"]
+    # world * batch independent requests; this rank drafts its share (no collective on the data path)
+    mine = shard.shard_requests([args.ctx] * (world * args.batch), world, rank, B)
+    noise, th = synth_inputs(cfgd, args.ctx, len(mine), dev, mine[0])
     out_h = torch.empty((args.batch, B, cfgd["hidden_size"]), dtype=torch.bfloat16, device=dev)
     out_t = torch.empty((args.batch, B - 1), dtype=torch.int32, device=dev)
     acc = torch.empty((args.batch,), dtype=torch.int32, device=dev)
@@ -310,11 +314,9 @@ def main():
     names = pkg._native.PHASE_NAMES
     for k in range(1, 8):
         phases[names[k]] = statistics.mean(ev[i][k - 1].elapsed_time(ev[i][k]) for i in range(args.steps))
-    t_ms = torch.tensor([ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t_ms, op=dist.ReduceOp.MAX)
-    ms_max = float(t_ms.item())
-    acc_mean = float(acc.float().mean().item())
+    ms_max = shard.max_over_ranks(ms)
+    accs = shard.gather_to_rank0(acc.cpu().tolist())
+    acc_mean = statistics.mean(a for r in accs for a in r) if accs else None
 
     # end-to-end through the public API with host buffers
     e2e = None
@@ -349,13 +351,11 @@ def main():
             e2e_step()
         e2.record()
         torch.cuda.synchronize(dev)
-        ms_e2e = torch.tensor([s2.elapsed_time(e2) / k2], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(ms_e2e, op=dist.ReduceOp.MAX)
+        ms_e2e = shard.max_over_ranks(s2.elapsed_time(e2) / k2)
         h2d = noise.numel() * 2 + th.numel() * 2 + target.numel() * 4
         d2h = out_t.numel() * 4 + acc.numel() * 4 + cor.numel() * 4
-        e2e = {"value": world * args.batch * (B - 1) / (float(ms_e2e.item()) / 1e3), "unit": "draft tok/s",
-               "ms_per_step": float(ms_e2e.item()), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        e2e = {"value": shard.job_throughput([args.batch * (B - 1)] * world, ms_e2e), "unit": "draft tok/s",
+               "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "steps": k2, "api": "DFlashDraftModel.draft_step on pinned host tensors"}
 
     if sampler:
@@ -378,7 +378,8 @@ def main():
             traffic = json.load(f).get(f"fc_gemm_{args.config}_ctx{args.ctx}")
     t_step = ms_max / 1e3
     line = {
-        "metric": METRIC, "value": world * args.batch * (B - 1) / t_step, "unit": "draft tok/s",
+        "metric": METRIC, "value": shard.job_throughput([args.batch * (B - 1)] * world, ms_max),
+        "unit": "draft tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
         "us_per_step": ms_max * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "w8a16: int8 weights, bf16/f16 activations, fp32 accumulate", "data": "synthetic",
