@@ -88,7 +88,8 @@ struct Handle {
   float* ctx_part = nullptr;
   __half* ctx_n = nullptr;
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
-  __half* xn = nullptr;             // RMSNorm'd block rows (f16) feeding q|k|v and gate|up
+  int8_t* xl = nullptr;             // projection input limbs [3][64][max(H, NQ*128, I)]
+  float* xs = nullptr;              // their row scales [64]
   float *opart = nullptr, *mpart = nullptr, *lpart = nullptr;
   size_t attn_part_rows = 0;
   __nv_bfloat16* hn = nullptr;
@@ -295,7 +296,8 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->Q, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->attn_out, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->act, (size_t)Mx * I));
-  CKC(A.alloc(&hd->xn, (size_t)Mx * H));
+  CKC(A.alloc(&hd->xl, (size_t)3 * 64 * std::max(std::max(H, NQ * 128), I)));
+  CKC(A.alloc(&hd->xs, 64));
   // the split count never exceeds what the longest rows give, and a cache can
   // make rows longer than max_ctx + max_block: size for any length
   hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, 1 << 28, hd->num_sms);
@@ -490,10 +492,10 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     __half* Kl = Kbase + l * layer_stride;
     __half* Vl = Vbase + l * layer_stride;
     // q | k | v of the block rows: input RMSNorm fused into the activation load
-    CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xn, st));
+    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xl, hd->xs, st));
     W8Params p{};
     p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
-    p.x = hd->xn; p.eps = d.rms_norm_eps;
+    p.xl = hd->xl; p.xscale = hd->xs; p.eps = d.rms_norm_eps;
     p.q_out = hd->Q; p.k_out = Kl; p.v_out = Vl; p.q_norm = ly.q_norm; p.k_norm = hd->k_norm_all + l * 128;
     p.rope = hd->rope; p.n_q_heads = NQ; p.n_kv_heads = NKV; p.block = B; p.rope_blk0 = Ctot;
     p.kv = m;
@@ -509,22 +511,24 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     CK(attn_launch(ap, b, hd->attn_out, st));
     // o_proj + residual
     W8Params o{};
-    o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.x = hd->attn_out;
+    CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->xl, hd->xs, st));
+    o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.xl = hd->xl; o.xscale = hd->xs;
     o.h_out = hd->h; o.hstat_out = hd->hstat;
     CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     hparts = H / 128;
     // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
-    CK(rmsnorm_f16_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xn, st));
+    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xl, hd->xs, st));
     W8Params gu{};
     gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
-    gu.x = hd->xn; gu.act = hd->act;
+    gu.xl = hd->xl; gu.xscale = hd->xs; gu.act = hd->act;
     CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     // down + residual
     W8Params dn{};
-    dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.x = hd->act;
+    CK(w8_limbs_launch(hd->act, M, I, hd->xl, hd->xs, st));
+    dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.xl = hd->xl; dn.xscale = hd->xs;
     dn.h_out = hd->h; dn.hstat_out = hd->hstat;
     CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
-    launches += 8;  // 2 norms, qkv, attention partial + combine, o, gate|up, down
+    launches += 10;  // 2 norms + 2 limb splits, qkv, attention partial + combine, o, gate|up, down
   }
   CK(mark(5));
   CK(final_norm_launch(hd->h, hd->hstat, hparts, M, H, hd->norm, d.rms_norm_eps, hd->hn,
@@ -719,9 +723,14 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   int8_t* wt = nullptr;
   CK(cudaMallocAsync(&wt, (size_t)N * K, st));
   CK(w8_tilepack_launch(q, N, K, wt, 1 << 30, 0, 0, st));
+  int8_t* xl = nullptr;
+  float* xs = nullptr;
+  CK(cudaMallocAsync(&xl, (size_t)3 * 64 * K, st));
+  CK(cudaMallocAsync(&xs, 64 * sizeof(float), st));
+  CK(w8_limbs_launch(reinterpret_cast<const __half*>(x), M, K, xl, xs, st));
   W8Params p{};
   p.scale = sp; p.N = N; p.K = K; p.M = M;
-  p.x = reinterpret_cast<const __half*>(x); p.y = reinterpret_cast<__half*>(y);
+  p.xl = xl; p.xscale = xs; p.y = reinterpret_cast<__half*>(y);
   const size_t pf = w8tc_part_floats(N, K, M, sms);
   float* part = nullptr;
   int* cnt = nullptr;
@@ -735,6 +744,8 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
     e = cudaStreamSynchronize(st);
   }
   cudaFreeAsync(sp, st);
+  cudaFreeAsync(xl, st);
+  cudaFreeAsync(xs, st);
   cudaFreeAsync(wt, st);
   cudaFreeAsync(part, st);
   cudaFreeAsync(cnt, st);

@@ -49,7 +49,10 @@ __host__ __device__ __forceinline__ int kv_seq_of_ctx_row(const KvMap& m, int ro
   return lo;
 }
 
-// W8A16 projection epilogues (w8_tc.cu):
+// W8A16 projections (w8_tc.cu).  Activations enter as three int8 limbs per
+// element with a power-of-two scale per row (w8_limbs / rmsnorm_limbs):
+// int8 [3][MP][K] limb-major, MP = M padded to 16, rows >= M zero.
+// Epilogues:
 //   kStore   : Y as f16
 //   kQKV     : per-head RMSNorm + neox RoPE for q and k heads, plain v, written
 //              into the attention layouts (dflash.py:290-305)
@@ -63,7 +66,8 @@ struct W8Params {
   const float* scale;     // [N] fp32 per-output-channel scale (from the fp16 scale)
   int N, K, M;            // M = activation rows (batch * block)
   int splits;             // K splits (set by w8tc_launch)
-  const __half* x;        // [M, K] f16 activations
+  const int8_t* xl;       // activation limbs [3][MP][K]
+  const float* xscale;    // [MP] row scales (powers of two)
   // outputs
   __half* y;              // kStore: [M, N]
   float* h_out;           // kResid: [M, N] (in place residual)
@@ -129,11 +133,12 @@ struct LmParams {
 };
 
 // ---- host launchers (return cudaErrorInvalidValue on unsupported shapes)
-cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
-                               const float* w, float eps, __half* x, cudaStream_t st);
 // tcgen05 W8A16 path (w8_tc.cu): w_tiles is the int8 weight packed by
-// w8_tilepack_launch ([N/128][K/64][128][64 B]); part / counters are the
-// split-K scratch (w8tc_part_floats floats; counters zero, one per tile).
+// w8_tilepack_launch ([N/128][K/128][128][128 B], swizzled); part / counters
+// are the split-K scratch (w8tc_part_floats floats; counters zero, one per tile).
+cudaError_t w8_limbs_launch(const __half* x, int M, int K, int8_t* xl, float* xscale, cudaStream_t st);
+cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, int hparts, int M, int K,
+                                 const float* w, float eps, int8_t* xl, float* xscale, cudaStream_t st);
 void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups);
 size_t w8tc_part_floats(int N, int K, int M, int num_sms);
 cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int* err, float* part,

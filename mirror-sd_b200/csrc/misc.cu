@@ -7,7 +7,6 @@
 //   final_norm   : final RMSNorm (dflash.py:403) -> bf16 for the lm_head and
 //                  the optional hidden-state output
 //   i8_to_f16    : exact f16 copy of int8 weights (context K/V GEMM operand)
-//   rmsnorm_f16  : RMSNorm of the block rows before a projection -> f16
 #include "kernels.cuh"
 
 namespace dfl {
@@ -188,44 +187,6 @@ cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStrea
   return cudaGetLastError();
 }
 
-// ------------------------------------------------------------------ RMSNorm rows
-// x[m, k] = f16(h[m, k] * rsqrt(sum_p hstat[p, m] / K + eps) * w[k]); one CTA per row
-__global__ void rmsnorm_f16_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
-                                   int hparts, int M, int K, const float* __restrict__ w, float eps,
-                                   __half* __restrict__ x) {
-  const int m = blockIdx.x;
-  __shared__ float part[32];
-  float ss = 0.f;
-  for (int q = threadIdx.x; q < hparts; q += blockDim.x) ss += hstat[(size_t)q * M + m];
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) part[0] = rsqrtf(t / static_cast<float>(K) + eps);
-  }
-  __syncthreads();
-  const float r = part[0];
-  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
-    const float4 a = *reinterpret_cast<const float4*>(h + (size_t)m * K + k);
-    const float4 b = *reinterpret_cast<const float4*>(h + (size_t)m * K + k + 4);
-    const float4 wa = *reinterpret_cast<const float4*>(w + k);
-    const float4 wb = *reinterpret_cast<const float4*>(w + k + 4);
-    uint4 o;
-    o.x = pack_f16x2(a.x * r * wa.x, a.y * r * wa.y);
-    o.y = pack_f16x2(a.z * r * wa.z, a.w * r * wa.w);
-    o.z = pack_f16x2(b.x * r * wb.x, b.y * r * wb.y);
-    o.w = pack_f16x2(b.z * r * wb.z, b.w * r * wb.w);
-    *reinterpret_cast<uint4*>(x + (size_t)m * K + k) = o;
-  }
-}
 
-cudaError_t rmsnorm_f16_launch(const float* h, const float* hstat, int hparts, int M, int K,
-                               const float* w, float eps, __half* x, cudaStream_t st) {
-  if (K % 8 || M < 1) return cudaErrorInvalidValue;
-  rmsnorm_f16_kernel<<<M, 256, 0, st>>>(h, hstat, hparts, M, K, w, eps, x);
-  return cudaGetLastError();
-}
 
 }  // namespace dfl

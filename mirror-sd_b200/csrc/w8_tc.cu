@@ -1,84 +1,85 @@
-// W8A16 skinny GEMM on the 5th-gen tensor cores (tcgen05 + TMA), for the
-// block rows of the draft forward (q|k|v, o, gate|up, down projections).
+// W8A16 skinny GEMM on the 5th-gen tensor cores for the block rows of the
+// draft forward (q|k|v, o, gate|up, down projections).
 //
 //   Y[m, n] = scale[n] * sum_k X[m, k] * Wq[n, k]      m < M <= 64, Wq int8
 //
-// Swap-AB: the 128 output channels of a tile are the UMMA M dimension and the
-// (padded) activation rows are N (16..64), so one tcgen05.mma.kind::f16
-// M=128 N=MP K=16 covers a whole tile.
+// The f16 activations run on the int8 tensor pipe (tcgen05.mma kind::i8) as
+// three int8 limbs.  Each row m gets a power-of-two scale 2^(e_m - 20),
+// where 2^e_m bounds max|x|.  Then x * 2^(20 - e_m) rounds to an integer
+// q, |q| < 2^20, written as q = l0 + 128 l1 + 16384 l2 with
+// l0, l1 in [-64, 63] and l2 in [-64, 64].
+// For every element within 2^10 of the row maximum this is exact: an f16 has
+// 11 significant bits.  Smaller elements lose at most 2^(e_m - 21), below the
+// f16 rounding of the larger ones.  The weight-limb products accumulate
+// exactly in int32 (|sum| < 127 * 64 * K < 2^31 for K <= 2^18).  Hence the
+// integer sums, recombined in fp32 and scaled, are the W8A16 product with no
+// rounding inside the dot product.
 //
-// Persistent, one CTA per SM.  CTAs form groups of S (the K-split); group g
-// walks tiles g, g + groups, ... and CTA `split` of the group covers the same
-// K-slice of each of them, so every CTA streams the same number of bytes.
-// Roles (14 warps):
-//   warp 0     producer: each tile's k64 weight block is one contiguous 8 KB
-//              run of the packed weights (cp.async.bulk); the f16 activation
-//              tile [MP x 64] arrives by TMA with the 128-byte swizzle.  A deep
-//              ring (NA stages) keeps ~100 KB of weights in flight per SM.
-//   warps 2-9  converters: int8 -> 128-byte-swizzled f16 tile in a 4-stage
-//              ring (PRMT with 0x6464 builds 1024+u, one f16x2 subtract
-//              recovers q exactly), fence.proxy.async, arrive.
-//   warp 1     single-thread UMMA issue into one of two 128 x MP fp32 TMEM
-//              accumulators; tcgen05.commit frees the ring slots.
-//   warps 10-13 epilogue of the previous tile while the next one streams: with
-//              S > 1 each CTA writes its fp32 partial to global scratch and
-//              the last CTA of the tile (per-tile arrival counter) sums the S
-//              partials in split order (deterministic) and runs the fused
-//              epilogue of kernels.cuh (kStore / kQKV / kResid / kSiluMul).
-// The fp16 per-channel scale is applied in the epilogue (int8 values are exact
-// in f16, so the product is the reference's q * s up to fp32 rounding).
+// Why: weights go straight from the bulk-copy ring into the MMA, as the
+// lm_head kernel does.  No int8 -> f16 conversion pass through shared memory
+// remains, which was the bound of the f16 formulation.
+//
+// Swap-AB: the 128 output channels of a tile are UMMA M.  The 3 * MP limb rows
+// (MP = M padded to 16) are N.  One k128 block of a tile is
+// 4 x tcgen05.mma.kind::i8 M=128 N=3MP K=32.
+//
+// Persistent, one CTA per SM, 6 warps.  CTAs form groups of S (the K-split);
+// group g walks tiles g, g + groups, ... and CTA `split` of the group covers
+// the same K-slice of each of them.
+//   warp 0   producer: the tile's k128 weight block, 16 KB, is one contiguous
+//            pre-swizzled run (cp.async.bulk); the limb tile [3MP x 128 B]
+//            arrives by TMA with the 128-byte swizzle.
+//   warp 1   single-thread UMMA issue into one of two int32 TMEM accumulators;
+//            tcgen05.commit frees ring stages.
+//   warps 2-5 epilogue of the previous tile while the next one streams.  With
+//            S > 1, each CTA writes its fp32 partial to global scratch; the
+//            last CTA of the tile (per-tile arrival counter) sums the S
+//            partials in split order (deterministic) and runs the fused
+//            epilogue:
+//     kStore   : Y as f16
+//     kQKV     : per-head RMSNorm + neox RoPE for q and k heads, plain v,
+//                written into the KvMap K/V layout (dflash.py:290-305)
+//     kResid   : h += Y (fp32 residual stream) and per-128-channel sum of h^2
+//                partials for the next RMSNorm (dflash.py:356, :361)
+//     kSiluMul : each 128-channel tile holds 64 gate and the 64 matching up
+//                channels -> silu(g) * u (dflash.py:330)
 // Every mbarrier wait is bounded; a timeout raises the device error word and
 // the CTA unwinds (TMEM released on every path).
 #include "kernels.cuh"
 
 namespace dfl {
 
-constexpr int WP_THREADS = 448;  // 14 warps: producer, MMA, 8 converters, 4 epilogue
-constexpr int WP_NCW = 8;        // converter warps
-constexpr int WP_NB = 4;         // converted f16 ring
-constexpr int WP_W8 = 128 * 64;  // int8 tile bytes per k64
-constexpr int WP_WF = 128 * 128; // f16 tile bytes per k64
-constexpr int WP_SMEM_BUDGET = 206 * 1024;
+constexpr int WI_THREADS = 192;       // producer, MMA, 4 epilogue warps
+constexpr int WI_WB = 128 * 128;      // int8 weight block: 128 channels x k128
+constexpr int WI_SMEM_BUDGET = 200 * 1024;
 
 template <int MP>
-struct WpCfg {
-  static constexpr int X_BYTES = MP * 128;
-  static constexpr int A_STAGE = X_BYTES + WP_W8;  // [X swizzled | int8 weights]
-  static constexpr int RED_BYTES = MP * 129 * 4;  // S == 1 epilogue staging [MP][129]
-  static constexpr int NA_RAW = (WP_SMEM_BUDGET - WP_NB * WP_WF - RED_BYTES) / A_STAGE;
-  static constexpr int NA = NA_RAW > 16 ? 16 : NA_RAW;
-  static constexpr int RING_BYTES = WP_NB * WP_WF + NA * A_STAGE;
-  static constexpr uint32_t ACC_COLS = MP <= 32 ? 32 : 64;
-  static constexpr size_t SMEM = (size_t)RING_BYTES + RED_BYTES + 1024 + 512;
+struct WiCfg {
+  static constexpr int NB = 3 * MP;                // UMMA N: three limbs of MP rows
+  static constexpr int X_BYTES = NB * 128;         // limb tile per k128
+  static constexpr int STAGE = WI_WB + X_BYTES;    // multiple of 1024
+  static constexpr int RED_BYTES = MP * 129 * 4;   // S == 1 epilogue staging [MP][129]
+  static constexpr int NS_RAW = (WI_SMEM_BUDGET - RED_BYTES) / STAGE;
+  static constexpr int NS = NS_RAW > 12 ? 12 : NS_RAW;
+  static constexpr uint32_t ACC_COLS = NB <= 64 ? 64 : (NB <= 128 ? 128 : 256);
+  static constexpr size_t SMEM = (size_t)NS * STAGE + RED_BYTES + 1024 + 256;
 };
 
-__device__ __forceinline__ uint4 lds128_u(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ void sts128_u(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// 16 int8 -> 16 f16 (exact); x ^ 0x80 biases to u = q + 128
-__device__ __forceinline__ void i8x16_to_f16x16(uint4 v, uint4& lo, uint4& hi) {
-  const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
-  uint32_t o[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    o[2 * i] = u8x2_to_f16x2(w[i], 0x5140);
-    o[2 * i + 1] = u8x2_to_f16x2(w[i], 0x5342);
-  }
-  lo = make_uint4(o[0], o[1], o[2], o[3]);
-  hi = make_uint4(o[4], o[5], o[6], o[7]);
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// kind::i8 instruction descriptor: s32 accumulate, signed int8 A and B, K-major
+__host__ __device__ constexpr uint32_t umma_idesc_s8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ void rope_lane_t(float (&y)[4], int lane, const float2* __restrict__ cs_row) {
@@ -93,9 +94,9 @@ __device__ __forceinline__ void rope_lane_t(float (&y)[4], int lane, const float
   }
 }
 
-struct WpArgs {
+struct WiArgs {
   W8Params p;
-  const int8_t* w_tiles;  // [N/128][K/64][128 rows][64 B]
+  const int8_t* w_tiles;  // [N/128][K/128][128 rows][128 B], 16-byte chunks swizzled
   float* part;            // [tiles][S][MP][128] fp32 split partials (S > 1)
   int* counters;          // [tiles] arrival counters, zero between launches
   int groups;             // grid = groups * S
@@ -103,14 +104,17 @@ struct WpArgs {
 };
 
 // Fused epilogue for one activation row m of tile `tile` (a warp; lane owns
-// EPC consecutive channels).  v / u hold the unscaled sums.
+// EPC consecutive channels).  v / u hold the integer sums of the row's limbs
+// (exact up to the fp32 conversion); the row's power-of-two scale and the
+// channel scales turn them into the W8A16 product.
 template <int MODE>
 __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int m, int lane,
                                                 float (&v)[4], float (&u)[4]) {
   constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;
   const int gch = tile * 128 + lane * EPC;
+  const float rs = __ldg(p.xscale + m);
 #pragma unroll
-  for (int e = 0; e < EPC; ++e) v[e] *= __ldg(p.scale + gch + e);
+  for (int e = 0; e < EPC; ++e) v[e] *= __ldg(p.scale + gch + e) * rs;
   if (MODE == kStore) {
     uint2 o;
     o.x = pack_f16x2(v[0], v[1]);
@@ -129,7 +133,7 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const float gv = v[e];
-      const float uv = u[e] * __ldg(p.scale + gch + 64 + e);
+      const float uv = u[e] * (__ldg(p.scale + gch + 64 + e) * rs);
       o[e] = (gv / (1.0f + expf(-gv))) * uv;
     }
     *reinterpret_cast<uint32_t*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) = pack_f16x2(o[0], o[1]);
@@ -165,20 +169,17 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
 }
 
 template <int MP, int MODE>
-__global__ void __launch_bounds__(WP_THREADS, 1)
-    w8p_kernel(const __grid_constant__ CUtensorMap map_x, const WpArgs args) {
-  using C = WpCfg<MP>;
+__global__ void __launch_bounds__(WI_THREADS, 1)
+    w8i_kernel(const __grid_constant__ CUtensorMap map_x, const WiArgs args) {
+  using C = WiCfg<MP>;
   const W8Params& p = args.p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ringB = smem;                       // [NB][128 x 128 B] swizzled f16 weights
-  uint8_t* ringA = smem + WP_NB * WP_WF;       // [NA][X | int8]
-  float* red = reinterpret_cast<float*>(smem + C::RING_BYTES);  // [MP][129], S == 1 only
-  uint64_t* fullA = reinterpret_cast<uint64_t*>(smem + C::RING_BYTES + C::RED_BYTES);
-  uint64_t* emptyA = fullA + C::NA;
-  uint64_t* convd = emptyA + C::NA;
-  uint64_t* freeB = convd + WP_NB;
-  uint64_t* accf = freeB + WP_NB;  // [2]
+  uint8_t* ring = smem;                                         // [NS][W block | limb tile]
+  float* red = reinterpret_cast<float*>(smem + C::NS * C::STAGE);  // [MP][129], S == 1 only
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE + C::RED_BYTES);
+  uint64_t* empty = full + C::NS;
+  uint64_t* accf = empty + C::NS;  // [2]
   uint64_t* acce = accf + 2;       // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -190,19 +191,15 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
   const int tiles = p.N / 128;
   const int ntile = tiles > group ? (tiles - group + args.groups - 1) / args.groups : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkb_all = p.K / 64;
+  const int nkb_all = p.K / 128;
   const int kb0 = split * nkb_all / S;
   const int nkb = (split + 1) * nkb_all / S - kb0;
   const int total = ntile * nkb;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::NA; ++s) {
-      mbar_init(&fullA[s], 1);
-      mbar_init(&emptyA[s], 1);
-    }
-    for (int s = 0; s < WP_NB; ++s) {
-      mbar_init(&convd[s], WP_NCW);
-      mbar_init(&freeB[s], 1);
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
@@ -226,18 +223,17 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
       for (int it = 0; it < total; ++it) {
         const int ti = it / nkb, kb = it - ti * nkb;
         const int tile = group + ti * args.groups;
-        const int s = it % C::NA;
-        if (!mbar_wait(&emptyA[s], ((it / C::NA) & 1) ^ 1, args.err, abort_flag)) break;
-        uint8_t* st = ringA + s * C::A_STAGE;
-        mbar_arrive_expect_tx(&fullA[s], C::A_STAGE);
-        bulk_load(st + C::X_BYTES, args.w_tiles + ((size_t)tile * nkb_all + kb0 + kb) * WP_W8, WP_W8,
-                  &fullA[s]);
-        tma_load_2d(st, &map_x, &fullA[s], (kb0 + kb) * 64, 0);
+        const int s = it % C::NS;
+        if (!mbar_wait(&empty[s], ((it / C::NS) & 1) ^ 1, args.err, abort_flag)) break;
+        uint8_t* st = ring + s * C::STAGE;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        bulk_load(st, args.w_tiles + ((size_t)tile * nkb_all + kb0 + kb) * WI_WB, WI_WB, &full[s]);
+        tma_load_2d(st + WI_WB, &map_x, &full[s], (kb0 + kb) * 128, 0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(128, MP, 0);
+      constexpr uint32_t idesc = umma_idesc_s8(128, C::NB);
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < ntile && ok; ++ti) {
@@ -246,63 +242,42 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
         tc_fence_after();
         const uint32_t acc = tmem + b * C::ACC_COLS;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int sa = it % C::NA, sb = it % WP_NB;
-          if (!mbar_wait(&convd[sb], (it / WP_NB) & 1, args.err, abort_flag)) { ok = false; break; }
+          const int s = it % C::NS;
+          if (!mbar_wait(&full[s], (it / C::NS) & 1, args.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(ringB + sb * WP_WF));
-          const uint64_t bdesc = umma_desc_sw128(smem_u32(ringA + sa * C::A_STAGE));
+          const uint64_t adesc = umma_desc_sw128(smem_u32(ring + s * C::STAGE));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(ring + s * C::STAGE + WI_WB));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
-          umma_commit(&emptyA[sa]);
-          umma_commit(&freeB[sb]);
+          for (int k = 0; k < 4; ++k) umma_i8(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[s]);
         }
         umma_commit(&accf[b]);
       }
     }
-  } else if (warp < 2 + WP_NCW) {
-    // converters: piece c = 128*i + t is 16 int8 of row c/4, k 16*(c%4) .. +15;
-    // reads are consecutive 16-byte pieces and the two 16-byte f16 writes of a
-    // quarter-warp land on 8 distinct swizzled slots: no bank conflicts.
-    const int t = threadIdx.x - 64;  // 0 .. 32*NCW-1
-    for (int it = 0; it < total; ++it) {
-      const int sa = it % C::NA, sb = it % WP_NB;
-      if (!mbar_wait(&fullA[sa], (it / C::NA) & 1, args.err, abort_flag)) break;
-      if (!mbar_wait(&freeB[sb], ((it / WP_NB) & 1) ^ 1, args.err, abort_flag)) break;
-      const uint32_t src = smem_u32(ringA + sa * C::A_STAGE + C::X_BYTES);
-      const uint32_t dstb = smem_u32(ringB + sb * WP_WF);
-#pragma unroll
-      for (int i = 0; i < 512 / (32 * WP_NCW); ++i) {
-        const int c = i * 32 * WP_NCW + t;
-        const int r = c >> 2, ch = c & 3;
-        uint4 lo, hi;
-        i8x16_to_f16x16(lds128_u(src + c * 16), lo, hi);
-        const uint32_t dst = dstb + r * 128;
-        sts128_u(dst + (((2 * ch) ^ (r & 7)) << 4), lo);
-        sts128_u(dst + (((2 * ch + 1) ^ (r & 7)) << 4), hi);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&convd[sb]);
-    }
   } else {
     // epilogue warps -> TMEM lane quadrant warp % 4 (= channels q*32 ..)
     const int q = warp & 3;
-    const int et = threadIdx.x - 32 * (2 + WP_NCW);  // 0..127
+    const int et = threadIdx.x - 64;  // 0..127
     constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;
     for (int ti = 0; ti < ntile; ++ti) {
       const int b = ti & 1;
       const int tile = group + ti * args.groups;
       if (!mbar_wait(&accf[b], (ti >> 1) & 1, args.err, abort_flag)) break;
       tc_fence_after();
-      uint32_t r[MP];
+      // accumulator column l * MP + m holds limb l of row m: recombine
+      float r[MP];
+      const uint32_t tb = tmem + b * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
 #pragma unroll
       for (int c0 = 0; c0 < MP; c0 += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + b * C::ACC_COLS + ((uint32_t)(q * 32) << 16) + c0, rr);
+        uint32_t a0[32], a1[32], a2[32];
+        tmem_ld32(tb + c0, a0);
+        tmem_ld32(tb + MP + c0, a1);
+        tmem_ld32(tb + 2 * MP + c0, a2);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e)
-          if (c0 + e < MP) r[c0 + e] = rr[e];
+          if (c0 + e < MP)
+            r[c0 + e] = fmaf((float)(int)a2[e], 16384.f, fmaf((float)(int)a1[e], 128.f, (float)(int)a0[e]));
       }
       tc_fence_before();
       __syncwarp();
@@ -311,7 +286,7 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
       if (S == 1) {
         // own tile: stage the accumulator in shared memory rows and run the epilogue
 #pragma unroll
-        for (int m = 0; m < MP; ++m) red[m * 129 + ch] = __uint_as_float(r[m]);
+        for (int m = 0; m < MP; ++m) red[m * 129 + ch] = r[m];
         named_bar(1, 128);
         for (int m = q; m < p.M; m += 4) {
           float v[4], u[4];
@@ -327,7 +302,7 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
         // split partial -> global [tile][split][m][128], coalesced per row
         float* dst = args.part + ((size_t)tile * S + split) * MP * 128;
 #pragma unroll
-        for (int m = 0; m < MP; ++m) dst[m * 128 + ch] = __uint_as_float(r[m]);
+        for (int m = 0; m < MP; ++m) dst[m * 128 + ch] = r[m];
         __threadfence();
         named_bar(1, 128);
         if (et == 0) *last_flag = (atomicAdd(args.counters + tile, 1) == S - 1);
@@ -385,23 +360,149 @@ __global__ void __launch_bounds__(WP_THREADS, 1)
   }
 }
 
-// ------------------------------------------------------------------ tile packing
+// ------------------------------------------------------------------ weight packing
 // Source row r (int8 [n_src, K] row-major) becomes output channel
 // d = (r / grp) * gstride + r % grp + base (concatenation / gate|up interleave)
-// and is stored tile-major: [d / 128][kb][d % 128][64 B], so the 8 KB of
-// every (128-channel tile, k64) block is contiguous.
+// and is stored tile-major, [d / 128][k / 128][d % 128][128 B], with the
+// 16-byte chunk j of row d % 128 at position j ^ (d % 8): every (tile, k128)
+// block is one contiguous 16 KB run already in the UMMA 128-byte swizzle.
 __global__ void w8_tilepack_kernel(const int8_t* __restrict__ src, int n_src, int K,
                                    int8_t* __restrict__ dst, int grp, int gstride, int base) {
   const int cpr = K / 16;
-  const int nkb = K / 64;
+  const int nkb = K / 128;
   const size_t total = (size_t)n_src * cpr;
   for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
        idx += (size_t)gridDim.x * blockDim.x) {
     const int r = idx / cpr, c = idx % cpr;
     const int d = (r / grp) * gstride + r % grp + base;
-    const int kb = c / 4, piece = c % 4;
-    const size_t off = (((size_t)(d / 128) * nkb + kb) * 128 + d % 128) * 64 + piece * 16;
+    const int kb = c / 8, j = c % 8, row = d % 128;
+    const size_t off = (((size_t)(d / 128) * nkb + kb) * 128 + row) * 128 + ((j ^ (row & 7)) << 4);
     *reinterpret_cast<uint4*>(dst + off) = reinterpret_cast<const uint4*>(src + (size_t)r * K)[c];
+  }
+}
+
+// ------------------------------------------------------------------ activation limbs
+// Limb layout of one launch: int8 [3][MP][K] (limb-major), rows M..MP-1 zero,
+// plus the fp32 row scale 2^(e_m - 20) with max|x_m| < 2^e_m.
+__device__ __forceinline__ void limbs_of(float x, float up, int8_t& l0, int8_t& l1, int8_t& l2) {
+  const int qv = __float2int_rn(x * up);   // exact scaling by a power of two, |qv| < 2^20
+  const int x0 = ((qv + 64) & 127) - 64;
+  const int r1 = (qv - x0) / 128;          // exact
+  const int x1 = ((r1 + 64) & 127) - 64;
+  l0 = (int8_t)x0;
+  l1 = (int8_t)x1;
+  l2 = (int8_t)((r1 - x1) / 128);
+}
+
+__device__ __forceinline__ float block_max(float v, float* sh) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    t = warp_max(t);
+    if (threadIdx.x == 0) sh[32] = t;
+  }
+  __syncthreads();
+  return sh[32];
+}
+
+// f16 rows -> limbs; one CTA per (padded) row
+__global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int K,
+                                int8_t* __restrict__ xl, float* __restrict__ xscale) {
+  __shared__ float sh[33];
+  const int m = blockIdx.x;
+  int8_t* o0 = xl + (size_t)m * K;
+  int8_t* o1 = o0 + (size_t)MP * K;
+  int8_t* o2 = o1 + (size_t)MP * K;
+  if (m >= M) {
+    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+      *reinterpret_cast<uint32_t*>(o0 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(o1 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(o2 + k) = 0u;
+    }
+    if (threadIdx.x == 0) xscale[m] = 1.f;
+    return;
+  }
+  const __half* row = x + (size_t)m * K;
+  float mx = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+  }
+  int e;
+  frexpf(block_max(mx, sh), &e);
+  const float up = ldexpf(1.f, 20 - e);
+  if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
+  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    const float v[4] = {a.x, a.y, b.x, b.y};
+    int8_t l[3][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
+    *reinterpret_cast<char4*>(o0 + k) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
+    *reinterpret_cast<char4*>(o1 + k) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
+    *reinterpret_cast<char4*>(o2 + k) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
+  }
+}
+
+// RMSNorm of the residual rows (h fp32, sum of squares from hstat partials)
+// rounded to f16 like the reference's activations, then split into limbs
+__global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
+                                     int hparts, int M, int MP, int K, const float* __restrict__ w,
+                                     float eps, int8_t* __restrict__ xl, float* __restrict__ xscale) {
+  __shared__ float sh[33];
+  const int m = blockIdx.x;
+  int8_t* o0 = xl + (size_t)m * K;
+  int8_t* o1 = o0 + (size_t)MP * K;
+  int8_t* o2 = o1 + (size_t)MP * K;
+  if (m >= M) {
+    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+      *reinterpret_cast<uint32_t*>(o0 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(o1 + k) = 0u;
+      *reinterpret_cast<uint32_t*>(o2 + k) = 0u;
+    }
+    if (threadIdx.x == 0) xscale[m] = 1.f;
+    return;
+  }
+  float ss = 0.f;
+  for (int qq = threadIdx.x; qq < hparts; qq += blockDim.x) ss += hstat[(size_t)qq * M + m];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) sh[32] = rsqrtf(t / static_cast<float>(K) + eps);
+  }
+  __syncthreads();
+  const float rstd = sh[32];
+  __syncthreads();
+  const float* row = h + (size_t)m * K;
+  auto xval = [&](int k, float hv) { return __half2float(__float2half_rn(hv * rstd * __ldg(w + k))); };
+  float mx = 0.f;
+  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    const float4 hv = *reinterpret_cast<const float4*>(row + k);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xval(k, hv.x)), fabsf(xval(k + 1, hv.y))),
+                         fmaxf(fabsf(xval(k + 2, hv.z)), fabsf(xval(k + 3, hv.w)))));
+  }
+  int e;
+  frexpf(block_max(mx, sh), &e);
+  const float up = ldexpf(1.f, 20 - e);
+  if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
+  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    const float4 hv = *reinterpret_cast<const float4*>(row + k);
+    const float v[4] = {xval(k, hv.x), xval(k + 1, hv.y), xval(k + 2, hv.z), xval(k + 3, hv.w)};
+    int8_t l[3][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
+    *reinterpret_cast<char4*>(o0 + k) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
+    *reinterpret_cast<char4*>(o1 + k) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
+    *reinterpret_cast<char4*>(o2 + k) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
   }
 }
 
@@ -423,28 +524,29 @@ static EncodeTiledFn2 encode_fn() {
   return fn;
 }
 
-static bool map_f16_rows(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
+// limb tensor int8 [rows][K], box [rows][128 B] with the 128-byte swizzle
+static bool map_i8_rows(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
   EncodeTiledFn2 enc = encode_fn();
-  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
+  if (!enc || (reinterpret_cast<uintptr_t>(base) & 15) || K % 128 || rows > 256) return false;
   cuuint64_t dims[2] = {K, rows};
-  cuuint64_t strides[1] = {K * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  cuuint64_t strides[1] = {K};
+  cuuint32_t box[2] = {128, (cuuint32_t)rows};
   cuuint32_t es[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // K-split S in 1..8 and groups = floor(SMs / S) from a small cost model:
-// a tile slice streams nkb/S blocks of 8 KB at ~45 GB/s per SM; with S > 1
+// a tile slice streams nkb/S blocks of 16 KB at ~42 GB/s per SM; with S > 1
 // every tile also pays a split-K merge (~4 us, hidden behind the next tile's
 // stream when that is longer, exposed once at the end).
 void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups) {
-  const int tiles = N / 128, nkb = K / 64;
-  const double t_kb = 8192.0 / 45e3;  // us per k64 block per SM
+  const int tiles = N / 128, nkb = K / 128;
+  const double t_kb = 16384.0 / 42e3;  // us per k128 block per SM
   double best = 1e30;
   int bs = 1, bg = num_sms < tiles ? num_sms : tiles;
-  for (int s = 1; s <= 8 && s <= nkb / 2; ++s) {
+  for (int s = 1; s <= 8 && s <= nkb; ++s) {
     int g = num_sms / s;
     if (g > tiles) g = tiles;
     if (g < 1) break;
@@ -466,27 +568,28 @@ size_t w8tc_part_floats(int N, int K, int M, int num_sms) {
 }
 
 template <int MP, int MODE>
-static cudaError_t w8p_launch_t(const CUtensorMap& mx, const WpArgs& a, cudaStream_t st) {
-  using C = WpCfg<MP>;
+static cudaError_t w8i_launch_t(const CUtensorMap& mx, const WiArgs& a, cudaStream_t st) {
+  using C = WiCfg<MP>;
   const size_t smem = C::SMEM;
-  auto kern = w8p_kernel<MP, MODE>;
+  auto kern = w8i_kernel<MP, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<a.groups * a.p.splits, WP_THREADS, smem, st>>>(mx, a);
+  kern<<<a.groups * a.p.splits, WI_THREADS, smem, st>>>(mx, a);
   return cudaGetLastError();
 }
 
 template <int MODE>
-static cudaError_t w8p_mode(const CUtensorMap& mx, const WpArgs& a, int mp, cudaStream_t st) {
-  if (mp == 16) return w8p_launch_t<16, MODE>(mx, a, st);
-  if (mp == 32) return w8p_launch_t<32, MODE>(mx, a, st);
-  if (mp == 48) return w8p_launch_t<48, MODE>(mx, a, st);
-  return w8p_launch_t<64, MODE>(mx, a, st);
+static cudaError_t w8i_mode(const CUtensorMap& mx, const WiArgs& a, int mp, cudaStream_t st) {
+  if (mp == 16) return w8i_launch_t<16, MODE>(mx, a, st);
+  if (mp == 32) return w8i_launch_t<32, MODE>(mx, a, st);
+  if (mp == 48) return w8i_launch_t<48, MODE>(mx, a, st);
+  return w8i_launch_t<64, MODE>(mx, a, st);
 }
 
 cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& pin, int mode, int* err, float* part,
                         size_t part_floats, int* counters, int num_sms, cudaStream_t st) {
-  if (pin.M < 1 || pin.M > 64 || pin.N % 128 || pin.K % 128) return cudaErrorInvalidValue;
+  if (pin.M < 1 || pin.M > 64 || pin.N % 128 || pin.K % 128 || !pin.xl || !pin.xscale)
+    return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(w_tiles) & 15) return cudaErrorInvalidValue;
   W8Params p = pin;
   int groups = 1;
@@ -495,19 +598,34 @@ cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& pin, int mode, in
   if (p.splits > 1 && (!part || !counters || part_floats < (size_t)(p.N / 128) * p.splits * mp * 128))
     return cudaErrorInvalidValue;
   CUtensorMap mx;
-  if (!map_f16_rows(&mx, p.x, p.K, p.M, mp)) return cudaErrorInvalidValue;
-  WpArgs a{p, w_tiles, part, counters, groups, err};
-  if (mode == kQKV) return w8p_mode<kQKV>(mx, a, mp, st);
-  if (mode == kResid) return w8p_mode<kResid>(mx, a, mp, st);
-  if (mode == kSiluMul) return w8p_mode<kSiluMul>(mx, a, mp, st);
-  if (mode == kStore) return w8p_mode<kStore>(mx, a, mp, st);
+  if (!map_i8_rows(&mx, p.xl, p.K, 3 * mp)) return cudaErrorInvalidValue;
+  WiArgs a{p, w_tiles, part, counters, groups, err};
+  if (mode == kQKV) return w8i_mode<kQKV>(mx, a, mp, st);
+  if (mode == kResid) return w8i_mode<kResid>(mx, a, mp, st);
+  if (mode == kSiluMul) return w8i_mode<kSiluMul>(mx, a, mp, st);
+  if (mode == kStore) return w8i_mode<kStore>(mx, a, mp, st);
   return cudaErrorInvalidValue;
 }
 
 cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst, int grp, int gstride,
                                int base, cudaStream_t st) {
-  if (K % 64) return cudaErrorInvalidValue;
+  if (K % 128) return cudaErrorInvalidValue;
   w8_tilepack_kernel<<<1024, 256, 0, st>>>(src, n_src, K, dst, grp, gstride, base);
+  return cudaGetLastError();
+}
+
+cudaError_t w8_limbs_launch(const __half* x, int M, int K, int8_t* xl, float* xscale, cudaStream_t st) {
+  if (M < 1 || M > 64 || K % 128) return cudaErrorInvalidValue;
+  const int mp = (M + 15) / 16 * 16;
+  w8_limbs_kernel<<<mp, 256, 0, st>>>(x, M, mp, K, xl, xscale);
+  return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, int hparts, int M, int K,
+                                 const float* w, float eps, int8_t* xl, float* xscale, cudaStream_t st) {
+  if (M < 1 || M > 64 || K % 128) return cudaErrorInvalidValue;
+  const int mp = (M + 15) / 16 * 16;
+  rmsnorm_limbs_kernel<<<mp, 256, 0, st>>>(h, hstat, hparts, M, mp, K, w, eps, xl, xscale);
   return cudaGetLastError();
 }
 
