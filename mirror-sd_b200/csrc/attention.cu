@@ -281,6 +281,12 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
   pk.y = pack_f16x2(acc[2] * inv, acc[3] * inv);
   *reinterpret_cast<uint2*>(out + ((size_t)bi * p.block + j) * ((size_t)p.nq * 128) +
                             (size_t)head * 128 + lane * 4) = pk;
+  if (p.omax) {  // per (head, row) max |out| for the o-projection's limb split
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&pk.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&pk.y));
+    const float mx = warp_max(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+    if (lane == 0) p.omax[(size_t)head * gridDim.y * p.block + (size_t)bi * p.block + j] = mx;
+  }
 }
 
 size_t attn_smem_bytes(int nq, int nkv, int block) {
@@ -312,10 +318,12 @@ cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_
   cudaError_t e = cudaFuncSetAttribute(attn_partial_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  DFL_TRY(max_smem_carveout(attn_partial_kernel));
   attn_partial_kernel<<<dim3(p.splits, p.nkv, batch), nwarps * 32, smem, st>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int rows = p.nq * p.block;
+  DFL_TRY(max_smem_carveout(attn_combine_kernel));
   attn_combine_kernel<<<dim3((rows + 7) / 8, batch), 256, 0, st>>>(p, out);
   return cudaGetLastError();
 }

@@ -256,6 +256,22 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Every kernel of the draft path asks for the largest shared-memory carveout:
+// the step alternates kernels that need ~200 KB of shared memory with small
+// ones, and a launch whose carveout differs from the running one makes the SM
+// reconfigure its L1 / shared split first.
+#define DFL_TRY(call)                      \
+  do {                                     \
+    const cudaError_t e_ = (call);         \
+    if (e_ != cudaSuccess) return e_;      \
+  } while (0)
+
+template <class Kern>
+inline cudaError_t max_smem_carveout(Kern* kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              (int)cudaSharedmemCarveoutMaxShared);
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

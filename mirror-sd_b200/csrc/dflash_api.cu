@@ -90,6 +90,8 @@ struct Handle {
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
   int8_t* xl = nullptr;             // projection input limbs [3][64][max(H, NQ*128, I)]
   float* xs = nullptr;              // their row scales [64]
+  float* hmax = nullptr;            // [H/128, Mx] partial max |h * next norm weight|
+  float* amax = nullptr;            // [max(NQ, 2I/128), Mx] partial max |attention out| / |act|
   float *opart = nullptr, *mpart = nullptr, *lpart = nullptr;
   size_t attn_part_rows = 0;
   __nv_bfloat16* hn = nullptr;
@@ -298,6 +300,8 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->act, (size_t)Mx * I));
   CKC(A.alloc(&hd->xl, (size_t)3 * 64 * std::max(std::max(H, NQ * 128), I)));
   CKC(A.alloc(&hd->xs, 64));
+  CKC(A.alloc(&hd->hmax, (size_t)(H / 128) * Mx));
+  CKC(A.alloc(&hd->amax, (size_t)std::max(NQ, 2 * I / 128) * Mx));
   // the split count never exceeds what the longest rows give, and a cache can
   // make rows longer than max_ctx + max_block: size for any length
   hd->attn_part_rows = attn_rows_capacity(d.max_batch, NKV, G * d.max_block, 1 << 28, hd->num_sms);
@@ -455,7 +459,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
 
   CK(mark(0));
   CK(rope_table_map_launch(m, B, hd->inv_freq, hd->rope, st));
-  CK(init_h_launch(reinterpret_cast<const __nv_bfloat16*>(a->noise), M, H, hd->h, hd->hstat, st));
+  CK(init_h_launch(reinterpret_cast<const __nv_bfloat16*>(a->noise), M, H, hd->h, hd->hstat,
+                   hd->layers[0].in_norm, hd->hmax, st));
   launches += 2;
   CK(mark(1));
 
@@ -492,7 +497,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     __half* Kl = Kbase + l * layer_stride;
     __half* Vl = Vbase + l * layer_stride;
     // q | k | v of the block rows: input RMSNorm fused into the activation load
-    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xl, hd->xs, st));
+    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hd->hmax, hparts, M, H, ly.in_norm, d.rms_norm_eps,
+                            hd->xl, hd->xs, st));
     W8Params p{};
     p.scale = ly.s_qkv; p.N = (NQ + 2 * NKV) * 128; p.K = H; p.M = M;
     p.xl = hd->xl; p.xscale = hd->xs; p.eps = d.rms_norm_eps;
@@ -508,25 +514,31 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     ap.scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
     ap.normrope = 0;
     ap.kv = m;
+    ap.omax = hd->amax;
     CK(attn_launch(ap, b, hd->attn_out, st));
     // o_proj + residual
     W8Params o{};
-    CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->xl, hd->xs, st));
+    CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->amax, NQ, hd->xl, hd->xs, st));
     o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.xl = hd->xl; o.xscale = hd->xs;
-    o.h_out = hd->h; o.hstat_out = hd->hstat;
+    o.h_out = hd->h; o.hstat_out = hd->hstat; o.hmax_out = hd->hmax; o.next_norm = ly.post_norm;
     CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     hparts = H / 128;
     // gate|up with post-attention RMSNorm fused, silu(g)*u epilogue
-    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xl, hd->xs, st));
+    CK(rmsnorm_limbs_launch(hd->h, hd->hstat, hd->hmax, hparts, M, H, ly.post_norm, d.rms_norm_eps,
+                            hd->xl, hd->xs, st));
     W8Params gu{};
     gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
-    gu.xl = hd->xl; gu.xscale = hd->xs; gu.act = hd->act;
+    gu.xl = hd->xl; gu.xscale = hd->xs; gu.act = hd->act; gu.amax_out = hd->amax;
     CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     // down + residual
     W8Params dn{};
-    CK(w8_limbs_launch(hd->act, M, I, hd->xl, hd->xs, st));
+    CK(w8_limbs_launch(hd->act, M, I, hd->amax, 2 * I / 128, hd->xl, hd->xs, st));
     dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.xl = hd->xl; dn.xscale = hd->xs;
     dn.h_out = hd->h; dn.hstat_out = hd->hstat;
+    if (l + 1 < nl) {  // the next layer's input RMSNorm reads h
+      dn.hmax_out = hd->hmax;
+      dn.next_norm = hd->layers[l + 1].in_norm;
+    }
     CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     launches += 10;  // 2 norms + 2 limb splits, qkv, attention partial + combine, o, gate|up, down
   }
@@ -727,7 +739,7 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   float* xs = nullptr;
   CK(cudaMallocAsync(&xl, (size_t)3 * 64 * K, st));
   CK(cudaMallocAsync(&xs, 64 * sizeof(float), st));
-  CK(w8_limbs_launch(reinterpret_cast<const __half*>(x), M, K, xl, xs, st));
+  CK(w8_limbs_launch(reinterpret_cast<const __half*>(x), M, K, nullptr, 0, xl, xs, st));
   W8Params p{};
   p.scale = sp; p.N = N; p.K = K; p.M = M;
   p.xl = xl; p.xscale = xs; p.y = reinterpret_cast<__half*>(y);

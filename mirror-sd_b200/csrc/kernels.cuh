@@ -65,14 +65,17 @@ enum W8Mode : int { kStore = 0, kQKV = 1, kResid = 2, kSiluMul = 3 };
 struct W8Params {
   const float* scale;     // [N] fp32 per-output-channel scale (from the fp16 scale)
   int N, K, M;            // M = activation rows (batch * block)
-  int splits;             // K splits (set by w8tc_launch)
+  int splits;             // grid size (set by w8tc_launch)
   const int8_t* xl;       // activation limbs [3][MP][K]
   const float* xscale;    // [MP] row scales (powers of two)
   // outputs
   __half* y;              // kStore: [M, N]
   float* h_out;           // kResid: [M, N] (in place residual)
-  float* hstat_out;       // kResid: [N/128, M]
+  float* hstat_out;       // kResid: [N/128, M] partial sums of h^2
+  float* hmax_out;        // kResid: [N/128, M] partial max |h * next_norm| (or NULL)
+  const float* next_norm; // kResid: weight of the RMSNorm that reads h next
   __half* act;            // kSiluMul: [M, N/2]
+  float* amax_out;        // kSiluMul: [N/128, M] partial max |act| (or NULL)
   // kQKV
   __half* q_out;          // [b, NQ, B, 128]
   __half* k_out;          // this layer's K store [seq][NKV][kv.slots][128] (KvMap)
@@ -102,6 +105,7 @@ struct AttnParams {
   float eps;
   int q_row0, k_row0;   // table rows: q row j -> q_row0 + j, k row i -> k_row0 + i
   KvMap kv;             // nseq > 0: sequence s reads logical rows [0, n_att[s]) at rs_post[s]
+  float* omax;          // combine: [NQ, b * block] max |out| per head and row (or NULL)
 };
 
 enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2 };
@@ -136,10 +140,15 @@ struct LmParams {
 // tcgen05 W8A16 path (w8_tc.cu): w_tiles is the int8 weight packed by
 // w8_tilepack_launch ([N/128][K/128][128][128 B], swizzled); part / counters
 // are the split-K scratch (w8tc_part_floats floats; counters zero, one per tile).
-cudaError_t w8_limbs_launch(const __half* x, int M, int K, int8_t* xl, float* xscale, cudaStream_t st);
-cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, int hparts, int M, int K,
-                                 const float* w, float eps, int8_t* xl, float* xscale, cudaStream_t st);
-void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups);
+// maxpart: [nparts, M] partial row maxima of |x| from the producer (or NULL:
+// the kernel finds the maxima itself, one CTA per row)
+cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart, int nparts,
+                            int8_t* xl, float* xscale, cudaStream_t st);
+// x = f16(h * rsqrt(mean h^2 + eps) * w) -> limbs; hstat / hmax: [hparts, M]
+// partial sums of h^2 and partial maxima of |h * w|
+cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float* hmax, int hparts,
+                                 int M, int K, const float* w, float eps, int8_t* xl, float* xscale,
+                                 cudaStream_t st);
 size_t w8tc_part_floats(int N, int K, int M, int num_sms);
 cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& p, int mode, int* err, float* part,
                         size_t part_floats, int* counters, int num_sms, cudaStream_t st);
@@ -173,7 +182,7 @@ cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2*
 cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
                                   cudaStream_t st);
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
-                          cudaStream_t st);
+                          const float* w, float* hmax, cudaStream_t st);
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st);
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,

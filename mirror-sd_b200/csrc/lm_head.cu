@@ -304,6 +304,7 @@ static cudaError_t lm_tc_t(const CUtensorMap& mh, const LmParams& p, const uint8
   const size_t smem = (size_t)LT_NS * (LT_E_BYTES + MP * 128) + 1024 + 256 + 8 * 64 * 4;
   cudaError_t e = cudaFuncSetAttribute(lm_tc_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  DFL_TRY(max_smem_carveout(lm_tc_kernel<MP>));
   lm_tc_kernel<MP><<<grid, LT_THREADS, smem, st>>>(mh, p, et, per, err);
   return cudaGetLastError();
 }
@@ -337,6 +338,7 @@ cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int
                                  int batch, int32_t* out_tokens, const int32_t* target,
                                  int32_t* acc_len, int32_t* correction, cudaStream_t st) {
   if (block < 2 || block > 1024) return cudaErrorInvalidValue;
+  DFL_TRY(max_smem_carveout(argmax_accept_kernel));
   argmax_accept_kernel<<<batch, 32 * (block - 1 < 32 ? block - 1 : 32), 0, st>>>(
       bv, bi, nparts, M, block, out_tokens, target, acc_len, correction);
   return cudaGetLastError();
@@ -345,6 +347,7 @@ cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int
 cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch, int block,
                           int32_t* acc_len, int32_t* correction, cudaStream_t st) {
   if (block < 2 || batch < 1) return cudaErrorInvalidValue;
+  DFL_TRY(max_smem_carveout(accept_kernel));
   accept_kernel<<<(batch + 127) / 128, 128, 0, st>>>(draft, target, batch, block, acc_len, correction);
   return cudaGetLastError();
 }

@@ -44,15 +44,20 @@ __global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
   out[idx] = make_float2(cs, sn);
 }
 
-// one warp per row
+// h = noise (fp32) with its sum of squares and max |h * w| (w: the first
+// layer's input RMSNorm weight) for the limb split of the first projection;
+// one CTA per row
 __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, int H,
-                              float* __restrict__ h, float* __restrict__ hstat) {
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;
-  float ss = 0.f;
-  for (int k = lane * 8; k < H; k += 256) {
+                              float* __restrict__ h, float* __restrict__ hstat,
+                              const float* __restrict__ w, float* __restrict__ hmax) {
+  __shared__ float red[2][32];
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float ss = 0.f, mw = 0.f;
+  for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
     const uint4 v = *reinterpret_cast<const uint4*>(noise + (size_t)row * H + k);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + k));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + k + 4));
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
     float f[8];
 #pragma unroll
@@ -64,11 +69,31 @@ __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, in
     float4* dst = reinterpret_cast<float4*>(h + (size_t)row * H + k);
     dst[0] = make_float4(f[0], f[1], f[2], f[3]);
     dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    for (int e = 0; e < 8; ++e) {
+      ss += f[e] * f[e];
+      mw = fmaxf(mw, fabsf(f[e] * wv[e]));
+    }
   }
   ss = warp_sum(ss);
-  if (lane == 0) hstat[row] = ss;
+  mw = warp_max(mw);
+  if (lane == 0) {
+    red[0][warp] = ss;
+    red[1][warp] = mw;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    float a = lane < nw ? red[0][lane] : 0.f;
+    float b = lane < nw ? red[1][lane] : 0.f;
+    a = warp_sum(a);
+    b = warp_max(b);
+    if (lane == 0) {
+      hstat[row] = a;
+      hmax[row] = b;
+    }
+  }
 }
 
 // ctx_out[r, k] = f16(raw[r, k] * rsqrt(sum_p part[p, r] / H + eps) * w[k]); one CTA per row
@@ -145,6 +170,7 @@ __global__ void f16_to_f32_kernel(const __half* __restrict__ src, size_t n, floa
 
 cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st) {
   if (rows < 1) return cudaSuccess;
+  DFL_TRY(max_smem_carveout(rope_table_kernel));
   rope_table_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(pos0, rows, inv_freq, out);
   return cudaGetLastError();
 }
@@ -153,18 +179,21 @@ cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_fr
                                   cudaStream_t st) {
   if (m.nseq < 1 || m.nseq > kKvMaxSeq || block < 1) return cudaErrorInvalidValue;
   const int rows = m.ctx_start[m.nseq] + m.nseq * block;
+  DFL_TRY(max_smem_carveout(rope_table_map_kernel));
   rope_table_map_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(m, block, rows, inv_freq, out);
   return cudaGetLastError();
 }
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
-                          cudaStream_t st) {
+                          const float* w, float* hmax, cudaStream_t st) {
   if (H % 8) return cudaErrorInvalidValue;
-  init_h_kernel<<<(M + 7) / 8, 256, 0, st>>>(noise, M, H, h, hstat);
+  DFL_TRY(max_smem_carveout(init_h_kernel));
+  init_h_kernel<<<M, 256, 0, st>>>(noise, M, H, h, hstat, w, hmax);
   return cudaGetLastError();
 }
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st) {
   if (H % 8 || rows < 1) return cudaErrorInvalidValue;
+  DFL_TRY(max_smem_carveout(ctx_norm_kernel));
   ctx_norm_kernel<<<rows, 256, 0, st>>>(raw, part, nparts, rows, H, w, eps, out);
   return cudaGetLastError();
 }
@@ -172,6 +201,9 @@ cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, in
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
                               cudaStream_t st) {
   if (H % 4) return cudaErrorInvalidValue;
+  const cudaError_t ce = out_f32 ? max_smem_carveout(final_norm_kernel<true>)
+                                 : max_smem_carveout(final_norm_kernel<false>);
+  if (ce != cudaSuccess) return ce;
   if (out_f32)
     final_norm_kernel<true><<<M, 256, 0, st>>>(h, hstat, hparts, M, H, w, eps, hn, out);
   else

@@ -260,6 +260,7 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid(p.N / TC_BN, (p.M + TC_BM - 1) / TC_BM);
+  DFL_TRY(max_smem_carveout(kern));
   kern<<<grid, TC_THREADS, TC_SMEM, st>>>(ma, mb, p);
   return cudaGetLastError();
 }

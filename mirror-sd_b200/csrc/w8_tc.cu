@@ -23,19 +23,28 @@
 // (MP = M padded to 16) are N.  One k128 block of a tile is
 // 4 x tcgen05.mma.kind::i8 M=128 N=3MP K=32.
 //
-// Persistent, one CTA per SM, 6 warps.  CTAs form groups of S (the K-split);
-// group g walks tiles g, g + groups, ... and CTA `split` of the group covers
-// the same K-slice of each of them.
+// Persistent, one CTA per SM, 6 warps.  A CTA works through "segments":
+// k-block ranges of one 128-channel tile accumulated into one TMEM buffer.
+// Two schedules share the kernel:
+//   split    CTAs form groups of S.  Group g takes tiles g, g + groups, ...;
+//            CTA `split` of the group takes the same K-slice of each of them.
+//   stream-K the U = tiles * K/128 (tile, k-block) units, tile-major, are cut
+//            into G equal contiguous runs, one per CTA.  A run covers whole
+//            tiles and at most two partial ones.
+// The host picks stream-K for long K (>= 64 k-blocks), where a split plan
+// leaves many partial tiles to merge at the end, and the split plan otherwise
+// (it was faster on the 40-block shapes of the 27B draft).
 //   warp 0   producer: the tile's k128 weight block, 16 KB, is one contiguous
 //            pre-swizzled run (cp.async.bulk); the limb tile [3MP x 128 B]
 //            arrives by TMA with the 128-byte swizzle.
 //   warp 1   single-thread UMMA issue into one of two int32 TMEM accumulators;
 //            tcgen05.commit frees ring stages.
-//   warps 2-5 epilogue of the previous tile while the next one streams.  With
-//            S > 1, each CTA writes its fp32 partial to global scratch; the
-//            last CTA of the tile (per-tile arrival counter) sums the S
-//            partials in split order (deterministic) and runs the fused
-//            epilogue:
+//   warps 2-5 epilogue of the previous segment while the next one streams.  A
+//            segment that is a whole tile goes straight to the fused
+//            epilogue.  Otherwise the CTA writes its fp32 partial to the
+//            tile's slot in global scratch; the last of the tile's CTAs
+//            (per-tile arrival counter) sums the partials in slot order
+//            (deterministic) and runs the fused epilogue:
 //     kStore   : Y as f16
 //     kQKV     : per-head RMSNorm + neox RoPE for q and k heads, plain v,
 //                written into the KvMap K/V layout (dflash.py:290-305)
@@ -45,6 +54,8 @@
 //                channels -> silu(g) * u (dflash.py:330)
 // Every mbarrier wait is bounded; a timeout raises the device error word and
 // the CTA unwinds (TMEM released on every path).
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace dfl {
@@ -97,10 +108,66 @@ __device__ __forceinline__ void rope_lane_t(float (&y)[4], int lane, const float
 struct WiArgs {
   W8Params p;
   const int8_t* w_tiles;  // [N/128][K/128][128 rows][128 B], 16-byte chunks swizzled
-  float* part;            // [tiles][S][MP][128] fp32 split partials (S > 1)
+  float* part;            // [tiles][maxseg][MP][128] fp32 partials of split tiles
   int* counters;          // [tiles] arrival counters, zero between launches
-  int groups;             // grid = groups * S
+  int maxseg;             // partial slots per tile (<= 8)
+  int stream_k;           // 1: stream-K runs; 0: split plan (S = p.splits, groups)
+  int groups;
   int* err;
+};
+
+// stream-K: CTA c of G owns units [c U / G, (c + 1) U / G)
+__host__ __device__ __forceinline__ int sk_begin(int c, long long U, int G) {
+  return (int)((long long)c * U / G);
+}
+__host__ __device__ __forceinline__ int sk_owner(int u, long long U, int G) {
+  int o = (int)((long long)u * G / U);
+  while (o + 1 < G && sk_begin(o + 1, U, G) <= u) ++o;
+  while (o > 0 && sk_begin(o, U, G) > u) --o;
+  return o;
+}
+
+// segment i of CTA c: tile, k-block range [kb_lo, kb_hi], the CTA's slot among
+// the tile's contributors and their number
+struct Seg {
+  int tile, kb_lo, kb_hi, slot, n;
+};
+
+struct Sched {
+  int stream_k, nkb, tiles, G, S, groups;
+  long long U;
+  int u0, u1;  // stream-K run of this CTA
+  __host__ __device__ Sched(int sk, int N, int K, int G_, int S_, int groups_, int c)
+      : stream_k(sk), nkb(K / 128), tiles(N / 128), G(G_), S(S_), groups(groups_) {
+    U = (long long)tiles * nkb;
+    u0 = sk_begin(c, U, G);
+    u1 = sk_begin(c + 1, U, G);
+  }
+  __host__ __device__ int count(int c) const {
+    if (stream_k) return u1 > u0 ? (u1 - 1) / nkb - u0 / nkb + 1 : 0;
+    const int g = c / S;
+    return tiles > g ? (tiles - g + groups - 1) / groups : 0;
+  }
+  __host__ __device__ Seg get(int c, int i) const {
+    Seg sg;
+    if (stream_k) {
+      const int t0 = u0 / nkb, t1 = (u1 - 1) / nkb;
+      sg.tile = t0 + i;
+      sg.kb_lo = i == 0 ? u0 % nkb : 0;
+      sg.kb_hi = sg.tile == t1 ? (u1 - 1) % nkb : nkb - 1;
+      const int first = sk_owner(sg.tile * nkb, U, G);
+      sg.slot = c - first;
+      sg.n = sk_owner(sg.tile * nkb + nkb - 1, U, G) - first + 1;
+    } else {
+      const int split = c % S;
+      sg.tile = c / S + i * groups;
+      sg.kb_lo = split * nkb / S;
+      sg.kb_hi = (split + 1) * nkb / S - 1;
+      sg.slot = split;
+      sg.n = S;
+    }
+    return sg;
+  }
 };
 
 // Fused epilogue for one activation row m of tile `tile` (a warp; lane owns
@@ -128,6 +195,12 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
     float ss = hv.x * hv.x + hv.y * hv.y + hv.z * hv.z + hv.w * hv.w;
     ss = warp_sum(ss);
     if (lane == 0) p.hstat_out[(size_t)tile * p.M + m] = ss;
+    if (p.hmax_out) {
+      const float4 nw = __ldg(reinterpret_cast<const float4*>(p.next_norm + gch));
+      float mw = fmaxf(fmaxf(fabsf(hv.x * nw.x), fabsf(hv.y * nw.y)), fmaxf(fabsf(hv.z * nw.z), fabsf(hv.w * nw.w)));
+      mw = warp_max(mw);
+      if (lane == 0) p.hmax_out[(size_t)tile * p.M + m] = mw;
+    }
   } else if (MODE == kSiluMul) {
     float o[2];
 #pragma unroll
@@ -136,7 +209,13 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
       const float uv = u[e] * (__ldg(p.scale + gch + 64 + e) * rs);
       o[e] = (gv / (1.0f + expf(-gv))) * uv;
     }
-    *reinterpret_cast<uint32_t*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) = pack_f16x2(o[0], o[1]);
+    const uint32_t pk = pack_f16x2(o[0], o[1]);
+    *reinterpret_cast<uint32_t*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) = pk;
+    if (p.amax_out) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk));
+      const float mx = warp_max(fmaxf(fabsf(f.x), fabsf(f.y)));
+      if (lane == 0) p.amax_out[(size_t)tile * p.M + m] = mx;
+    }
   } else {  // kQKV: the tile is one head
     const int head = tile;
     const int bi = m / p.block, j = m - bi * p.block;
@@ -176,7 +255,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;                                         // [NS][W block | limb tile]
-  float* red = reinterpret_cast<float*>(smem + C::NS * C::STAGE);  // [MP][129], S == 1 only
+  float* red = reinterpret_cast<float*>(smem + C::NS * C::STAGE);  // [MP][129]
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE + C::RED_BYTES);
   uint64_t* empty = full + C::NS;
   uint64_t* accf = empty + C::NS;  // [2]
@@ -185,16 +264,11 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
-  const int S = p.splits;
-  const int group = blockIdx.x / S;
-  const int split = blockIdx.x % S;
-  const int tiles = p.N / 128;
-  const int ntile = tiles > group ? (tiles - group + args.groups - 1) / args.groups : 0;
+  const int nkb = p.K / 128;
+  const int c = blockIdx.x;
+  const Sched sch(args.stream_k, p.N, p.K, gridDim.x, p.splits, args.groups, c);
+  const int nseg = sch.count(c);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nkb_all = p.K / 128;
-  const int kb0 = split * nkb_all / S;
-  const int nkb = (split + 1) * nkb_all / S - kb0;
-  const int total = ntile * nkb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NS; ++s) {
@@ -220,15 +294,18 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int it = 0; it < total; ++it) {
-        const int ti = it / nkb, kb = it - ti * nkb;
-        const int tile = group + ti * args.groups;
-        const int s = it % C::NS;
-        if (!mbar_wait(&empty[s], ((it / C::NS) & 1) ^ 1, args.err, abort_flag)) break;
-        uint8_t* st = ring + s * C::STAGE;
-        mbar_arrive_expect_tx(&full[s], C::STAGE);
-        bulk_load(st, args.w_tiles + ((size_t)tile * nkb_all + kb0 + kb) * WI_WB, WI_WB, &full[s]);
-        tma_load_2d(st + WI_WB, &map_x, &full[s], (kb0 + kb) * 128, 0);
+      int it = 0;
+      bool ok = true;
+      for (int i = 0; i < nseg && ok; ++i) {
+        const Seg sg = sch.get(c, i);
+        for (int kb = sg.kb_lo; kb <= sg.kb_hi; ++kb, ++it) {
+          const int s = it % C::NS;
+          if (!mbar_wait(&empty[s], ((it / C::NS) & 1) ^ 1, args.err, abort_flag)) { ok = false; break; }
+          uint8_t* st = ring + s * C::STAGE;
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          bulk_load(st, args.w_tiles + ((size_t)sg.tile * nkb + kb) * WI_WB, WI_WB, &full[s]);
+          tma_load_2d(st + WI_WB, &map_x, &full[s], kb * 128, 0);
+        }
       }
     }
   } else if (warp == 1) {
@@ -236,19 +313,21 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
       constexpr uint32_t idesc = umma_idesc_s8(128, C::NB);
       int it = 0;
       bool ok = true;
-      for (int ti = 0; ti < ntile && ok; ++ti) {
-        const int b = ti & 1;
-        if (!mbar_wait(&acce[b], ((ti >> 1) & 1) ^ 1, args.err, abort_flag)) break;
+      for (int i = 0; i < nseg && ok; ++i) {
+        const Seg sg = sch.get(c, i);
+        const int b = i & 1;  // take a free accumulator
+        if (!mbar_wait(&acce[b], ((i >> 1) & 1) ^ 1, args.err, abort_flag)) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * C::ACC_COLS;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        for (int kb = sg.kb_lo; kb <= sg.kb_hi; ++kb, ++it) {
           const int s = it % C::NS;
           if (!mbar_wait(&full[s], (it / C::NS) & 1, args.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = umma_desc_sw128(smem_u32(ring + s * C::STAGE));
           const uint64_t bdesc = umma_desc_sw128(smem_u32(ring + s * C::STAGE + WI_WB));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) umma_i8(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k)
+            umma_i8(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb == sg.kb_lo && k == 0) ? 0u : 1u);
           umma_commit(&empty[s]);
         }
         umma_commit(&accf[b]);
@@ -259,10 +338,12 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
     const int q = warp & 3;
     const int et = threadIdx.x - 64;  // 0..127
     constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;
-    for (int ti = 0; ti < ntile; ++ti) {
-      const int b = ti & 1;
-      const int tile = group + ti * args.groups;
-      if (!mbar_wait(&accf[b], (ti >> 1) & 1, args.err, abort_flag)) break;
+    for (int seg = 0; seg < nseg; ++seg) {
+      const int b = seg & 1;
+      const Seg sg = sch.get(c, seg);
+      const int tile = sg.tile;
+      const bool whole = sg.n == 1;
+      if (!mbar_wait(&accf[b], (seg >> 1) & 1, args.err, abort_flag)) break;
       tc_fence_after();
       // accumulator column l * MP + m holds limb l of row m: recombine
       float r[MP];
@@ -281,9 +362,9 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[b]);  // accumulator free for tile ti + 2
+      if (lane == 0) mbar_arrive(&acce[b]);  // accumulator free for segment seg + 2
       const int ch = q * 32 + lane;
-      if (S == 1) {
+      if (whole) {
         // own tile: stage the accumulator in shared memory rows and run the epilogue
 #pragma unroll
         for (int m = 0; m < MP; ++m) red[m * 129 + ch] = r[m];
@@ -299,18 +380,19 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
         }
         named_bar(1, 128);
       } else {
-        // split partial -> global [tile][split][m][128], coalesced per row
-        float* dst = args.part + ((size_t)tile * S + split) * MP * 128;
+        // partial -> the tile's slot, coalesced per row
+        const int n_seg = sg.n;
+        float* dst = args.part + ((size_t)tile * args.maxseg + sg.slot) * MP * 128;
 #pragma unroll
         for (int m = 0; m < MP; ++m) dst[m * 128 + ch] = r[m];
         __threadfence();
         named_bar(1, 128);
-        if (et == 0) *last_flag = (atomicAdd(args.counters + tile, 1) == S - 1);
+        if (et == 0) *last_flag = (atomicAdd(args.counters + tile, 1) == n_seg - 1);
         named_bar(1, 128);
         if (*last_flag) {
           __threadfence();
-          const float* src = args.part + (size_t)tile * S * MP * 128;
-          // two rows per pass, every split's partial loaded before any add
+          const float* src = args.part + (size_t)tile * args.maxseg * MP * 128;
+          // two rows per pass, every slot's partial loaded before any add
           for (int m0 = q; m0 < p.M; m0 += 8) {
             float4 va[2][8], ua[2][8];
 #pragma unroll
@@ -320,7 +402,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
                 const int m = m0 + 4 * rr;
                 va[rr][s] = make_float4(0.f, 0.f, 0.f, 0.f);
                 ua[rr][s] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (s < S && m < p.M) {
+                if (s < n_seg && m < p.M) {
                   const float* rowp = src + ((size_t)s * MP + m) * 128;
                   if (EPC == 4) {
                     va[rr][s] = __ldcg(reinterpret_cast<const float4*>(rowp + lane * 4));
@@ -338,7 +420,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
               if (m < p.M) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int s = 0; s < 8; ++s) {  // fixed split order: deterministic
+                for (int s = 0; s < 8; ++s) {  // fixed slot order: deterministic
                   v[0] += va[rr][s].x; v[1] += va[rr][s].y; v[2] += va[rr][s].z; v[3] += va[rr][s].w;
                   u[0] += ua[rr][s].x; u[1] += ua[rr][s].y;
                 }
@@ -407,70 +489,102 @@ __device__ __forceinline__ float block_max(float v, float* sh) {
   return sh[32];
 }
 
-// f16 rows -> limbs; one CTA per (padded) row
+// f16 rows -> limbs.  With producer maxima (maxpart [nparts, M]) every CTA
+// converts one 1024-element chunk of one row in a single pass; without them a
+// CTA owns a whole row and finds its maximum first.
+constexpr int LB_CHUNK = 1024;
+
+__device__ __forceinline__ void limbs_store4(int8_t* o0, int8_t* o1, int8_t* o2, int k,
+                                             const float (&v)[4], float up) {
+  int8_t l[3][4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
+  *reinterpret_cast<char4*>(o0 + k) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
+  *reinterpret_cast<char4*>(o1 + k) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
+  *reinterpret_cast<char4*>(o2 + k) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
+}
+
+__device__ __forceinline__ void load_h4(const __half* row, int k, float (&v)[4]) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+
+// max over the producer's partials of row m (every thread of the CTA gets it)
+__device__ __forceinline__ float part_max(const float* part, int nparts, int M, int m, float* sh) {
+  float mx = 0.f;
+  for (int q = threadIdx.x; q < nparts; q += blockDim.x) mx = fmaxf(mx, part[(size_t)q * M + m]);
+  return block_max(mx, sh);
+}
+
 __global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int K,
+                                const float* __restrict__ maxpart, int nparts,
                                 int8_t* __restrict__ xl, float* __restrict__ xscale) {
   __shared__ float sh[33];
-  const int m = blockIdx.x;
+  const int m = blockIdx.y;
+  const int k0 = maxpart ? blockIdx.x * LB_CHUNK : 0;
+  const int k1 = maxpart ? min(K, k0 + LB_CHUNK) : K;
   int8_t* o0 = xl + (size_t)m * K;
   int8_t* o1 = o0 + (size_t)MP * K;
   int8_t* o2 = o1 + (size_t)MP * K;
   if (m >= M) {
-    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
       *reinterpret_cast<uint32_t*>(o0 + k) = 0u;
       *reinterpret_cast<uint32_t*>(o1 + k) = 0u;
       *reinterpret_cast<uint32_t*>(o2 + k) = 0u;
     }
-    if (threadIdx.x == 0) xscale[m] = 1.f;
+    if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = 1.f;
     return;
   }
   const __half* row = x + (size_t)m * K;
-  float mx = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+  float mx;
+  if (maxpart) {
+    mx = part_max(maxpart, nparts, M, m, sh);
+  } else {
+    mx = 0.f;
+    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+      float v[4];
+      load_h4(row, k, v);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+    }
+    mx = block_max(mx, sh);
   }
   int e;
-  frexpf(block_max(mx, sh), &e);
+  frexpf(mx, &e);  // every |x| <= mx < 2^e
   const float up = ldexpf(1.f, 20 - e);
-  if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
-  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(row + k);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-    const float v[4] = {a.x, a.y, b.x, b.y};
-    int8_t l[3][4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
-    *reinterpret_cast<char4*>(o0 + k) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
-    *reinterpret_cast<char4*>(o1 + k) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
-    *reinterpret_cast<char4*>(o2 + k) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
+  if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
+  for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
+    float v[4];
+    load_h4(row, k, v);
+    limbs_store4(o0, o1, o2, k, v, up);
   }
 }
 
-// RMSNorm of the residual rows (h fp32, sum of squares from hstat partials)
-// rounded to f16 like the reference's activations, then split into limbs
+// RMSNorm of the residual rows (h fp32; sums of h^2 and maxima of |h * w| from
+// the producer's partials) rounded to f16 like the reference's activations,
+// then split into limbs; one 1024-element chunk of one row per CTA
 __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
-                                     int hparts, int M, int MP, int K, const float* __restrict__ w,
-                                     float eps, int8_t* __restrict__ xl, float* __restrict__ xscale) {
+                                     const float* __restrict__ hmax, int hparts, int M, int MP, int K,
+                                     const float* __restrict__ w, float eps, int8_t* __restrict__ xl,
+                                     float* __restrict__ xscale) {
   __shared__ float sh[33];
-  const int m = blockIdx.x;
+  const int m = blockIdx.y;
+  const int k0 = blockIdx.x * LB_CHUNK, k1 = min(K, k0 + LB_CHUNK);
   int8_t* o0 = xl + (size_t)m * K;
   int8_t* o1 = o0 + (size_t)MP * K;
   int8_t* o2 = o1 + (size_t)MP * K;
   if (m >= M) {
-    for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+    for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
       *reinterpret_cast<uint32_t*>(o0 + k) = 0u;
       *reinterpret_cast<uint32_t*>(o1 + k) = 0u;
       *reinterpret_cast<uint32_t*>(o2 + k) = 0u;
     }
-    if (threadIdx.x == 0) xscale[m] = 1.f;
+    if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = 1.f;
     return;
   }
   float ss = 0.f;
-  for (int qq = threadIdx.x; qq < hparts; qq += blockDim.x) ss += hstat[(size_t)qq * M + m];
+  for (int q = threadIdx.x; q < hparts; q += blockDim.x) ss += hstat[(size_t)q * M + m];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -482,27 +596,22 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
   __syncthreads();
   const float rstd = sh[32];
   __syncthreads();
-  const float* row = h + (size_t)m * K;
-  auto xval = [&](int k, float hv) { return __half2float(__float2half_rn(hv * rstd * __ldg(w + k))); };
-  float mx = 0.f;
-  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-    const float4 hv = *reinterpret_cast<const float4*>(row + k);
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(xval(k, hv.x)), fabsf(xval(k + 1, hv.y))),
-                         fmaxf(fabsf(xval(k + 2, hv.z)), fabsf(xval(k + 3, hv.w)))));
-  }
+  // bound on max |f16(h * rstd * w)|: the fp32 products and the f16 rounding
+  // stay within 2^-9 of rstd * max |h * w|
+  const float bound = part_max(hmax, hparts, M, m, sh) * rstd * (1.f + 1.f / 512.f);
   int e;
-  frexpf(block_max(mx, sh), &e);
+  frexpf(bound, &e);
   const float up = ldexpf(1.f, 20 - e);
-  if (threadIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
-  for (int k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
+  const float* row = h + (size_t)m * K;
+  for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
     const float4 hv = *reinterpret_cast<const float4*>(row + k);
-    const float v[4] = {xval(k, hv.x), xval(k + 1, hv.y), xval(k + 2, hv.z), xval(k + 3, hv.w)};
-    int8_t l[3][4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
-    *reinterpret_cast<char4*>(o0 + k) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
-    *reinterpret_cast<char4*>(o1 + k) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
-    *reinterpret_cast<char4*>(o2 + k) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
+    const float4 wv = __ldg(reinterpret_cast<const float4*>(w + k));
+    const float v[4] = {__half2float(__float2half_rn(hv.x * rstd * wv.x)),
+                        __half2float(__float2half_rn(hv.y * rstd * wv.y)),
+                        __half2float(__float2half_rn(hv.z * rstd * wv.z)),
+                        __half2float(__float2half_rn(hv.w * rstd * wv.w))};
+    limbs_store4(o0, o1, o2, k, v, up);
   }
 }
 
@@ -537,13 +646,12 @@ static bool map_i8_rows(CUtensorMap* m, const void* base, uint64_t K, uint64_t r
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// K-split S in 1..8 and groups = floor(SMs / S) from a small cost model:
-// a tile slice streams nkb/S blocks of 16 KB at ~42 GB/s per SM; with S > 1
-// every tile also pays a split-K merge (~4 us, hidden behind the next tile's
-// stream when that is longer, exposed once at the end).
-void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups) {
-  const int tiles = N / 128, nkb = K / 128;
-  const double t_kb = 16384.0 / 42e3;  // us per k128 block per SM
+// Split plan: S in 1..8 and groups = floor(SMs / S) from a small cost model
+// (a slice streams nkb/S blocks of 16 KB at ~42 GB/s per SM; S > 1 adds a
+// merge of ~4 us per tile, hidden behind the next tile's stream when that is
+// longer, exposed once at the end).
+static void w8i_split_plan(int tiles, int nkb, int num_sms, int* splits, int* groups) {
+  const double t_kb = 16384.0 / 42e3;
   double best = 1e30;
   int bs = 1, bg = num_sms < tiles ? num_sms : tiles;
   for (int s = 1; s <= 8 && s <= nkb; ++s) {
@@ -560,11 +668,41 @@ void w8tc_plan(int N, int K, int num_sms, int* splits, int* groups) {
   *groups = bg;
 }
 
+// The launch schedule: grid size, split plan, stream-K or not, partial slots.
+struct W8Schedule {
+  int grid, splits, groups, stream_k, maxseg;
+};
+
+static W8Schedule w8i_schedule(int N, int K, int num_sms) {
+  const int tiles = N / 128, nkb = K / 128;
+  W8Schedule w{};
+  if (nkb >= 64) {
+    // stream-K: one CTA per SM (never more CTAs than units), shrunk until no
+    // tile is shared by more than 8 CTAs
+    const long long U = (long long)tiles * nkb;
+    int G = (int)std::min<long long>(num_sms, U);
+    for (;;) {
+      int ms = 1;
+      for (int t = 0; t < tiles; ++t)
+        ms = std::max(ms, sk_owner(t * nkb + nkb - 1, U, G) - sk_owner(t * nkb, U, G) + 1);
+      if (ms <= 8 || G == 1) {
+        w.grid = G; w.splits = G; w.groups = 1; w.stream_k = 1; w.maxseg = ms;
+        return w;
+      }
+      --G;
+    }
+  }
+  w8i_split_plan(tiles, nkb, num_sms, &w.splits, &w.groups);
+  w.grid = w.splits * w.groups;
+  w.stream_k = 0;
+  w.maxseg = w.splits;
+  return w;
+}
+
 size_t w8tc_part_floats(int N, int K, int M, int num_sms) {
-  int s, g;
-  w8tc_plan(N, K, num_sms, &s, &g);
+  const W8Schedule w = w8i_schedule(N, K, num_sms);
   const int mp = (M + 15) / 16 * 16;
-  return s > 1 ? (size_t)(N / 128) * s * mp * 128 : 0;
+  return (size_t)(N / 128) * w.maxseg * mp * 128;
 }
 
 template <int MP, int MODE>
@@ -574,7 +712,8 @@ static cudaError_t w8i_launch_t(const CUtensorMap& mx, const WiArgs& a, cudaStre
   auto kern = w8i_kernel<MP, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  kern<<<a.groups * a.p.splits, WI_THREADS, smem, st>>>(mx, a);
+  DFL_TRY(max_smem_carveout(kern));
+  kern<<<a.stream_k ? a.p.splits : a.p.splits * a.groups, WI_THREADS, smem, st>>>(mx, a);
   return cudaGetLastError();
 }
 
@@ -592,14 +731,14 @@ cudaError_t w8tc_launch(const int8_t* w_tiles, const W8Params& pin, int mode, in
     return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(w_tiles) & 15) return cudaErrorInvalidValue;
   W8Params p = pin;
-  int groups = 1;
-  w8tc_plan(p.N, p.K, num_sms, &p.splits, &groups);
+  const W8Schedule w = w8i_schedule(p.N, p.K, num_sms);
+  p.splits = w.splits;  // stream-K: the grid size; split plan: S
   const int mp = (p.M + 15) / 16 * 16;
-  if (p.splits > 1 && (!part || !counters || part_floats < (size_t)(p.N / 128) * p.splits * mp * 128))
+  if (!part || !counters || part_floats < (size_t)(p.N / 128) * w.maxseg * mp * 128)
     return cudaErrorInvalidValue;
   CUtensorMap mx;
   if (!map_i8_rows(&mx, p.xl, p.K, 3 * mp)) return cudaErrorInvalidValue;
-  WiArgs a{p, w_tiles, part, counters, groups, err};
+  WiArgs a{p, w_tiles, part, counters, w.maxseg, w.stream_k, w.groups, err};
   if (mode == kQKV) return w8i_mode<kQKV>(mx, a, mp, st);
   if (mode == kResid) return w8i_mode<kResid>(mx, a, mp, st);
   if (mode == kSiluMul) return w8i_mode<kSiluMul>(mx, a, mp, st);
@@ -614,18 +753,24 @@ cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst,
   return cudaGetLastError();
 }
 
-cudaError_t w8_limbs_launch(const __half* x, int M, int K, int8_t* xl, float* xscale, cudaStream_t st) {
+cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart, int nparts,
+                            int8_t* xl, float* xscale, cudaStream_t st) {
   if (M < 1 || M > 64 || K % 128) return cudaErrorInvalidValue;
   const int mp = (M + 15) / 16 * 16;
-  w8_limbs_kernel<<<mp, 256, 0, st>>>(x, M, mp, K, xl, xscale);
+  const dim3 grid(maxpart ? (K + LB_CHUNK - 1) / LB_CHUNK : 1, mp);
+  DFL_TRY(max_smem_carveout(w8_limbs_kernel));
+  w8_limbs_kernel<<<grid, 256, 0, st>>>(x, M, mp, K, maxpart, nparts, xl, xscale);
   return cudaGetLastError();
 }
 
-cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, int hparts, int M, int K,
-                                 const float* w, float eps, int8_t* xl, float* xscale, cudaStream_t st) {
-  if (M < 1 || M > 64 || K % 128) return cudaErrorInvalidValue;
+cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float* hmax, int hparts,
+                                 int M, int K, const float* w, float eps, int8_t* xl, float* xscale,
+                                 cudaStream_t st) {
+  if (M < 1 || M > 64 || K % 128 || !hmax) return cudaErrorInvalidValue;
   const int mp = (M + 15) / 16 * 16;
-  rmsnorm_limbs_kernel<<<mp, 256, 0, st>>>(h, hstat, hparts, M, mp, K, w, eps, xl, xscale);
+  const dim3 grid((K + LB_CHUNK - 1) / LB_CHUNK, mp);
+  DFL_TRY(max_smem_carveout(rmsnorm_limbs_kernel));
+  rmsnorm_limbs_kernel<<<grid, 256, 0, st>>>(h, hstat, hmax, hparts, M, mp, K, w, eps, xl, xscale);
   return cudaGetLastError();
 }
 

@@ -8,6 +8,8 @@ Cases (27B-class draft dims, 32 block rows):
   w8_gu    gate|up W8A16 projection   N=34816 K=5120   (178 MB int8)
   w8_down  down W8A16 projection      N=5120  K=17408  (89 MB)
   w8_qkv   fused q|k|v projection     N=7168  K=5120   (37 MB)
+  w8_o     o projection               N=5120  K=5120   (21 MB)
+  w8:N:K   any W8A16 shape (N, K multiples of 128)
   lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
   attn     block attention            40/8 heads, 32 queries, kv 4128
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
@@ -36,8 +38,12 @@ def main():
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
     M = 32
-    if a.case.startswith("w8_"):
-        N, Kd = {"w8_gu": (34816, 5120), "w8_down": (5120, 17408), "w8_qkv": (7168, 5120)}[a.case]
+    if a.case.startswith("w8_") or a.case.startswith("w8:"):
+        if a.case.startswith("w8:"):  # w8:N:K
+            N, Kd = (int(v) for v in a.case.split(":")[1:3])
+        else:
+            N, Kd = {"w8_gu": (34816, 5120), "w8_down": (5120, 17408), "w8_qkv": (7168, 5120),
+                     "w8_o": (5120, 5120)}[a.case]
         q = torch.randint(-127, 128, (N, Kd), generator=g, device=dev, dtype=torch.int8)
         s = (torch.rand(N, generator=g, device=dev) * 1e-3).to(torch.float16)
         x = torch.randn(M, Kd, generator=g, device=dev).to(torch.float16)
