@@ -13,10 +13,14 @@
 //       epilogue: scale, per-head k RMSNorm + neox RoPE, f16 store into the
 //       per-layer K / V buffers.
 //
-// CTA tile 128 x 256, K step 64 (one 128-byte swizzle atom), 4-stage TMA ring.
+// Persistent: one CTA per SM walks output tiles 128 x 256 (blockIdx.x, +grid,
+// ...) in a rasterised order (groups of 8 n-blocks, n fastest), so the tiles
+// in flight at once share A and B rows in L2.  K step 64 (one 128-byte
+// swizzle atom), 4-stage TMA ring across tile boundaries.
 // Warp 0: TMA producer.  Warp 1: TMEM allocator + single-thread UMMA issuer
-// (tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, fp32 accumulator in
-// 256 TMEM columns).  Warps 2-5: epilogue (tcgen05.ld, each thread owns one
+// (tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16) into one of two fp32
+// accumulators (2 x 256 TMEM columns), so the epilogue of a tile overlaps the
+// main loop of the next.  Warps 2-5: epilogue (tcgen05.ld, each thread owns one
 // accumulator row, so per-row and per-head reductions are thread-local).
 // Every mbarrier wait is bounded; a timeout sets the device error word and the
 // CTA unwinds (TMEM is released on every path).
@@ -30,6 +34,18 @@ constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;   // 32 KB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_THREADS = 192;
 constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int TC_GROUP_N = 8;  // rasterisation: n-blocks per tile group
+
+// tile t -> (m-block, n-block): groups of TC_GROUP_N n-blocks; inside a group
+// the n-block runs fastest
+__device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& nb) {
+  const int g = t / (nmb * TC_GROUP_N);
+  const int first = g * TC_GROUP_N;
+  const int gw = min(TC_GROUP_N, nnb - first);
+  const int r = t - g * nmb * TC_GROUP_N;
+  mb = r / gw;
+  nb = first + r % gw;
+}
 
 
 
@@ -41,27 +57,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
   uint64_t* empty = full + TC_STAGES;
-  uint64_t* accum = empty + TC_STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* accf = empty + TC_STAGES;  // [2] accumulator ready
+  uint64_t* acce = accf + 2;           // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
   const int nk = p.K / TC_BK;
+  const int nmb = (p.M + TC_BM - 1) / TC_BM, nnb = p.N / TC_BN;
+  const int ntiles = nmb * nnb;
+  const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TC_BN);
+    tmem_alloc(tmem_slot, 2 * TC_BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -71,149 +93,171 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % TC_STAGES;
-        const uint32_t ph = (kb / TC_STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) break;
-        uint8_t* sa = smem + s * TC_STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
-        tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, m0);
-        tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, n0);
+      int it = 0;
+      bool ok = true;
+      for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        int mb, nb;
+        tc_tile(blockIdx.x + ti * gridDim.x, nmb, nnb, mb, nb);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % TC_STAGES;
+          const uint32_t ph = (it / TC_STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * TC_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
+          tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, mb * TC_BM);
+          tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, nb * TC_BN);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_f16(TC_BM, TC_BN, AB_FMT);
+      int it = 0;
       bool ok = true;
-      for (int kb = 0; kb < nk && ok; ++kb) {
-        const int s = kb % TC_STAGES;
-        const uint32_t ph = (kb / TC_STAGES) & 1;
-        if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
+      for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        const int b = ti & 1;
+        if (!mbar_wait(&acce[b], ((ti >> 1) & 1) ^ 1, p.err, abort_flag)) break;
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
-        const uint64_t adesc = umma_desc_sw128(sa);
-        const uint64_t bdesc = umma_desc_sw128(sa + TC_A_BYTES);
+        const uint32_t acc = tmem + b * TC_BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % TC_STAGES;
+          const uint32_t ph = (it / TC_STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
+          const uint64_t adesc = umma_desc_sw128(sa);
+          const uint64_t bdesc = umma_desc_sw128(sa + TC_A_BYTES);
 #pragma unroll
-        for (int k = 0; k < TC_BK / 16; ++k) {
-          // advance 16 elements (32 bytes) inside the swizzle atom: +2 in 16-byte units
-          umma_f16(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < TC_BK / 16; ++k) {
+            // advance 16 elements (32 bytes) inside the swizzle atom: +2 in 16-byte units
+            umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[s]);
         }
-        umma_commit(&empty[s]);
+        umma_commit(&accf[b]);  // fires once every MMA of the tile has retired
       }
-      umma_commit(accum);  // fires once every issued MMA has retired
     }
   } else {
     // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
     const int q = warp & 3;
     const int row_local = q * 32 + lane;
-    const int row = m0 + row_local;
-    const bool row_ok = row < p.M;
-    const bool ok = mbar_wait(accum, 0, p.err, abort_flag) && !*abort_flag;
-    tc_fence_after();
-    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
-    if (ok) {
-      if (MODE == kTcFc || MODE == kTcStoreF32) {
-        float ss = 0.f;
+    for (int ti = 0; ti < my_tiles; ++ti) {
+      const int buf = ti & 1;
+      int mb, nb;
+      tc_tile(blockIdx.x + ti * gridDim.x, nmb, nnb, mb, nb);
+      const int n0 = nb * TC_BN;
+      const int row = mb * TC_BM + row_local;
+      const bool row_ok = row < p.M;
+      if (!mbar_wait(&accf[buf], (ti >> 1) & 1, p.err, abort_flag) || *abort_flag) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem + buf * TC_BN + ((uint32_t)(q * 32) << 16);
+      {
+        if (MODE == kTcFc || MODE == kTcStoreF32) {
+          float ss = 0.f;
 #pragma unroll 1
-        for (int ch = 0; ch < TC_BN / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld32(tbase + ch * 32, r);
-          tmem_ld_wait();
-          if (row_ok) {
-            float4* dst = reinterpret_cast<float4*>(p.out_f32 + (size_t)row * p.N + n0 + ch * 32);
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              const float4 f = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                                           __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-              if (MODE == kTcFc) ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
-              dst[v] = f;
-            }
-          }
-        }
-        if (MODE == kTcFc && row_ok) p.sumsq_part[(size_t)blockIdx.x * p.M + row] = ss;
-      } else {  // kTcCtxKV: two 128-wide heads per tile
-        // sequence and slot of this packed context row (rows >= M are never stored)
-        const int crow = row_ok ? row : 0;
-        const int bi = kv_seq_of_ctx_row(p.kv, crow);
-        const int slot = kv_slot(p.kv, p.kv.n0[bi] + crow - p.kv.ctx_start[bi], p.kv.rs_pre[bi]);
-        const int per_layer = 2 * p.nkv * 128;
-#pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          const int col0 = n0 + hh * 128;
-          const int layer = col0 / per_layer;
-          const int within = col0 - layer * per_layer;
-          const bool is_v = within >= p.nkv * 128;
-          const int kvh = (within % (p.nkv * 128)) / 128;
-          const float* sc = p.scale + col0;
-          float rstd = 1.f;
-          if (!is_v) {
-            float ss = 0.f;
-#pragma unroll 1
-            for (int ch = 0; ch < 4; ++ch) {
-              uint32_t r[32];
-              tmem_ld32(tbase + hh * 128 + ch * 32, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 32; ++e) {
-                const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
-                ss += y * y;
-              }
-            }
-            rstd = rsqrtf(ss / 128.0f + p.eps);
-          }
-          __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
-                        (((size_t)bi * p.nkv + kvh) * p.kv.slots + slot) * 128;
-          const float* kn = p.k_norm + layer * 128;
-          const float2* cs = p.rope + (size_t)crow * 64;
-#pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            uint32_t r1[32], r2[32];
-            tmem_ld32(tbase + hh * 128 + half * 32, r1);
-            tmem_ld32(tbase + hh * 128 + 64 + half * 32, r2);
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tbase + ch * 32, r);
             tmem_ld_wait();
             if (row_ok) {
-              uint32_t o1[16], o2[16];
+              float4* dst = reinterpret_cast<float4*>(p.out_f32 + (size_t)row * p.N + n0 + ch * 32);
 #pragma unroll
-              for (int e = 0; e < 32; e += 2) {
-                float a[2], b[2];
-#pragma unroll
-                for (int t = 0; t < 2; ++t) {
-                  const int d = half * 32 + e + t;
-                  float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
-                  float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
-                  if (!is_v) {
-                    y1 = y1 * rstd * __ldg(kn + d);
-                    y2 = y2 * rstd * __ldg(kn + d + 64);
-                    const float2 t2 = __ldg(cs + d);
-                    const float cth = t2.x, sth = t2.y;
-                    a[t] = y1 * cth - y2 * sth;
-                    b[t] = y1 * sth + y2 * cth;
-                  } else {
-                    a[t] = y1;
-                    b[t] = y2;
-                  }
-                }
-                o1[e / 2] = pack_f16x2(a[0], a[1]);
-                o2[e / 2] = pack_f16x2(b[0], b[1]);
+              for (int v = 0; v < 8; ++v) {
+                const float4 f = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                             __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                if (MODE == kTcFc) ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
+                dst[v] = f;
               }
-              uint4* d1 = reinterpret_cast<uint4*>(dst + half * 32);
-              uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + half * 32);
+            }
+          }
+          if (MODE == kTcFc && row_ok) p.sumsq_part[(size_t)nb * p.M + row] = ss;
+        } else {  // kTcCtxKV: two 128-wide heads per tile
+          // sequence and slot of this packed context row (rows >= M are never stored)
+          const int crow = row_ok ? row : 0;
+          const int bi = kv_seq_of_ctx_row(p.kv, crow);
+          const int slot = kv_slot(p.kv, p.kv.n0[bi] + crow - p.kv.ctx_start[bi], p.kv.rs_pre[bi]);
+          const int per_layer = 2 * p.nkv * 128;
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
+            const int col0 = n0 + hh * 128;
+            const int layer = col0 / per_layer;
+            const int within = col0 - layer * per_layer;
+            const bool is_v = within >= p.nkv * 128;
+            const int kvh = (within % (p.nkv * 128)) / 128;
+            const float* sc = p.scale + col0;
+            float rstd = 1.f;
+            if (!is_v) {
+              float ss = 0.f;
+#pragma unroll 1
+              for (int ch = 0; ch < 4; ++ch) {
+                uint32_t r[32];
+                tmem_ld32(tbase + hh * 128 + ch * 32, r);
+                tmem_ld_wait();
 #pragma unroll
-              for (int v = 0; v < 4; ++v) {
-                d1[v] = make_uint4(o1[4 * v], o1[4 * v + 1], o1[4 * v + 2], o1[4 * v + 3]);
-                d2[v] = make_uint4(o2[4 * v], o2[4 * v + 1], o2[4 * v + 2], o2[4 * v + 3]);
+                for (int e = 0; e < 32; ++e) {
+                  const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
+                  ss += y * y;
+                }
+              }
+              rstd = rsqrtf(ss / 128.0f + p.eps);
+            }
+            __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
+                          (((size_t)bi * p.nkv + kvh) * p.kv.slots + slot) * 128;
+            const float* kn = p.k_norm + layer * 128;
+            const float2* cs = p.rope + (size_t)crow * 64;
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+              uint32_t r1[32], r2[32];
+              tmem_ld32(tbase + hh * 128 + half * 32, r1);
+              tmem_ld32(tbase + hh * 128 + 64 + half * 32, r2);
+              tmem_ld_wait();
+              if (row_ok) {
+                uint32_t o1[16], o2[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                  float a[2], b[2];
+#pragma unroll
+                  for (int t = 0; t < 2; ++t) {
+                    const int d = half * 32 + e + t;
+                    float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
+                    float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
+                    if (!is_v) {
+                      y1 = y1 * rstd * __ldg(kn + d);
+                      y2 = y2 * rstd * __ldg(kn + d + 64);
+                      const float2 t2 = __ldg(cs + d);
+                      const float cth = t2.x, sth = t2.y;
+                      a[t] = y1 * cth - y2 * sth;
+                      b[t] = y1 * sth + y2 * cth;
+                    } else {
+                      a[t] = y1;
+                      b[t] = y2;
+                    }
+                  }
+                  o1[e / 2] = pack_f16x2(a[0], a[1]);
+                  o2[e / 2] = pack_f16x2(b[0], b[1]);
+                }
+                uint4* d1 = reinterpret_cast<uint4*>(dst + half * 32);
+                uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + half * 32);
+#pragma unroll
+                for (int v = 0; v < 4; ++v) {
+                  d1[v] = make_uint4(o1[4 * v], o1[4 * v + 1], o1[4 * v + 2], o1[4 * v + 3]);
+                  d2[v] = make_uint4(o2[4 * v], o2[4 * v + 1], o2[4 * v + 2], o2[4 * v + 3]);
+                }
               }
             }
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);  // accumulator free for tile ti + 2
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, TC_BN);
+    tmem_dealloc(tmem, 2 * TC_BN);
   }
 }
 
@@ -259,9 +303,12 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   auto kern = tc_gemm_kernel<FMT, MODE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
   if (e != cudaSuccess) return e;
-  dim3 grid(p.N / TC_BN, (p.M + TC_BM - 1) / TC_BM);
+  int dev = 0, sms = 148;
+  DFL_TRY(cudaGetDevice(&dev));
+  DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
   DFL_TRY(max_smem_carveout(kern));
-  kern<<<grid, TC_THREADS, TC_SMEM, st>>>(ma, mb, p);
+  kern<<<tiles < sms ? tiles : sms, TC_THREADS, TC_SMEM, st>>>(ma, mb, p);
   return cudaGetLastError();
 }
 
