@@ -51,6 +51,8 @@ __device__ __forceinline__ void normrope_row(__half* row, const float* w, const 
 }
 
 __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ __align__(16) uint8_t smem[];
   const int split = blockIdx.x, kvh = blockIdx.y, bi = blockIdx.z;
   const int G = p.nq / p.nkv;
@@ -241,6 +243,8 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
 // one warp per (batch, head, block row), lanes split the splits for the
 // max / denominator and the head dims for the weighted sum.
 __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -319,13 +323,11 @@ cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   DFL_TRY(max_smem_carveout(attn_partial_kernel));
-  attn_partial_kernel<<<dim3(p.splits, p.nkv, batch), nwarps * 32, smem, st>>>(p);
-  e = cudaGetLastError();
+  e = launch_pdl(attn_partial_kernel, dim3(p.splits, p.nkv, batch), dim3(nwarps * 32), smem, st, p);
   if (e != cudaSuccess) return e;
   const int rows = p.nq * p.block;
   DFL_TRY(max_smem_carveout(attn_combine_kernel));
-  attn_combine_kernel<<<dim3((rows + 7) / 8, batch), 256, 0, st>>>(p, out);
-  return cudaGetLastError();
+  return launch_pdl(attn_combine_kernel, dim3((rows + 7) / 8, batch), dim3(256), 0, st, p, out);
 }
 
 }  // namespace dfl

@@ -260,6 +260,33 @@ __device__ __forceinline__ float warp_sum(float v) {
 // the step alternates kernels that need ~200 KB of shared memory with small
 // ones, and a launch whose carveout differs from the running one makes the SM
 // reconfigure its L1 / shared split first.
+// Programmatic dependent launch.  A kernel started with launch_pdl may begin
+// while the previous kernel of the stream is still running; griddep_wait()
+// blocks until that kernel has completed and its writes are visible, so every
+// such kernel calls it before it reads or writes anything earlier kernels
+// touch (without the launch attribute it returns at once).
+// griddep_launch_dependents() lets the next kernel be scheduled early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 #define DFL_TRY(call)                      \
   do {                                     \
     const cudaError_t e_ = (call);         \

@@ -43,6 +43,8 @@ template <int MP>
 __global__ void __launch_bounds__(LT_THREADS, 1)
     lm_tc_kernel(const __grid_constant__ CUtensorMap map_h, const LmParams p, const uint8_t* e_tiles,
                  int tiles_per_cta, int* err) {
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int H_BYTES = MP * 128;
   constexpr int STAGE = LT_E_BYTES + H_BYTES;
   static_assert(STAGE % 1024 == 0, "stage alignment");
@@ -219,6 +221,8 @@ __global__ void argmax_accept_kernel(const float* __restrict__ best_val,
                                      int32_t* __restrict__ out_tokens,
                                      const int32_t* __restrict__ target, int32_t* __restrict__ acc_len,
                                      int32_t* __restrict__ correction) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int toks[1024];
@@ -305,8 +309,7 @@ static cudaError_t lm_tc_t(const CUtensorMap& mh, const LmParams& p, const uint8
   cudaError_t e = cudaFuncSetAttribute(lm_tc_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   DFL_TRY(max_smem_carveout(lm_tc_kernel<MP>));
-  lm_tc_kernel<MP><<<grid, LT_THREADS, smem, st>>>(mh, p, et, per, err);
-  return cudaGetLastError();
+  return launch_pdl(lm_tc_kernel<MP>, dim3(grid), dim3(LT_THREADS), smem, st, mh, p, et, per, err);
 }
 
 // returns the grid used (partials written for that many CTAs) via *grid_out
@@ -339,9 +342,8 @@ cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int
                                  int32_t* acc_len, int32_t* correction, cudaStream_t st) {
   if (block < 2 || block > 1024) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(argmax_accept_kernel));
-  argmax_accept_kernel<<<batch, 32 * (block - 1 < 32 ? block - 1 : 32), 0, st>>>(
-      bv, bi, nparts, M, block, out_tokens, target, acc_len, correction);
-  return cudaGetLastError();
+  return launch_pdl(argmax_accept_kernel, dim3(batch), dim3(32 * (block - 1 < 32 ? block - 1 : 32)), 0,
+                    st, bv, bi, nparts, M, block, out_tokens, target, acc_len, correction);
 }
 
 cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch, int block,

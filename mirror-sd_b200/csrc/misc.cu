@@ -26,6 +26,8 @@ __global__ void rope_table_kernel(int pos0, int rows, const float* __restrict__ 
 // then block row m = s * block + j at pos0[s] + ctx_s + j
 __global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
                                       const float* __restrict__ inv_freq, float2* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * 64) return;
   const int r = idx >> 6, i = idx & 63;
@@ -50,6 +52,8 @@ __global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
 __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, int H,
                               float* __restrict__ h, float* __restrict__ hstat,
                               const float* __restrict__ w, float* __restrict__ hmax) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float red[2][32];
   const int row = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -100,6 +104,8 @@ __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, in
 __global__ void ctx_norm_kernel(const float* __restrict__ raw, const float* __restrict__ part,
                                 int nparts, int rows, int H, const float* __restrict__ w, float eps,
                                 __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int r = blockIdx.x;
   __shared__ float rs;
   if (threadIdx.x == 0) {
@@ -129,6 +135,8 @@ template <bool OUT_F32>
 __global__ void final_norm_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
                                   int hparts, int M, int H, const float* __restrict__ w, float eps,
                                   __nv_bfloat16* __restrict__ hn, void* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int row = blockIdx.x;
   __shared__ float rs;
   if (threadIdx.x == 0) {
@@ -180,22 +188,20 @@ cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_fr
   if (m.nseq < 1 || m.nseq > kKvMaxSeq || block < 1) return cudaErrorInvalidValue;
   const int rows = m.ctx_start[m.nseq] + m.nseq * block;
   DFL_TRY(max_smem_carveout(rope_table_map_kernel));
-  rope_table_map_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(m, block, rows, inv_freq, out);
-  return cudaGetLastError();
+  return launch_pdl(rope_table_map_kernel, dim3((rows * 64 + 255) / 256), dim3(256), 0, st, m, block,
+                    rows, inv_freq, out);
 }
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
                           const float* w, float* hmax, cudaStream_t st) {
   if (H % 8) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(init_h_kernel));
-  init_h_kernel<<<M, 256, 0, st>>>(noise, M, H, h, hstat, w, hmax);
-  return cudaGetLastError();
+  return launch_pdl(init_h_kernel, dim3(M), dim3(256), 0, st, noise, M, H, h, hstat, w, hmax);
 }
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st) {
   if (H % 8 || rows < 1) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(ctx_norm_kernel));
-  ctx_norm_kernel<<<rows, 256, 0, st>>>(raw, part, nparts, rows, H, w, eps, out);
-  return cudaGetLastError();
+  return launch_pdl(ctx_norm_kernel, dim3(rows), dim3(256), 0, st, raw, part, nparts, rows, H, w, eps, out);
 }
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
@@ -205,10 +211,10 @@ cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, in
                                  : max_smem_carveout(final_norm_kernel<false>);
   if (ce != cudaSuccess) return ce;
   if (out_f32)
-    final_norm_kernel<true><<<M, 256, 0, st>>>(h, hstat, hparts, M, H, w, eps, hn, out);
-  else
-    final_norm_kernel<false><<<M, 256, 0, st>>>(h, hstat, hparts, M, H, w, eps, hn, out);
-  return cudaGetLastError();
+    return launch_pdl(final_norm_kernel<true>, dim3(M), dim3(256), 0, st, h, hstat, hparts, M, H, w, eps,
+                      hn, out);
+  return launch_pdl(final_norm_kernel<false>, dim3(M), dim3(256), 0, st, h, hstat, hparts, M, H, w, eps,
+                    hn, out);
 }
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st) {
   i8_to_f16_kernel<<<1024, 256, 0, st>>>(src, n, dst);

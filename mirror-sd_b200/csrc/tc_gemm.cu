@@ -53,6 +53,8 @@ template <int AB_FMT, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const TcParams p) {
+  griddep_wait();
+  griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
@@ -308,8 +310,7 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
   DFL_TRY(max_smem_carveout(kern));
-  kern<<<tiles < sms ? tiles : sms, TC_THREADS, TC_SMEM, st>>>(ma, mb, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
 }
 
 // a_bf16: A/B element type (true: bf16, false: f16).  mode: TcMode.

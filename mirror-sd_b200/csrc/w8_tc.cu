@@ -291,22 +291,39 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
+      // The weights depend on nothing earlier in the stream: the first NS ring
+      // stages get their weight blocks before this kernel waits for the
+      // previous one (programmatic dependent launch); their limb tiles follow
+      // once it has completed.
+      int pre_kb[C::NS];
       int it = 0;
-      bool ok = true;
+      bool ok = true, waited = false;
+      auto release_prefetch = [&](int n) {
+        griddep_wait();
+        waited = true;
+        for (int j = 0; j < n; ++j)
+          tma_load_2d(ring + j * C::STAGE + WI_WB, &map_x, &full[j], pre_kb[j] * 128, 0);
+      };
       for (int i = 0; i < nseg && ok; ++i) {
         const Seg sg = sch.get(c, i);
         for (int kb = sg.kb_lo; kb <= sg.kb_hi; ++kb, ++it) {
           const int s = it % C::NS;
+          if (it == C::NS) release_prefetch(C::NS);
           if (!mbar_wait(&empty[s], ((it / C::NS) & 1) ^ 1, args.err, abort_flag)) { ok = false; break; }
           uint8_t* st = ring + s * C::STAGE;
           mbar_arrive_expect_tx(&full[s], C::STAGE);
           bulk_load(st, args.w_tiles + ((size_t)sg.tile * nkb + kb) * WI_WB, WI_WB, &full[s]);
-          tma_load_2d(st + WI_WB, &map_x, &full[s], kb * 128, 0);
+          if (it < C::NS)
+            pre_kb[it] = kb;
+          else
+            tma_load_2d(st + WI_WB, &map_x, &full[s], kb * 128, 0);
         }
       }
+      if (!waited) release_prefetch(it < C::NS ? it : C::NS);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -335,6 +352,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
     }
   } else {
     // epilogue warps -> TMEM lane quadrant warp % 4 (= channels q*32 ..)
+    griddep_wait();  // the epilogue reads and writes what earlier kernels touch
     const int q = warp & 3;
     const int et = threadIdx.x - 64;  // 0..127
     constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;
@@ -521,6 +539,8 @@ __device__ __forceinline__ float part_max(const float* part, int nparts, int M, 
 __global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int K,
                                 const float* __restrict__ maxpart, int nparts,
                                 int8_t* __restrict__ xl, float* __restrict__ xscale) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float sh[33];
   const int m = blockIdx.y;
   const int k0 = maxpart ? blockIdx.x * LB_CHUNK : 0;
@@ -568,6 +588,8 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
                                      const float* __restrict__ hmax, int hparts, int M, int MP, int K,
                                      const float* __restrict__ w, float eps, int8_t* __restrict__ xl,
                                      float* __restrict__ xscale) {
+  griddep_wait();
+  griddep_launch_dependents();
   __shared__ float sh[33];
   const int m = blockIdx.y;
   const int k0 = blockIdx.x * LB_CHUNK, k1 = min(K, k0 + LB_CHUNK);
@@ -713,8 +735,8 @@ static cudaError_t w8i_launch_t(const CUtensorMap& mx, const WiArgs& a, cudaStre
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   DFL_TRY(max_smem_carveout(kern));
-  kern<<<a.stream_k ? a.p.splits : a.p.splits * a.groups, WI_THREADS, smem, st>>>(mx, a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(a.stream_k ? a.p.splits : a.p.splits * a.groups), dim3(WI_THREADS), smem,
+                    st, mx, a);
 }
 
 template <int MODE>
@@ -759,8 +781,7 @@ cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart,
   const int mp = (M + 15) / 16 * 16;
   const dim3 grid(maxpart ? (K + LB_CHUNK - 1) / LB_CHUNK : 1, mp);
   DFL_TRY(max_smem_carveout(w8_limbs_kernel));
-  w8_limbs_kernel<<<grid, 256, 0, st>>>(x, M, mp, K, maxpart, nparts, xl, xscale);
-  return cudaGetLastError();
+  return launch_pdl(w8_limbs_kernel, grid, dim3(256), 0, st, x, M, mp, K, maxpart, nparts, xl, xscale);
 }
 
 cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float* hmax, int hparts,
@@ -770,8 +791,8 @@ cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float
   const int mp = (M + 15) / 16 * 16;
   const dim3 grid((K + LB_CHUNK - 1) / LB_CHUNK, mp);
   DFL_TRY(max_smem_carveout(rmsnorm_limbs_kernel));
-  rmsnorm_limbs_kernel<<<grid, 256, 0, st>>>(h, hstat, hmax, hparts, M, mp, K, w, eps, xl, xscale);
-  return cudaGetLastError();
+  return launch_pdl(rmsnorm_limbs_kernel, grid, dim3(256), 0, st, h, hstat, hmax, hparts, M, mp, K, w, eps,
+                    xl, xscale);
 }
 
 }  // namespace dfl
