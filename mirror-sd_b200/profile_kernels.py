@@ -13,6 +13,8 @@ Cases (27B-class draft dims, 32 block rows):
   lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
   attn     block attention            40/8 heads, 32 queries, kv 4128
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
+  attn_sweep  block attention, 40/8 heads, 32 queries, ctx 1K..32K, batch 1 and 16
+              (prints a markdown table: time, bandwidth, fraction of measured HBM)
 Prints the mean launch time measured with CUDA events and the achieved
 bandwidth (or TFLOP/s for fc).
 """
@@ -27,6 +29,45 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 
 
+def attn_sweep(K, dev, iters):
+    """c4: block attention (40 query / 8 kv heads, 32 queries, head 128) over
+    ctx 1K..32K at batch 1 and 16; algorithmic bytes = Q + O + K + V (f16)."""
+    peaks = os.path.join(os.path.dirname(HERE), "MEASURED_PEAKS.json")
+    hbm = 6650.0
+    if os.path.exists(peaks):
+        import json
+        with open(peaks) as f:
+            hbm = float(json.load(f).get("hbm_gbs", hbm))
+    print("| batch | ctx | kv rows | MB | us | GB/s | of HBM | TFLOP/s |")
+    print("|---|---|---|---|---|---|---|---|")
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = None
+    for b in (1, 16):
+        for C in (1024, 4096, 8192, 16384, 32768):
+            L = C + 32
+            q = torch.randn(b, 40, 32, 128, generator=g, device=dev).to(torch.float16)
+            k = torch.randn(b, 8, L, 128, generator=g, device=dev).to(torch.float16)
+            v = torch.randn(b, 8, L, 128, generator=g, device=dev).to(torch.float16)
+            need = K.N.load().dflash_attention_workspace_size(b, 40, 8, 32, L)
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            for _ in range(3):
+                K.attention(q, k, v, workspace=ws)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                K.attention(q, k, v, workspace=ws)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) / iters * 1e3
+            nbytes = 2 * b * 40 * 32 * 128 * 2 + 2 * b * 8 * L * 128 * 2
+            flops = 4.0 * b * 40 * 32 * L * 128
+            print(f"| {b} | {C} | {L} | {nbytes / 1e6:.1f} | {us:.1f} | {nbytes / us / 1e3:.0f} | "
+                  f"{nbytes / us / 1e3 / hbm:.2f} | {flops / us / 1e6:.0f} |")
+            del q, k, v
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
@@ -36,6 +77,10 @@ def main():
     importlib.import_module("mirror-sd_b200")
     K = importlib.import_module("mirror-sd_b200.kernels")
     dev = torch.device("cuda", 0)
+    if a.case == "attn_sweep":
+        K.N = importlib.import_module("mirror-sd_b200._native")
+        attn_sweep(K, dev, a.iters)
+        return
     g = torch.Generator(device=dev).manual_seed(0)
     M = 32
     if a.case.startswith("w8_") or a.case.startswith("w8:"):
