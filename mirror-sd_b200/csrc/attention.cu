@@ -325,6 +325,10 @@ cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_
   DFL_TRY(max_smem_carveout(attn_partial_kernel));
   e = launch_pdl(attn_partial_kernel, dim3(p.splits, p.nkv, batch), dim3(nwarps * 32), smem, st, p);
   if (e != cudaSuccess) return e;
+  return attn_combine_launch(p, batch, out, st);
+}
+
+cudaError_t attn_combine_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st) {
   const int rows = p.nq * p.block;
   DFL_TRY(max_smem_carveout(attn_combine_kernel));
   return launch_pdl(attn_combine_kernel, dim3((rows + 7) / 8, batch), dim3(256), 0, st, p, out);

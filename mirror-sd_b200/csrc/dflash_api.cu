@@ -515,7 +515,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     ap.normrope = 0;
     ap.kv = m;
     ap.omax = hd->amax;
-    CK(attn_launch(ap, b, hd->attn_out, st));
+    ap.err = hd->dev_err;
+    CK(attn_tc_launch(ap, b, hd->attn_out, st));
     // o_proj + residual
     W8Params o{};
     CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->amax, NQ, hd->xl, hd->xs, st));
@@ -848,7 +849,11 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
     p.q_norm = q_norm; p.k_norm = k_norm; p.rope = rope; p.eps = eps;
     p.q_row0 = q_pos0; p.k_row0 = k_pos0;
   }
-  CK(attn_launch(p, batch, reinterpret_cast<__half*>(out), st));
+  // the tensor-core kernel, or the mma.sync one where Q/K need the fused norm + RoPE
+  if (normrope)
+    CK(attn_launch(p, batch, reinterpret_cast<__half*>(out), st));
+  else
+    CK(attn_tc_launch(p, batch, reinterpret_cast<__half*>(out), st));
   return DFLASH_OK;
 }
 

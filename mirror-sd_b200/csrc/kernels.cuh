@@ -106,6 +106,7 @@ struct AttnParams {
   int q_row0, k_row0;   // table rows: q row j -> q_row0 + j, k row i -> k_row0 + i
   KvMap kv;             // nseq > 0: sequence s reads logical rows [0, n_att[s]) at rs_post[s]
   float* omax;          // combine: [NQ, b * block] max |out| per head and row (or NULL)
+  int* err;             // device error word for bounded waits (tcgen05 kernel), or NULL
 };
 
 enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2 };
@@ -161,7 +162,11 @@ cudaError_t quantize_q8_launch(const float* w, int oc, int ic, int8_t* q, __half
 
 size_t attn_smem_bytes(int nq, int nkv, int block);
 void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits);
+// mma.sync split kernel (also the fused QK-norm + RoPE variant) + combine
 cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
+// tcgen05 split kernel (S and O in TMEM; no normrope) + combine
+cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
+cudaError_t attn_combine_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
 
 cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
                            cudaStream_t st);
