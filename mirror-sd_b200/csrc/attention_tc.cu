@@ -7,50 +7,58 @@
 // order.  Here both products run on tcgen05 with the accumulators in TMEM:
 //
 //   S_g = Q_g K_j^T     M=128 query rows, N=64 kv rows, K=128 (kind::f16)
-//   O_g += P_g V_j      M=128, N=128 head dims, K=64 kv rows (V as an
-//                       MN-major operand: kv rows of 128-byte d chunks)
+//   O_g += P_g V_j      M=128, N=128 head dims, K=64 kv rows; P is the A
+//                       operand straight from TMEM (f16 pairs written over
+//                       its own S columns), V the B operand from shared
+//                       memory as an MN-major tile (kv rows of 128-byte d
+//                       chunks)
 //
-// The query rows are padded to NG groups of 128 (NG = 1 or 2).
+// The query rows are padded to NG groups of 128 (NG = 1 or 2).  S/P is
+// double-buffered in TMEM per group, so the MMAs of tile j+1 run while the
+// softmax works on tile j, and with P out of shared memory the K/V ring gets
+// every byte that Q leaves (5 or 6 stages in flight).
 // Roles:
 //   warps 0 .. 4NG-1  softmax, one thread per query row (TMEM lane).  Each
-//       thread reads its S row, computes base-2 exponents and the running sum,
-//       and writes P (f16) into shared memory in the UMMA 128-byte swizzle.
-//       O is rescaled in TMEM only when the running max grows by more than 2^8
-//       (P then stays below 256, exact enough in f16), so most tiles need no
-//       O traffic.
-//   4 producer warps  cp.async of the K/V tiles, each row through the KvMap
-//       (cache rings), into the swizzled stages of a 3-stage ring; a tile is
-//       signalled once the next one is issued (two tiles in flight).
-//   1 MMA warp        single-thread issue.  Order per tile: S_0, S_1, then
-//       PV_0 and the next S_0 once P_0 is ready, PV_1 ... so the softmax of one
-//       group overlaps the MMAs of the other.
+//       thread reads its S row, computes base-2 exponents (an FMA per element,
+//       one f16x2 ex2 per pair) and the running sum, and stores P into its
+//       TMEM lane.  O is rescaled in TMEM only when
+//       the running max grows by more than 2^8 (P then stays below 256), so
+//       most tiles need no O traffic.  Warps whose 32 rows are all padding
+//       take no part.
+//   4 producer warps  K/V tiles into the swizzled stages of the ring.  A full
+//       tile whose 64 rows sit in 64 consecutive slots (always in the
+//       stateless forward; in a cache ring except at the sink / wrap
+//       boundaries) is one TMA copy per 64-column half, completed by
+//       transaction bytes, so NS tiles stay in flight.  Other tiles are
+//       copied row by row through the KvMap with cp.async, zero-filling the
+//       rows past the end (stale V rows must not reach P.V).
+//   1 MMA warp        single-thread issue: S(j) of every group, then PV(j-1)
+//       of every group once its P is ready.
 // Every mbarrier wait is bounded; a timeout sets the error word and unwinds.
 #include "kernels.cuh"
 
 namespace dfl {
 
 constexpr int TA_TK = 64;                  // kv rows per tile
-constexpr int TA_NS = 3;                   // K/V stages
 constexpr int TA_PROD = 4;                 // producer warps
 constexpr int TA_KV_BYTES = TA_TK * 256;   // K (or V) of one tile: 64 rows x 128 f16
 constexpr int TA_STAGE = 2 * TA_KV_BYTES;  // K then V
 constexpr int TA_QG = 128 * 256;           // one query group: 128 rows x 128 f16
-constexpr int TA_PG = 128 * 128;           // P of one group: 128 rows x 64 f16
 constexpr float TA_RESCALE = 8.0f;         // log2 of the largest P before O is rescaled
 
 template <int NG>
 struct TaCfg {
+  static constexpr int NS = NG == 1 ? 6 : 5;  // K/V stages (shared memory allows)
   static constexpr int SOFT_WARPS = 4 * NG;
   static constexpr int PROD_WARP0 = SOFT_WARPS;
   static constexpr int MMA_WARP = SOFT_WARPS + TA_PROD;
   static constexpr int THREADS = 32 * (MMA_WARP + 1);
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = NG * TA_QG;
-  static constexpr int P_OFF = KV_OFF + TA_NS * TA_STAGE;
-  static constexpr int BAR_OFF = P_OFF + NG * TA_PG;
+  static constexpr int BAR_OFF = KV_OFF + NS * TA_STAGE;
   static constexpr size_t SMEM = (size_t)BAR_OFF + 256 + 1024;
-  static constexpr uint32_t S_COL = 0;        // S_g at g * 64
-  static constexpr uint32_t O_COL = NG * 64;  // O_g at O_COL + g * 128
+  static constexpr uint32_t S_COL = 0;            // S/P[g][buffer] at (2g + buffer) * 64
+  static constexpr uint32_t O_COL = NG * 2 * 64;  // O_g at O_COL + g * 128
   static constexpr uint32_t TMEM_COLS = NG == 1 ? 256 : 512;
 };
 
@@ -68,6 +76,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// D (TMEM) += A (TMEM, K-major, f16 pairs per column) . B (shared-memory descriptor)
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // SW128 descriptor of an MN-major operand: 64-element (128-byte) MN chunks
 // lbo_bytes apart, 8-row K groups 1024 bytes apart
@@ -81,18 +98,56 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
   return d;
 }
 
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// map_k / map_v: [batch * NKV planes][kv_cap slots][128] f16, box 64 x 64 x 1
+// non-aligned named barrier: threads of one warp may arrive at different times
+// (producer lane 0 can still be waiting on a stage while its warp-mates arrive)
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// two base-2 exponentials in one MUFU op: the f16 pair ex2(x0), ex2(x1)
+__device__ __forceinline__ uint32_t ex2_f16x2(float x0, float x1) {
+  const uint32_t a = pack_f16x2(x0, x1);
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(a));
+  return y;
+}
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+  uint32_t y;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(y) : "r"(a), "r"(b));
+  return y;
+}
+
 template <int NG>
-__global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                   const AttnParams p) {
   using C = TaCfg<NG>;
+  constexpr int TA_NS = C::NS;
   griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + TA_NS;
-  uint64_t* s_ready = empty + TA_NS;  // [NG]
-  uint64_t* p_ready = s_ready + NG;   // [NG]
-  uint64_t* o_ready = p_ready + NG;   // [NG]
+  uint64_t* s_ready = empty + TA_NS;    // [NG][2] S(j) in TMEM buffer j & 1
+  uint64_t* p_ready = s_ready + 2 * NG;  // [NG][2] P(j) stored over S(j)
+  uint64_t* pv_done = p_ready + 2 * NG;  // [NG][2] PV(j) complete (S/P buffer free, O current)
+  uint64_t* o_ready = pv_done + 2 * NG;  // [NG]
   uint64_t* q_ready = o_ready + NG;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -111,12 +166,18 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const At
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TA_NS; ++s) {
-      mbar_init(&full[s], 32 * TA_PROD);
+      mbar_init(&full[s], 1);  // producer thread 0 (with the TMA bytes, or after cp.async)
       mbar_init(&empty[s], 1);
     }
     for (int g = 0; g < NG; ++g) {
-      mbar_init(&s_ready[g], 1);
-      mbar_init(&p_ready[g], 128);
+      // softmax threads of group g: its warps holding at least one real row
+      const int rows = min(128, R - g * 128);
+      const int nthr = 32 * ((rows + 31) / 32);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&s_ready[2 * g + b], 1);
+        mbar_init(&p_ready[2 * g + b], nthr);
+        mbar_init(&pv_done[2 * g + b], 1);
+      }
       mbar_init(&o_ready[g], 1);
     }
     mbar_init(q_ready, 32 * TA_PROD);
@@ -148,82 +209,98 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const At
     mbar_arrive(q_ready);
     const __half* kg = p.k + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
     const __half* vg = p.v + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
-    int issued = 0;
+    const int plane = bi * p.nkv + kvh;
+    // Producer thread 0 alone waits for free stages and issues the TMA tiles;
+    // the other producer threads sleep on a named barrier and join only for the
+    // tiles copied row by row.  Nobody leaves the loop early: every producer
+    // thread reaches the same named barriers, and after a timeout (thread 0's
+    // `dead`) the copies are skipped while the bounded waits elsewhere unwind.
+    bool dead = false;
     for (int j = 0; j < ntiles; ++j) {
       const int s = j % TA_NS;
-      if (!mbar_wait(&empty[s], ((j / TA_NS) & 1) ^ 1, p.err, abort_flag)) break;
       uint8_t* st = smem + C::KV_OFF + s * TA_STAGE;
-      for (int idx = t; idx < TA_TK * 16; idx += 32 * TA_PROD) {
-        const int r = idx >> 4, c = idx & 15, ch = c >> 3, cc = c & 7;
-        const int row = kv0 + j * TA_TK + r;
-        const bool ok = row < kv1;
-        const int lrow = ok ? row : kv0;  // a valid address even when nothing is read
-        const size_t off = (size_t)(mapped ? kv_slot(p.kv, lrow, rs) : lrow) * 128 + c * 8;
-        const int sw = ch * (TA_TK * 128) + r * 128 + ((cc ^ (r & 7)) << 4);
-        cp_async16_zfill(smem_u32(st + sw), kg + off, ok);
-        cp_async16_zfill(smem_u32(st + TA_KV_BYTES + sw), vg + off, ok);
-      }
-      cp_async_commit();
-      ++issued;
-      // tile j-1 has landed once at most one copy group (tile j) is in flight.
-      // Signalling one tile behind keeps two tiles in flight and never holds a
-      // tile back that the MMA needs before it can free a stage.
-      if (j >= 1) {
-        cp_async_wait<1>();
-        fence_proxy_async_smem();
-        mbar_arrive(&full[(j - 1) % TA_NS]);
+      const int row0 = kv0 + j * TA_TK;
+      const int slot0 = mapped ? kv_slot(p.kv, row0, rs) : row0;
+      const bool whole = row0 + TA_TK <= kv1;
+      // consecutive slots: the map is piecewise consecutive and every break
+      // (sink -> ring, ring wrap) changes the end-to-end distance
+      const bool contig = whole && (mapped ? kv_slot(p.kv, row0 + TA_TK - 1, rs) : row0 + TA_TK - 1) ==
+                                       slot0 + TA_TK - 1;
+      if (t == 0 && !dead && !mbar_wait(&empty[s], ((j / TA_NS) & 1) ^ 1, p.err, abort_flag)) dead = true;
+      if (contig) {
+        if (t == 0 && !dead) {
+          mbar_arrive_expect_tx(&full[s], TA_STAGE);
+          for (int ch = 0; ch < 2; ++ch) {
+            tma_load_3d(st + ch * (TA_TK * 128), &map_k, &full[s], ch * 64, slot0, plane);
+            tma_load_3d(st + TA_KV_BYTES + ch * (TA_TK * 128), &map_v, &full[s], ch * 64, slot0, plane);
+          }
+        }
+      } else {
+        named_bar_sync(1, 32 * TA_PROD);  // thread 0 has seen the stage free
+        if (!*abort_flag) {
+          for (int idx = t; idx < TA_TK * 16; idx += 32 * TA_PROD) {
+            const int r = idx >> 4, c = idx & 15, ch = c >> 3, cc = c & 7;
+            const int row = row0 + r;
+            const bool ok = row < kv1;
+            const int lrow = ok ? row : kv0;  // a valid address even when nothing is read
+            const size_t off = (size_t)(mapped ? kv_slot(p.kv, lrow, rs) : lrow) * 128 + c * 8;
+            const int sw = ch * (TA_TK * 128) + r * 128 + ((cc ^ (r & 7)) << 4);
+            cp_async16_zfill(smem_u32(st + sw), kg + off, ok);
+            cp_async16_zfill(smem_u32(st + TA_KV_BYTES + sw), vg + off, ok);
+          }
+          cp_async_commit();
+          cp_async_wait<0>();  // rare (partial or boundary tiles): no overlap needed
+          fence_proxy_async_smem();
+        }
+        named_bar_sync(1, 32 * TA_PROD);
+        if (t == 0 && !dead) mbar_arrive(&full[s]);
       }
     }
-    cp_async_wait<0>();
-    fence_proxy_async_smem();
-    if (issued > 0) mbar_arrive(&full[(issued - 1) % TA_NS]);
   } else if (warp == C::MMA_WARP) {
-    // ---- single-thread MMA issue
+    // ---- single-thread MMA issue: S(j) of every group, then PV(j-1)
     if (lane == 0 && ntiles > 0) {
       constexpr uint32_t idesc_s = umma_idesc_f16(128, TA_TK, 0);
       constexpr uint32_t idesc_o = umma_idesc_f16(128, 128, 0) | (1u << 16);  // B (V) MN-major
-      const uint32_t qa = smem_u32(smem + C::Q_OFF), kva = smem_u32(smem + C::KV_OFF),
-                     pa = smem_u32(smem + C::P_OFF);
-      auto issue_s = [&](int g, int s) {
+      const uint32_t qa = smem_u32(smem + C::Q_OFF), kva = smem_u32(smem + C::KV_OFF);
+      auto issue_s = [&](int g, int s, int b) {
         for (int kk = 0; kk < 8; ++kk) {
           const int ch = kk >> 2, w = kk & 3;
           const uint64_t ad = umma_desc_sw128(qa + g * TA_QG + ch * (128 * 128)) + 2 * w;
           const uint64_t bd = umma_desc_sw128(kva + s * TA_STAGE + ch * (TA_TK * 128)) + 2 * w;
-          umma_f16(tmem + C::S_COL + g * TA_TK, ad, bd, idesc_s, kk > 0);
+          umma_f16(tmem + C::S_COL + (2 * g + b) * TA_TK, ad, bd, idesc_s, kk > 0);
         }
       };
-      auto issue_pv = [&](int g, int s, bool acc) {
+      auto issue_pv = [&](int g, int s, int b, bool acc) {
         for (int ks = 0; ks < TA_TK / 16; ++ks) {
-          const uint64_t ad = umma_desc_sw128(pa + g * TA_PG) + 2 * ks;
+          // P: 16 kv columns of f16 pairs = 8 TMEM columns per K step
+          const uint32_t pt = tmem + C::S_COL + (2 * g + b) * TA_TK + ks * 8;
           const uint64_t bd = umma_desc_sw128_mn(kva + s * TA_STAGE + TA_KV_BYTES + ks * 2048, TA_TK * 128);
-          umma_f16(tmem + C::O_COL + g * 128, ad, bd, idesc_o, (acc || ks > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + C::O_COL + g * 128, pt, bd, idesc_o, (acc || ks > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(q_ready, 0, p.err, abort_flag) && mbar_wait(&full[0], 0, p.err, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        for (int g = 0; g < NG; ++g) {
-          issue_s(g, 0);
-          umma_commit(&s_ready[g]);
-        }
-      }
-      for (int j = 0; j < ntiles && ok; ++j) {
-        const int s = j % TA_NS, s1 = (j + 1) % TA_NS;
-        for (int g = 0; g < NG && ok; ++g) {
-          if (!mbar_wait(&p_ready[g], j & 1, p.err, abort_flag)) { ok = false; break; }
+      bool ok = mbar_wait(q_ready, 0, p.err, abort_flag);
+      for (int j = 0; j <= ntiles && ok; ++j) {
+        if (j < ntiles) {
+          const int s = j % TA_NS, b = j & 1;
+          if (!mbar_wait(&full[s], (j / TA_NS) & 1, p.err, abort_flag)) break;
           tc_fence_after();
-          issue_pv(g, s, j > 0);
-          if (g == NG - 1) umma_commit(&empty[s]);  // every read of stage s is issued
-          if (j + 1 < ntiles) {
-            if (g == 0) {
-              if (!mbar_wait(&full[s1], ((j + 1) / TA_NS) & 1, p.err, abort_flag)) { ok = false; break; }
-              tc_fence_after();
-            }
-            issue_s(g, s1);
-            umma_commit(&s_ready[g]);
-          } else {
-            umma_commit(&o_ready[g]);
+          for (int g = 0; g < NG && ok; ++g) {
+            // S(j) overwrites the S/P buffer PV(j-2) read: tcgen05.mma ops of
+            // one thread execute in issue order, so no wait is needed here
+            issue_s(g, s, b);
+            umma_commit(&s_ready[2 * g + b]);
           }
+        }
+        if (j >= 1 && ok) {
+          const int jj = j - 1, s = jj % TA_NS, b = jj & 1;
+          for (int g = 0; g < NG && ok; ++g) {
+            if (!mbar_wait(&p_ready[2 * g + b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(g, s, b, jj > 0);
+            umma_commit(&pv_done[2 * g + b]);
+            if (jj == ntiles - 1) umma_commit(&o_ready[g]);
+          }
+          umma_commit(&empty[s]);  // every read of stage s is issued
         }
       }
     }
@@ -233,36 +310,49 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const At
     const int r = 32 * (warp & 3) + lane;
     const int qrow = g * 128 + r;
     const bool valid = qrow < R;
+    const bool active = g * 128 + 32 * (warp & 3) < R;  // the warp holds a real row
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
-    const uint32_t s_t = tmem + C::S_COL + g * TA_TK + lane_off;
     const uint32_t o_t = tmem + C::O_COL + g * 128 + lane_off;
-    uint8_t* prow = smem + C::P_OFF + g * TA_PG + r * 128;
+    const float c = p.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!mbar_wait(&s_ready[g], j & 1, p.err, abort_flag)) { ok = false; break; }
+    for (int j = 0; j < ntiles && active; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_ready[2 * g + b], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t a[32], b[32];
-      tmem_ld32(s_t, a);
-      tmem_ld32(s_t + 32, b);
-      tmem_ld_wait();
-      const int nvalid = kv1 - (kv0 + j * TA_TK);  // >= 1
-      float sv[TA_TK];
-      float mx = -INFINITY;
+      uint32_t sv[TA_TK];
+      const uint32_t s_t = tmem + C::S_COL + (2 * g + b) * TA_TK + lane_off;
+      {
+        uint32_t a[32], bb[32];
+        tmem_ld32(s_t, a);
+        tmem_ld32(s_t + 32, bb);
+        tmem_ld_wait();
 #pragma unroll
-      for (int e = 0; e < TA_TK; ++e) {
-        float v = __uint_as_float(e < 32 ? a[e] : b[e - 32]) * p.scale_log2;
-        if (e >= nvalid) v = -INFINITY;
-        sv[e] = v;
-        mx = fmaxf(mx, v);
+        for (int e = 0; e < 32; ++e) {
+          sv[e] = a[e];
+          sv[32 + e] = bb[e];
+        }
       }
-      // rescale O only when the max has grown by more than 2^8 (warp-uniform
-      // TMEM traffic; lanes that need no rescale multiply by 1)
-      const bool grow = mx > m_used + TA_RESCALE;
-      const float m_new = grow ? mx : m_used;
+      const int nvalid = kv1 - (kv0 + j * TA_TK);  // >= 1
+      float mx = -INFINITY;
+      if (nvalid >= TA_TK) {
+#pragma unroll
+        for (int e = 0; e < TA_TK; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < TA_TK; ++e)
+          if (e < nvalid) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      }
+      // scores in base-2 units: s * c with c = log2(e) / sqrt(128) > 0, so the
+      // max commutes with the scaling
+      const float m_cand = mx * c;
+      const bool grow = m_cand > m_used + TA_RESCALE;
+      const float m_new = grow ? m_cand : m_used;
       if (__any_sync(0xffffffffu, grow) && j > 0) {
-        // O holds tiles < j: PV(j-1) was issued before S(j), so it is complete
-        const float f = grow ? exp2f(m_used - m_new) : 1.f;
+        // O must hold tiles < j before it is rescaled
+        if (!mbar_wait(&pv_done[2 * g + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const float f = grow ? ex2_approx(m_used - m_new) : 1.f;
 #pragma unroll 1
         for (int cblk = 0; cblk < 4; ++cblk) {
           uint32_t o[32];
@@ -276,23 +366,33 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const At
         l *= f;
       }
       m_used = m_new;
+      // P = 2^(s c - m) two at a time in f16 (the MMA consumes f16 P anyway);
+      // masked columns get -inf, hence 0.  The row sum adds f16 pairs in
+      // groups of 8 (at most 8 * 256, exact to 2^-10) and then in fp32.
       uint32_t pk[TA_TK / 2];
+      const float neg_m = -m_used;
 #pragma unroll
       for (int e = 0; e < TA_TK; e += 2) {
-        const float p0 = exp2f(sv[e] - m_used), p1 = exp2f(sv[e + 1] - m_used);
-        l += p0 + p1;
-        pk[e / 2] = pack_f16x2(p0, p1);
+        const float x0 = e < nvalid ? fmaf(__uint_as_float(sv[e]), c, neg_m) : -INFINITY;
+        const float x1 = e + 1 < nvalid ? fmaf(__uint_as_float(sv[e + 1]), c, neg_m) : -INFINITY;
+        pk[e / 2] = ex2_f16x2(x0, x1);
       }
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc)
-        *reinterpret_cast<uint4*>(prow + ((cc ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-      fence_proxy_async_smem();  // P visible to the tensor core
+      for (int q = 0; q < TA_TK / 2; q += 4) {
+        const uint32_t s4 = hadd2_u(hadd2_u(pk[q], pk[q + 1]), hadd2_u(pk[q + 2], pk[q + 3]));
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&s4));
+        l += f.x + f.y;
+      }
+      // P over the first 32 columns of this S buffer (its S values are read)
+      tmem_st32(s_t, pk);
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_ready[g]);
+      mbar_arrive(&p_ready[2 * g + b]);
     }
     float* orow = p.opart + (pbase + (valid ? qrow : 0)) * 128;
-    if (ntiles == 0 || !ok) {
+    if (!active) {
+      // padding rows only: nothing to write
+    } else if (ntiles == 0 || !ok) {
       if (valid) {
         for (int d = 0; d < 128; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(0.f, 0.f, 0.f, 0.f);
         p.mpart[pbase + qrow] = -INFINITY;
@@ -327,13 +427,42 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1) attn_tc_kernel(const At
   }
 }
 
+typedef CUresult (*EncodeTiledFnA)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [planes][slots][128] f16 -> box 64 x 64 x 1 with the 128-byte swizzle
+static bool map_kv(CUtensorMap* m, const void* base, uint64_t slots, uint64_t planes) {
+  static EncodeTiledFnA enc = nullptr;
+  if (!enc) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    enc = reinterpret_cast<EncodeTiledFnA>(ptr);
+  }
+  if (reinterpret_cast<uintptr_t>(base) & 15) return false;
+  cuuint64_t dims[3] = {128, slots, planes};
+  cuuint64_t strides[2] = {256, slots * 256};
+  cuuint32_t box[3] = {64, (cuuint32_t)TA_TK, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int NG>
 static cudaError_t attn_tc_launch_t(const AttnParams& p, int batch, cudaStream_t st) {
   using C = TaCfg<NG>;
   auto kern = attn_tc_kernel<NG>;
+  CUtensorMap mk, mv;
+  if (!map_kv(&mk, p.k, p.kv_cap, (uint64_t)batch * p.nkv) || !map_kv(&mv, p.v, p.kv_cap, (uint64_t)batch * p.nkv))
+    return cudaErrorInvalidValue;
   DFL_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
   DFL_TRY(max_smem_carveout(kern));
-  return launch_pdl(kern, dim3(p.splits, p.nkv, batch), dim3(C::THREADS), C::SMEM, st, p);
+  return launch_pdl(kern, dim3(p.splits, p.nkv, batch), dim3(C::THREADS), C::SMEM, st, mk, mv, p);
 }
 
 cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st) {

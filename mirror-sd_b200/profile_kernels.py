@@ -12,6 +12,7 @@ Cases (27B-class draft dims, 32 block rows):
   w8:N:K   any W8A16 shape (N, K multiples of 128)
   lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
   attn     block attention            40/8 heads, 32 queries, kv 4128
+  attn16   the same at batch 16, kv 32800 (2.1 GB of K/V)
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
   attn_sweep  block attention, 40/8 heads, 32 queries, ctx 1K..32K, batch 1 and 16
               (prints a markdown table: time, bandwidth, fraction of measured HBM)
@@ -101,14 +102,14 @@ def main():
         ws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.lm_head_argmax(hn, E, workspace=ws)
         nbytes, flops = V * H * 2, 2 * (M - 1) * V * H
-    elif a.case == "attn":
-        L = 4128
-        qq = torch.randn(1, 40, M, 128, generator=g, device=dev).to(torch.float16)
-        kk = torch.randn(1, 8, L, 128, generator=g, device=dev).to(torch.float16)
-        vv = torch.randn(1, 8, L, 128, generator=g, device=dev).to(torch.float16)
+    elif a.case in ("attn", "attn16"):
+        bsz, L = (1, 4128) if a.case == "attn" else (16, 32800)
+        qq = torch.randn(bsz, 40, M, 128, generator=g, device=dev).to(torch.float16)
+        kk = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
+        vv = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
         ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.attention(qq, kk, vv, workspace=ws)
-        nbytes, flops = 2 * 8 * L * 128 * 2, 4 * 40 * M * L * 128
+        nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * 40 * M * L * 128
     elif a.case == "fc":
         Mr, Kd, N = 4096, 25600, 5120
         A = torch.randn(Mr, Kd, generator=g, device=dev).to(torch.bfloat16)
