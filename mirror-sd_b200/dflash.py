@@ -89,6 +89,21 @@ class DFlashConfig:
             cfg.rope_scaling = d["rope_scaling"]
         return cfg
 
+    def to_dict(self) -> dict:
+        """HF-style ``config.json`` content that ``from_dict`` reads back
+        unchanged (the draft fields under ``dflash_config``)."""
+        d = {"hidden_size": self.hidden_size, "num_hidden_layers": self.num_hidden_layers,
+             "intermediate_size": self.intermediate_size, "num_attention_heads": self.num_attention_heads,
+             "num_key_value_heads": self.num_key_value_heads, "head_dim": self.head_dim,
+             "rms_norm_eps": self.rms_norm_eps, "rope_theta": self.rope_theta,
+             "max_position_embeddings": self.max_position_embeddings, "vocab_size": self.vocab_size,
+             "dflash_config": {"block_size": self.block_size, "mask_token_id": self.mask_token_id,
+                               "num_target_layers": self.num_target_layers,
+                               "target_layer_ids": list(self.target_layer_ids)}}
+        if getattr(self, "rope_scaling", None) is not None:
+            d["rope_scaling"] = self.rope_scaling
+        return d
+
 
 def build_target_layer_ids(num_target_layers: int, num_draft_layers: int) -> List[int]:
     """Evenly spaced target layers in [1, n-3] (dflash.py:108-119)."""
