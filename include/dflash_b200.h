@@ -131,6 +131,24 @@ typedef struct DFlashForwardArgs {
   const int32_t* ctx_lens;        /* HOST array [batch] of C_s, or NULL */
   const int32_t* rope_offsets;    /* HOST array [batch], or NULL; not used with a cache */
   void* cache;                    /* from dflash_cache_create, or NULL (cache=None) */
+  /* Soft anchor (generate.py:1422-1436): when anchor_logits is not NULL, row 0
+   * of every sequence's block is not read from `noise` but embedded as the
+   * softmax-weighted sum of the top-k rows of lm_head under that sequence's
+   * logits (the previous verify step at the correction position,
+   * generate.py:1639).  NULL keeps the hard anchor (the first step). */
+  const void* anchor_logits;      /* device [batch, anchor_logits_ld], fp32 or bf16 */
+  int64_t anchor_logits_ld;       /* elements between rows; 0 = vocab_size */
+  int32_t anchor_logits_bf16;
+  int32_t anchor_top_k;           /* 1..16; 0 = 8, the reference's k */
+  /* extract_context_feature fused into the fc GEMM (dflash.py:122-130): when
+   * target_layers is not NULL, target_hidden is not read; the fc GEMM loads
+   * its A operand from the F selected target layers where they lie.
+   * target_layers is a HOST array of num_target_features device pointers,
+   * layer f holding bf16 [sum_s C_s, H] context rows (packed like
+   * target_hidden) target_layers_ld elements apart (0 = H; 16-byte aligned
+   * base and row pitch). */
+  const uint16_t* const* target_layers;
+  int64_t target_layers_ld;
 } DFlashForwardArgs;
 
 #define DFLASH_PHASES 8
@@ -234,6 +252,17 @@ int dflash_attention_noalloc(const uint16_t* q, const uint16_t* k, const uint16_
  * final-normed hidden rows: hn [batch, block, H] bf16, E [V, H] bf16; writes
  * tokens [batch, block-1] for rows 1..block-1 (generate.py:604-606, :722-728).
  * workspace: dflash_lm_head_workspace_size() bytes. */
+/* Soft anchor on its own (generate.py:1422-1436): for each of `batch` rows
+ * of logits ([batch, ld], fp32 or bf16 when logits_bf16), the k largest
+ * entries (larger first, lower index first on ties), their fp32 softmax, and
+ * out[row] = bf16(sum_q w_q * E[id_q]) with E [V, H] bf16 row-major
+ * (H % 8 == 0, 16-byte aligned).  workspace: dflash_soft_anchor_workspace_size()
+ * bytes. */
+size_t dflash_soft_anchor_workspace_size(int batch);
+int dflash_soft_anchor(const void* logits, int logits_bf16, int batch, int V, int64_t ld, int k,
+                       const uint16_t* E, int H, uint16_t* out, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 size_t dflash_lm_head_workspace_size(int batch, int block);
 int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H,
                           int V, int32_t* tokens, const int32_t* target, int32_t* acc_len,

@@ -6,12 +6,12 @@ carries a hyphen).  The compute path is the CUDA library ``lib/libdflash_b200.so
 """
 from . import _native
 from .dflash import (DFlashCache, DFlashConfig, DFlashDraftModel, DFlashKVCache, DFlashWeightsQ8, Q8Layer,
-                     accept, build_target_layer_ids, extract_context_feature, quantize_q8, sample)
+                     accept, build_target_layer_ids, context_layers, extract_context_feature, quantize_q8, sample)
 from .weights import synth_weights_q8, weights_from_q8_numpy
 from .generate import SpecDecodeStats, spec_generate
 from .loader import load_dflash_model, load_dflash_weights, save_q8_checkpoint
 
 __all__ = ["DFlashCache", "DFlashConfig", "DFlashDraftModel", "DFlashKVCache", "DFlashWeightsQ8", "Q8Layer",
-           "accept", "build_target_layer_ids", "extract_context_feature", "quantize_q8", "sample",
+           "accept", "build_target_layer_ids", "context_layers", "extract_context_feature", "quantize_q8", "sample",
            "synth_weights_q8", "weights_from_q8_numpy", "SpecDecodeStats", "spec_generate",
            "load_dflash_model", "load_dflash_weights", "save_q8_checkpoint"]

@@ -51,7 +51,10 @@ class DFlashForwardArgs(ctypes.Structure):
                 ("acc_len", c_void_p), ("correction", c_void_p),
                 ("phase_events", ctypes.POINTER(c_void_p)), ("n_phase_events", c_int32),
                 ("ctx_lens", ctypes.POINTER(c_int32)), ("rope_offsets", ctypes.POINTER(c_int32)),
-                ("cache", c_void_p)]
+                ("cache", c_void_p),
+                ("anchor_logits", c_void_p), ("anchor_logits_ld", ctypes.c_int64),
+                ("anchor_logits_bf16", c_int32), ("anchor_top_k", c_int32),
+                ("target_layers", ctypes.POINTER(c_void_p)), ("target_layers_ld", ctypes.c_int64)]
 
 
 DFLASH_PHASES = 8
@@ -85,6 +88,10 @@ EXPORTS = {
                                    ctypes.c_int, c_void_p, c_void_p]),
     "dflash_tc_gemm": (c_int32, [c_void_p, c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_int, c_void_p, c_void_p]),
+    "dflash_soft_anchor_workspace_size": (c_size_t, [ctypes.c_int]),
+    "dflash_soft_anchor": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
+                                     ctypes.c_int, c_void_p, ctypes.c_int, c_void_p, c_void_p, c_size_t,
+                                     c_void_p]),
     "dflash_attention_workspace_size": (c_size_t, [ctypes.c_int] * 5),
     "dflash_attention": (c_int32, [c_void_p, c_void_p, c_void_p, ctypes.c_int, ctypes.c_int,
                                    ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,

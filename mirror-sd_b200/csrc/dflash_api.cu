@@ -101,6 +101,10 @@ struct Handle {
   float* w8_part = nullptr;          // split-K partials of the W8A16 projections
   size_t w8_part_floats = 0;
   int* w8_cnt = nullptr;             // per-tile arrival counters (zero between launches)
+  __nv_bfloat16* anchor = nullptr;   // [max_batch, H] soft anchor rows
+  float* sa_cand_v = nullptr;        // [max_batch, kSaMaxCtas, kSaMaxK] soft anchor candidates
+  int* sa_cand_i = nullptr;
+  int* sa_cnt = nullptr;             // [max_batch] arrival counters (zero between launches)
   int last_launches = 0;
 };
 
@@ -325,6 +329,14 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   }
   CKC(A.alloc(&hd->dev_err, 1));
   CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
+  {
+    const size_t nc = (size_t)d.max_batch * kSaMaxCtas * kSaMaxK;
+    CKC(A.alloc(&hd->anchor, (size_t)d.max_batch * H));
+    CKC(A.alloc(&hd->sa_cand_v, nc));
+    CKC(A.alloc(&hd->sa_cand_i, nc));
+    CKC(A.alloc(&hd->sa_cnt, (size_t)d.max_batch));
+    CKC(cudaMemset(hd->sa_cnt, 0, (size_t)d.max_batch * sizeof(int)));
+  }
   CKC(cudaDeviceSynchronize());
 #undef CKC
   *out = hd;
@@ -380,10 +392,37 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     cmax = std::max(cmax, c);
   }
   const int Ctot = m.ctx_start[b];
-  if (!a->noise || (Ctot > 0 && !a->target_hidden))
+  if (!a->noise || (Ctot > 0 && !a->target_hidden && !a->target_layers))
     return fail(DFLASH_ERR_INVALID, "noise / target_hidden must not be NULL");
+  TcSources fc_src{};
+  if (Ctot > 0) {
+    if (a->target_layers) {
+      if (F > kTcMaxSrc) return fail(DFLASH_ERR_INVALID, "target_layers: %d features above %d", F, kTcMaxSrc);
+      const long long ld = a->target_layers_ld ? a->target_layers_ld : H;
+      if (ld < H || ld % 8) return fail(DFLASH_ERR_INVALID, "target_layers_ld %lld: not >= %d and a multiple of 8", ld, H);
+      for (int f = 0; f < F; ++f) {
+        if (!a->target_layers[f] || (reinterpret_cast<uintptr_t>(a->target_layers[f]) & 15))
+          return fail(DFLASH_ERR_INVALID, "target_layers[%d] is NULL or not 16-byte aligned", f);
+        fc_src.ptr[f] = a->target_layers[f];
+        fc_src.ld[f] = ld;
+      }
+      fc_src.n = F;
+      fc_src.cols = H;
+    } else {
+      fc_src.ptr[0] = a->target_hidden;
+      fc_src.ld[0] = (long long)F * H;
+      fc_src.n = 1;
+      fc_src.cols = F * H;
+    }
+  }
   if (a->target_tokens && (!a->acc_len || !a->correction))
     return fail(DFLASH_ERR_INVALID, "acc_len and correction are required with target_tokens");
+  const int top_k = a->anchor_top_k ? a->anchor_top_k : 8;
+  const long long anchor_ld = a->anchor_logits_ld ? a->anchor_logits_ld : d.vocab_size;
+  if (a->anchor_logits && (top_k < 1 || top_k > kSaMaxK || top_k > d.vocab_size))
+    return fail(DFLASH_ERR_INVALID, "anchor_top_k %d outside [1, %d]", top_k, kSaMaxK);
+  if (a->anchor_logits && anchor_ld < d.vocab_size)
+    return fail(DFLASH_ERR_INVALID, "anchor_logits_ld %lld below vocab_size %d", anchor_ld, d.vocab_size);
   Cache* cc = static_cast<Cache*>(a->cache);
   if (cc && cc->owner != hd) return fail(DFLASH_ERR_INVALID, "the cache belongs to another handle");
   if (cc && b > cc->max_batch)
@@ -459,8 +498,17 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
 
   CK(mark(0));
   CK(rope_table_map_launch(m, B, hd->inv_freq, hd->rope, st));
+  if (a->anchor_logits) {
+    SaParams sp{};
+    sp.logits = a->anchor_logits; sp.logits_bf16 = a->anchor_logits_bf16 != 0;
+    sp.V = d.vocab_size; sp.ld = anchor_ld; sp.k = top_k;
+    sp.E = hd->lm_tiles; sp.H = H; sp.out = hd->anchor; sp.out_ld = H;
+    sp.cand_v = hd->sa_cand_v; sp.cand_i = hd->sa_cand_i; sp.counter = hd->sa_cnt;
+    CK(soft_anchor_launch(sp, b, true, hd->num_sms, st));
+    launches += 1;
+  }
   CK(init_h_launch(reinterpret_cast<const __nv_bfloat16*>(a->noise), M, H, hd->h, hd->hstat,
-                   hd->layers[0].in_norm, hd->hmax, st));
+                   hd->layers[0].in_norm, hd->hmax, a->anchor_logits ? hd->anchor : nullptr, B, st));
   launches += 2;
   CK(mark(1));
 
@@ -468,7 +516,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     TcParams fp{};
     fp.M = Ctot; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
     fp.out_f32 = hd->ctx_raw; fp.sumsq_part = hd->ctx_part;
-    CK(tc_gemm_launch(a->target_hidden, hd->fc, true, kTcFc, fp, st));
+    CK(tc_gemm_launch_src(fc_src, hd->fc, true, kTcFc, fp, st));
     CK(mark(2));
     CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, Ctot, H, hd->hidden_norm, d.rms_norm_eps,
                        hd->ctx_n, st));
@@ -854,6 +902,39 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
     CK(attn_launch(p, batch, reinterpret_cast<__half*>(out), st));
   else
     CK(attn_tc_launch(p, batch, reinterpret_cast<__half*>(out), st));
+  return DFLASH_OK;
+}
+
+size_t dflash_soft_anchor_workspace_size(int batch) {
+  if (batch < 1) return 0;
+  return (size_t)batch * kSaMaxCtas * kSaMaxK * 8 + (size_t)batch * sizeof(int) + 256;
+}
+
+int dflash_soft_anchor(const void* logits, int logits_bf16, int batch, int V, int64_t ld, int k,
+                       const uint16_t* E, int H, uint16_t* out, void* workspace, size_t ws_bytes,
+                       void* stream) {
+  if (!logits || !E || !out || !workspace) return fail(DFLASH_ERR_INVALID, "NULL pointer");
+  if (batch < 1 || V < 1 || ld < V || H < 8 || H % 8)
+    return fail(DFLASH_ERR_INVALID, "bad soft anchor shape (batch %d, V %d, ld %lld, H %d)", batch, V,
+                (long long)ld, H);
+  if (k < 1 || k > kSaMaxK || k > V) return fail(DFLASH_ERR_INVALID, "k %d outside [1, %d]", k, kSaMaxK);
+  if ((reinterpret_cast<uintptr_t>(E) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(DFLASH_ERR_INVALID, "E and out must be 16-byte aligned");
+  if (ws_bytes < dflash_soft_anchor_workspace_size(batch))
+    return fail(DFLASH_ERR_INVALID, "workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const size_t nc = (size_t)batch * kSaMaxCtas * kSaMaxK;
+  SaParams p{};
+  p.logits = logits; p.logits_bf16 = logits_bf16 != 0; p.V = V; p.ld = ld; p.k = k;
+  p.E = E; p.H = H; p.out = reinterpret_cast<__nv_bfloat16*>(out); p.out_ld = H;
+  p.cand_v = static_cast<float*>(workspace);
+  p.cand_i = reinterpret_cast<int*>(p.cand_v + nc);
+  p.counter = p.cand_i + nc;
+  CK(cudaMemsetAsync(p.counter, 0, (size_t)batch * sizeof(int), st));
+  CK(soft_anchor_launch(p, batch, false, sms, st));
   return DFLASH_OK;
 }
 

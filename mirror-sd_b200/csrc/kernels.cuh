@@ -113,6 +113,7 @@ enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2 };
 
 struct TcParams {
   int M, N, K;
+  int a_cols;               // K columns per A source (tc_gemm_launch_src); K for one source
   int* err;
   // kTcFc and kTcStoreF32
   float* out_f32;           // [M, N]
@@ -168,6 +169,17 @@ cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_
 cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
 cudaError_t attn_combine_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
 
+// A given as column blocks held in separate arrays: A[:, f*cols:(f+1)*cols] is
+// ptr[f] (rows ld[f] elements apart), f < n; n * cols == K
+constexpr int kTcMaxSrc = 8;
+struct TcSources {
+  const void* ptr[kTcMaxSrc];
+  long long ld[kTcMaxSrc];
+  int n;
+  int cols;
+};
+cudaError_t tc_gemm_launch_src(const TcSources& a, const void* B, bool bf16, int mode, TcParams p,
+                               cudaStream_t st);
 cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
                            cudaStream_t st);
 
@@ -182,12 +194,32 @@ cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int
 cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch, int block,
                           int32_t* acc_len, int32_t* correction, cudaStream_t st);
 
+// soft anchor (anchor.cu): rows of logits -> bf16 weighted embedding rows
+constexpr int kSaMaxK = 16;        // top-k bound
+constexpr int kSaMaxCtas = 160;    // CTAs per row bound (candidate workspace)
+struct SaParams {
+  const void* logits;   // [rows, ld] fp32, or bf16 when logits_bf16
+  int logits_bf16;
+  int V;
+  long long ld;         // elements between rows of logits
+  int k;
+  const void* E;        // bf16 [V, H] row-major, or lm_pack tiles
+  int H;
+  __nv_bfloat16* out;   // [rows, out_ld]
+  long long out_ld;
+  float* cand_v;        // [rows, kSaMaxCtas, kSaMaxK]
+  int* cand_i;
+  int* counter;         // [rows], zero between launches
+};
+int soft_anchor_ctas(int V, int rows, int num_sms);
+cudaError_t soft_anchor_launch(const SaParams& p, int rows, bool e_tiled, int num_sms, cudaStream_t st);
 cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st);
 // table rows of one forward: packed context rows, then nseq * block block rows (KvMap)
 cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
                                   cudaStream_t st);
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
-                          const float* w, float* hmax, cudaStream_t st);
+                          const float* w, float* hmax, const __nv_bfloat16* anchor, int block,
+                          cudaStream_t st);
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st);
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,

@@ -48,18 +48,22 @@ __global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
 
 // h = noise (fp32) with its sum of squares and max |h * w| (w: the first
 // layer's input RMSNorm weight) for the limb split of the first projection;
-// one CTA per row
+// one CTA per row.  With `anchor` ([M / block, H], the soft anchor rows), row
+// 0 of every block is read from there instead of from the noise.
 __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, int H,
                               float* __restrict__ h, float* __restrict__ hstat,
-                              const float* __restrict__ w, float* __restrict__ hmax) {
+                              const float* __restrict__ w, float* __restrict__ hmax,
+                              const __nv_bfloat16* __restrict__ anchor, int block) {
   griddep_wait();
   griddep_launch_dependents();
   __shared__ float red[2][32];
   const int row = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const __nv_bfloat16* src = (anchor && row % block == 0) ? anchor + (size_t)(row / block) * H
+                                                          : noise + (size_t)row * H;
   float ss = 0.f, mw = 0.f;
   for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(noise + (size_t)row * H + k);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + k);
     const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + k));
     const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + k + 4));
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
@@ -192,10 +196,12 @@ cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_fr
                     rows, inv_freq, out);
 }
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
-                          const float* w, float* hmax, cudaStream_t st) {
-  if (H % 8) return cudaErrorInvalidValue;
+                          const float* w, float* hmax, const __nv_bfloat16* anchor, int block,
+                          cudaStream_t st) {
+  if (H % 8 || block < 1) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(init_h_kernel));
-  return launch_pdl(init_h_kernel, dim3(M), dim3(256), 0, st, noise, M, H, h, hstat, w, hmax);
+  return launch_pdl(init_h_kernel, dim3(M), dim3(256), 0, st, noise, M, H, h, hstat, w, hmax, anchor,
+                    block);
 }
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st) {

@@ -49,9 +49,15 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 
 
 
-template <int AB_FMT, int MODE>
+// tensor maps of the A column blocks (one, or one per source array)
+template <int NSRC>
+struct TcAMaps {
+  CUtensorMap m[NSRC];
+};
+
+template <int AB_FMT, int MODE, int NSRC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+    tc_gemm_kernel(const __grid_constant__ TcAMaps<NSRC> maps_a, const __grid_constant__ CUtensorMap map_b,
                    const TcParams p) {
   griddep_wait();
   griddep_launch_dependents();
@@ -81,7 +87,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     *abort_flag = 0;
     fence_mbar_init();
-    prefetch_tmap(&map_a);
+    for (int f = 0; f < NSRC && f * p.a_cols < p.K; ++f) prefetch_tmap(&maps_a.m[f]);
     prefetch_tmap(&map_b);
   }
   if (warp == 1) {
@@ -106,7 +112,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) { ok = false; break; }
           uint8_t* sa = smem + s * TC_STAGE_BYTES;
           mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
-          tma_load_2d(sa, &map_a, &full[s], kb * TC_BK, mb * TC_BM);
+          int col = kb * TC_BK, f = 0;
+          if (NSRC > 1) {
+            f = col / p.a_cols;
+            col -= f * p.a_cols;
+          }
+          tma_load_2d(sa, &maps_a.m[f], &full[s], col, mb * TC_BM);
           tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, nb * TC_BN);
         }
       }
@@ -282,14 +293,15 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D K-major map: inner dim K (elements), outer dim rows; box 64 x box_rows, 128B swizzle
-static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t K, uint64_t rows,
-                     uint32_t box_rows) {
+// 2-D K-major map: inner dim `inner` (elements), outer dim rows `ld` elements
+// apart; box 64 x box_rows, 128B swizzle
+static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t rows,
+                     uint32_t box_rows, uint64_t ld) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
-  cuuint64_t dims[2] = {K, rows};
-  cuuint64_t strides[1] = {K * 2};
+  if (!base || (reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || ld < inner) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {TC_BK, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
@@ -299,10 +311,10 @@ static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t K, 
   return r == CUDA_SUCCESS;
 }
 
-template <int FMT, int MODE>
-static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& p,
+template <int FMT, int MODE, int NSRC>
+static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, const TcParams& p,
                                cudaStream_t st) {
-  auto kern = tc_gemm_kernel<FMT, MODE>;
+  auto kern = tc_gemm_kernel<FMT, MODE, NSRC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
@@ -313,21 +325,51 @@ static cudaError_t tc_launch_t(const CUtensorMap& ma, const CUtensorMap& mb, con
   return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
 }
 
-// a_bf16: A/B element type (true: bf16, false: f16).  mode: TcMode.
-cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
-                           cudaStream_t st) {
-  if (p.M < 1 || p.N % TC_BN || p.K % TC_BK || p.K < TC_BK) return cudaErrorInvalidValue;
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, A, bf16, p.K, p.M, TC_BM) || !make_map(&mb, B, bf16, p.K, p.N, TC_BN))
-    return cudaErrorInvalidValue;
+template <int NSRC>
+static cudaError_t tc_dispatch(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, bool bf16, int mode,
+                               const TcParams& p, cudaStream_t st) {
   if (bf16) {
-    if (mode == kTcFc) return tc_launch_t<1, kTcFc>(ma, mb, p, st);
-    if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32>(ma, mb, p, st);
+    if (mode == kTcFc) return tc_launch_t<1, kTcFc, NSRC>(ma, mb, p, st);
+    if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32, NSRC>(ma, mb, p, st);
   } else {
-    if (mode == kTcCtxKV) return tc_launch_t<0, kTcCtxKV>(ma, mb, p, st);
-    if (mode == kTcStoreF32) return tc_launch_t<0, kTcStoreF32>(ma, mb, p, st);
+    if constexpr (NSRC == 1) {
+      if (mode == kTcCtxKV) return tc_launch_t<0, kTcCtxKV, 1>(ma, mb, p, st);
+    }
+    if (mode == kTcStoreF32) return tc_launch_t<0, kTcStoreF32, NSRC>(ma, mb, p, st);
   }
   return cudaErrorInvalidValue;
+}
+
+// A [M, K] and B [N, K] K-major, both bf16 or both f16.  mode: TcMode.
+cudaError_t tc_gemm_launch_src(const TcSources& a, const void* B, bool bf16, int mode, TcParams p,
+                               cudaStream_t st) {
+  if (p.M < 1 || p.N % TC_BN || p.K % TC_BK || p.K < TC_BK) return cudaErrorInvalidValue;
+  if (a.n < 1 || a.n > kTcMaxSrc || a.cols < TC_BK || a.cols % TC_BK || (long long)a.n * a.cols != p.K)
+    return cudaErrorInvalidValue;
+  p.a_cols = a.cols;
+  CUtensorMap mb;
+  if (!make_map(&mb, B, bf16, p.K, p.N, TC_BN, p.K)) return cudaErrorInvalidValue;
+  if (a.n == 1) {
+    TcAMaps<1> ma;
+    if (!make_map(&ma.m[0], a.ptr[0], bf16, a.cols, p.M, TC_BM, a.ld[0])) return cudaErrorInvalidValue;
+    return tc_dispatch<1>(ma, mb, bf16, mode, p, st);
+  }
+  if (mode == kTcCtxKV) return cudaErrorInvalidValue;
+  TcAMaps<kTcMaxSrc> ma;
+  for (int f = 0; f < a.n; ++f)
+    if (!make_map(&ma.m[f], a.ptr[f], bf16, a.cols, p.M, TC_BM, a.ld[f])) return cudaErrorInvalidValue;
+  for (int f = a.n; f < kTcMaxSrc; ++f) ma.m[f] = ma.m[0];
+  return tc_dispatch<kTcMaxSrc>(ma, mb, bf16, mode, p, st);
+}
+
+cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
+                           cudaStream_t st) {
+  TcSources a{};
+  a.ptr[0] = A;
+  a.ld[0] = p.K;
+  a.n = 1;
+  a.cols = p.K;
+  return tc_gemm_launch_src(a, B, bf16, mode, p, st);
 }
 
 }  // namespace dfl

@@ -121,6 +121,15 @@ def extract_context_feature(hidden_states, layer_ids):
     return torch.cat([hidden_states[lid + 1] for lid in layer_ids], dim=-1)
 
 
+def context_layers(hidden_states, layer_ids):
+    """The layers ``extract_context_feature`` would concatenate (dflash.py:122-130),
+    left where they are: pass the list as ``target_hidden`` and the fc GEMM
+    reads them directly, with no [*, F*H] copy."""
+    if len(hidden_states) == len(layer_ids):
+        return list(hidden_states)
+    return [hidden_states[lid + 1] for lid in layer_ids]
+
+
 def sample(logits: torch.Tensor, temperature: float = 0.0) -> torch.Tensor:
     """Greedy argmax, first index on ties (dflash.py:133-136).  Sampling with
     temperature is part of the target-side loop and is not on this path."""
@@ -389,6 +398,20 @@ class DFlashDraftModel:
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 
+    def _layer_rows(self, t, H):
+        """One target layer as [rows, H] bf16 rows on the device with unit
+        column stride and a 16-byte row pitch (a view when it already is)."""
+        t = t.to(self.device, torch.bfloat16) if (t.device != self.device or t.dtype != torch.bfloat16) else t
+        if t.shape[-1] != H:
+            raise ValueError(f"target layer width {t.shape[-1]} differs from hidden size {H}")
+        try:
+            r = t.view(-1, H)
+        except RuntimeError:
+            r = t.reshape(-1, H).contiguous()
+        if r.stride(1) != 1 or r.stride(0) % 8 or r.data_ptr() % 16:
+            r = r.contiguous()
+        return r
+
     def _as_dev(self, t, dtype):
         if t.device != self.device:
             t = t.to(self.device, non_blocking=True)
@@ -398,7 +421,7 @@ class DFlashDraftModel:
                    target_tokens=None, want_hidden: bool = True, want_tokens: bool = True,
                    out_hidden=None, out_tokens=None, acc_len=None, correction=None,
                    hidden_fp32: bool = False, phase_events=None, cache=None, ctx_lens=None,
-                   rope_offsets=None):
+                   rope_offsets=None, anchor_logits=None, anchor_top_k: int = 8):
         """One draft step on the device: final-normed hidden states (bf16, or
         fp32 with ``hidden_fp32``), greedy draft ids for rows 1..q-1 and, given
         the verifier's posterior ``target_tokens`` [b, q], the accepted length
@@ -409,28 +432,55 @@ class DFlashDraftModel:
         ``make_cache``) the rows are appended to it and the step attends to
         everything it holds; without, positions start at ``rope_offset`` (or
         ``rope_offsets`` per sequence).  ``phase_events``: optional list of 8
-        ``torch.cuda.Event`` recorded at the phase boundaries."""
+        ``torch.cuda.Event`` recorded at the phase boundaries.
+
+        ``anchor_logits`` [b, V] (fp32 or bf16; the previous verify step's
+        logits at each sequence's correction position) replaces row 0 of every
+        block with the soft anchor: the softmax-weighted sum of the
+        ``anchor_top_k`` most likely tokens' embeddings (generate.py:1422-1436),
+        computed on the device inside the step."""
         noise = self._as_dev(noise_embedding, torch.bfloat16)
-        th = self._as_dev(target_hidden, torch.bfloat16)
         if noise.dim() != 3:
             raise ValueError("noise_embedding [b, q, H] expected")
         b, q, H = noise.shape
         F = len(self.config.target_layer_ids)
+        layers = None
+        if isinstance(target_hidden, (list, tuple)):
+            # the F selected target layers, each [b, ctx, H] (or packed rows
+            # with ctx_lens): the fc GEMM reads them in place
+            if len(target_hidden) != F:
+                raise ValueError(f"target_hidden needs {F} layers, got {len(target_hidden)}")
+            layers = [self._layer_rows(t, H) for t in target_hidden]
+            if len({tuple(t.shape) for t in layers}) != 1:
+                raise ValueError("target layers differ in shape")
+            if len({t.stride(0) for t in layers}) != 1:
+                layers = [t.contiguous() for t in layers]
+            th = layers[0].new_empty((0,))
+            rows = layers[0].shape[0]
+            src_shape = tuple(target_hidden[0].shape)
+        else:
+            th = self._as_dev(target_hidden, torch.bfloat16)
+            if th.shape[-1] != F * H:
+                raise ValueError("hidden size mismatch")
+            rows = th.reshape(-1, th.shape[-1]).shape[0]
+            src_shape = tuple(th.shape)
         lens_arr = offs_arr = None
         if ctx_lens is not None:
             lens = [int(c) for c in ctx_lens]
             if len(lens) != b:
                 raise ValueError(f"ctx_lens needs {b} entries")
-            th = th.reshape(-1, th.shape[-1])
-            if th.shape[0] != sum(lens):
-                raise ValueError(f"packed target_hidden has {th.shape[0]} rows, ctx_lens sum to {sum(lens)}")
+            if layers is None:
+                th = th.reshape(-1, th.shape[-1])
+            if rows != sum(lens):
+                raise ValueError(f"packed target_hidden has {rows} rows, ctx_lens sum to {sum(lens)}")
             lens_arr = (ctypes.c_int32 * b)(*lens)
             ctx_len = max(lens) if lens else 0
         else:
-            if th.dim() != 3 or th.shape[0] != b:
-                raise ValueError("noise_embedding [b, q, H] and target_hidden [b, ctx, F*H] expected")
-            ctx_len = th.shape[1]
-        if H != self.config.hidden_size or th.shape[-1] != F * H:
+            if len(src_shape) != 3 or src_shape[0] != b:
+                raise ValueError("noise_embedding [b, q, H] and target_hidden [b, ctx, F*H] "
+                                 "(or F layers [b, ctx, H]) expected")
+            ctx_len = src_shape[1]
+        if H != self.config.hidden_size:
             raise ValueError("hidden size mismatch")
         if rope_offsets is not None:
             if len(rope_offsets) != b:
@@ -448,6 +498,17 @@ class DFlashDraftModel:
             hidden_fp32 = out_hidden.dtype == torch.float32
         if (want_tokens or target_tokens is not None) and out_tokens is None:
             out_tokens = torch.empty((b, q - 1), dtype=torch.int32, device=self.device)
+        al = None
+        if anchor_logits is not None:
+            al = anchor_logits if anchor_logits.dim() == 2 else anchor_logits.reshape(b, -1)
+            if al.dtype not in (torch.float32, torch.bfloat16):
+                al = al.to(torch.float32)
+            if al.device != self.device:
+                al = al.to(self.device)
+            if al.stride(-1) != 1:
+                al = al.contiguous()
+            if al.shape != (b, self.config.vocab_size):
+                raise ValueError(f"anchor_logits must be [{b}, {self.config.vocab_size}], got {tuple(al.shape)}")
         tt = None
         if target_tokens is not None:
             tt = self._as_dev(target_tokens, torch.int32)
@@ -458,14 +519,23 @@ class DFlashDraftModel:
         args = N.DFlashForwardArgs(
             batch=b, block=q, ctx_len=ctx_len, rope_offset=int(rope_offset),
             num_layers=int(self.num_draft_layers),
-            noise=noise.data_ptr(), target_hidden=th.data_ptr() if th.numel() else None,
+            noise=noise.data_ptr(),
+            target_hidden=th.data_ptr() if layers is None and th.numel() else None,
             out_hidden=out_hidden.data_ptr() if out_hidden is not None else None,
             out_hidden_fp32=int(bool(hidden_fp32)),
             out_tokens=out_tokens.data_ptr() if out_tokens is not None else None,
             target_tokens=tt.data_ptr() if tt is not None else None,
             acc_len=acc_len.data_ptr() if acc_len is not None else None,
             correction=correction.data_ptr() if correction is not None else None,
-            ctx_lens=lens_arr, rope_offsets=offs_arr, cache=store.ptr if store is not None else None)
+            ctx_lens=lens_arr, rope_offsets=offs_arr, cache=store.ptr if store is not None else None,
+            anchor_logits=al.data_ptr() if al is not None else None,
+            anchor_logits_ld=al.stride(0) if al is not None else 0,
+            anchor_logits_bf16=int(al is not None and al.dtype == torch.bfloat16),
+            anchor_top_k=int(anchor_top_k))
+        if layers is not None and rows > 0:
+            ptrs = (ctypes.c_void_p * F)(*[t.data_ptr() for t in layers])
+            args.target_layers = ctypes.cast(ptrs, ctypes.POINTER(ctypes.c_void_p))
+            args.target_layers_ld = layers[0].stride(0)
         if phase_events is not None:
             if len(phase_events) < N.DFLASH_PHASES:
                 raise ValueError(f"phase_events needs {N.DFLASH_PHASES} events")
@@ -487,11 +557,13 @@ class DFlashDraftModel:
                                           want_hidden=True, want_tokens=False)
         return hidden
 
-    def draft_tokens(self, noise_embedding, target_hidden, rope_offset: int = 0, cache=None):
+    def draft_tokens(self, noise_embedding, target_hidden, rope_offset: int = 0, cache=None,
+                     anchor_logits=None, anchor_top_k: int = 8):
         """lm_head + greedy argmax fused on the device: ids [b, q-1] for rows
-        1..q-1 (generate.py:604-606)."""
+        1..q-1 (generate.py:604-606); ``anchor_logits`` as in draft_step."""
         _, toks, _, _ = self.draft_step(noise_embedding, target_hidden, rope_offset,
-                                        want_hidden=False, want_tokens=True, cache=cache)
+                                        want_hidden=False, want_tokens=True, cache=cache,
+                                        anchor_logits=anchor_logits, anchor_top_k=anchor_top_k)
         return toks
 
     # -- ANE-style split API (ane_model.py:538-604) ---------------------------

@@ -18,8 +18,9 @@ that takes.
 
 The target is any object with
     embed(ids [1, n] int64) -> [1, n, H] bf16 on the draft's device
-    forward(ids [1, n], cache) -> (logits [1, n, V], features [1, n, F*H] bf16),
-        appending the n positions to ``cache``
+    forward(ids [1, n], cache) -> (logits [1, n, V], features [1, n, F*H] bf16,
+        or the F selected layers as a list of [1, n, H] tensors, which the
+        draft's fc GEMM reads in place), appending the n positions to ``cache``
     make_cache() -> an object with trim(n)
 """
 from __future__ import annotations
@@ -62,8 +63,15 @@ class SpecDecodeStats:
 @torch.no_grad()
 def spec_generate(target, draft: DFlashDraftModel, input_ids: Sequence[int], max_new_tokens: int,
                   stop_token_ids: Optional[Sequence[int]] = None,
-                  sink_size: int = 64, window_size: int = 1024) -> Tuple[List[int], SpecDecodeStats]:
-    """Greedy speculative generation.  Returns (prompt + generated ids, stats)."""
+                  sink_size: int = 64, window_size: int = 1024,
+                  soft_anchor: bool = False, anchor_top_k: int = 8) -> Tuple[List[int], SpecDecodeStats]:
+    """Greedy speculative generation.  Returns (prompt + generated ids, stats).
+
+    ``soft_anchor``: from the second step on, the draft embeds block row 0 as
+    the softmax-weighted sum of the top ``anchor_top_k`` tokens under the
+    previous verify logits at the correction position (generate.py:1422-1436,
+    :1639), on the device.  The verify pass still scores the hard anchor, so
+    the output is unchanged; only the drafts (and the acceptance) differ."""
     if not 0 <= draft.mask_token_id < draft.config.vocab_size:
         raise ValueError(f"mask_token_id {draft.mask_token_id} is not a token of the "
                          f"{draft.config.vocab_size}-entry vocabulary")
@@ -83,12 +91,14 @@ def spec_generate(target, draft: DFlashDraftModel, input_ids: Sequence[int], max
 
     dcache = draft.make_cache(sink_size=sink_size, window_size=window_size)
     B = draft.block_size
+    prev_logits = None                    # [1, V] verify logits at the last correction position
     while len(out) - n_prompt < max_new_tokens and out[-1] not in stop:
         t1 = time.perf_counter()
         anchor = out[-1]
         block = torch.tensor([[anchor] + [draft.mask_token_id] * (B - 1)], device=dev)
         noise = target.embed(block)
-        drafts = draft.draft_tokens(noise, target_hidden, cache=dcache)   # [1, B-1] int32
+        drafts = draft.draft_tokens(noise, target_hidden, cache=dcache,   # [1, B-1] int32
+                                    anchor_logits=prev_logits, anchor_top_k=anchor_top_k)
         for c in dcache:
             c.trim(B)
         t2 = time.perf_counter()
@@ -100,7 +110,10 @@ def spec_generate(target, draft: DFlashDraftModel, input_ids: Sequence[int], max
         a = int(acc[0].item())                                            # one host sync per step
         new = drafts[0, :a].tolist() + [int(corr[0].item())]
         tcache.trim(B - (a + 1))                                          # rejected positions
-        target_hidden = feats[:, :a + 1, :]
+        target_hidden = ([f[:, :a + 1, :] for f in feats] if isinstance(feats, (list, tuple))
+                         else feats[:, :a + 1, :])
+        if soft_anchor:
+            prev_logits = logits[:, a, :]
         stats.total_verify_time += time.perf_counter() - t2
         stats.total_draft_time += t2 - t1
         for tok in new:

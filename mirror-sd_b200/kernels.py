@@ -78,3 +78,30 @@ def lm_head_argmax(hn, E, target=None, workspace=None):
                                       N.ptr(acc), N.ptr(cor), N.ptr(workspace), workspace.numel(),
                                       _st(hn.device)), "dflash_lm_head_argmax")
     return toks if target is None else (toks, acc, cor)
+
+
+def soft_anchor(logits, E, top_k=8, workspace=None):
+    """Soft anchor rows (generate.py:1422-1436): logits [b, V] (fp32 or bf16,
+    rows may be strided) and E [V, H] bf16 -> [b, H] bf16, the softmax-weighted
+    sum of the top_k rows of E under each row of logits."""
+    lib = N.load()
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    if logits.dtype not in (torch.float32, torch.bfloat16):
+        logits = logits.to(torch.float32)
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    b, V = logits.shape
+    E = E.to(torch.bfloat16).contiguous()
+    if E.shape[0] != V:
+        raise ValueError(f"E has {E.shape[0]} rows, logits {V} columns")
+    H = E.shape[1]
+    out = torch.empty((b, H), dtype=torch.bfloat16, device=logits.device)
+    need = lib.dflash_soft_anchor_workspace_size(b)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty((need,), dtype=torch.uint8, device=logits.device)
+    N.check(lib.dflash_soft_anchor(N.ptr(logits), int(logits.dtype == torch.bfloat16), b, V,
+                                   logits.stride(0), int(top_k), N.ptr(E), H, N.ptr(out),
+                                   N.ptr(workspace), workspace.numel(), _st(logits.device)),
+            "dflash_soft_anchor")
+    return out

@@ -297,6 +297,25 @@ def accept(draft_tokens, target_tokens):
     return acc, int(target_tokens[acc])
 
 
+def soft_anchor(logits: np.ndarray, E: np.ndarray, k: int = 8):
+    """Soft anchor (generate.py:1422-1436): for one row of logits [V] and the
+    embedding table E [V, H] (fp32 holding bf16 values), the k largest logits
+    (a stable argsort of -logits: lower index first on ties), their fp32
+    softmax, and the fp32 weighted sum of their embedding rows, summed in
+    order q = 0..k-1.  Returns (ids [k], weights [k], anchor [H] fp32); the
+    reference casts the anchor to the noise dtype (bf16) afterwards."""
+    x = np.asarray(logits, dtype=np.float32)
+    ids = np.argsort(-x, kind="stable")[:k]
+    top = x[ids].astype(np.float32)
+    e = np.exp(top - top.max())
+    w = (e / e.sum()).astype(np.float32)
+    rows = np.asarray(E, dtype=np.float32)[ids]
+    anchor = np.zeros(rows.shape[1], dtype=np.float32)
+    for q in range(k):
+        anchor = anchor + w[q] * rows[q]
+    return ids, w, anchor
+
+
 # --------------------------------------------------------------------------
 # seeded synthetic weights / inputs (the configs' N(0, 0.02) recipe)
 # --------------------------------------------------------------------------

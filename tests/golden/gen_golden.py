@@ -18,12 +18,17 @@ writes:
 * ``quantizer_q8.npz``: the int8 / fp16 bytes that
   ``ANEDraftModel._quantize_weight_q8`` (ane_model.py:265-279) returns for a
   matrix with a zero row, exact half-way ties and random rows;
-* ``layer_ids.json``: ``build_target_layer_ids`` (dflash.py:108-119) values.
+* ``layer_ids.json``: ``build_target_layer_ids`` (dflash.py:108-119) values;
+* ``soft_anchor.npz``: the block embedding that ``_make_soft_anchor``
+  (scripts/bench_ane_pipeline.py:76-84, the restatement of
+  generate.py:1422-1436 the reference benchmarks) returns for seeded logits
+  and a bf16-valued embedding table, fp32 and bf16-valued logits, k = 8, 1, 16.
 
 The shim only restates MLX primitive semantics; the fixtures pin the
 reference's composition of them, and the quantiser bit-exactly.
 """
 import importlib
+import importlib.util
 import json
 import os
 import sys
@@ -172,8 +177,44 @@ def main(ref_root):
            for nt, nd in [(36, 5), (64, 5), (40, 5), (28, 3), (36, 1), (48, 4)]}
     with open(os.path.join(HERE, "layer_ids.json"), "w") as f:
         json.dump(ids, f, indent=1, sort_keys=True)
+    soft_anchor_fixture(ref_root)
     print("wrote fixtures to", HERE)
 
 
+def soft_anchor_fixture(ref_root):
+    """``soft_anchor.npz`` from the reference's ``_make_soft_anchor``.  The
+    embedding table holds bf16 values (stored as bit patterns, used as fp32,
+    which is what MLX promotes bf16 * fp32 to); the noise rows are fp32, so
+    the returned row 0 is the fp32 sum before the cast to the noise dtype."""
+    sys.path.insert(0, os.path.join(HERE, "mlx_shim"))
+    spec = importlib.util.spec_from_file_location(
+        "bench_ane_pipeline", os.path.join(ref_root, "scripts", "bench_ane_pipeline.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    rng = np.random.default_rng(4242)
+    out = {}
+    cases = {"a": (256, 256, 4, 8, False, 3.0), "b": (1000, 64, 3, 8, True, 2.0),
+             "c": (777, 128, 2, 1, False, 1.0), "d": (777, 128, 2, 16, False, 0.5)}
+    for name, (V, H, rows, k, bf16_logits, scale) in cases.items():
+        eb = bf16_bits(rng.standard_normal((V, H)) * 0.05)
+        E = bf16_value(eb).astype(np.float32)
+        logits = (rng.standard_normal((rows, V)) * scale).astype(np.float32)
+        if bf16_logits:
+            logits = bf16_value(bf16_bits(logits)).astype(np.float32)
+        noise = np.zeros((1, 4, H), dtype=np.float32)
+        anchors = []
+        for r in range(rows):
+            blk = bench._make_soft_anchor(noise, logits[r], lambda ids: E[ids], top_k=k)
+            anchors.append(np.asarray(blk)[0, 0])
+        out.update({f"{name}.E": eb, f"{name}.logits": logits, f"{name}.k": np.int64(k),
+                    f"{name}.bf16_logits": np.int64(bf16_logits),
+                    f"{name}.anchor": np.stack(anchors).astype(np.float32)})
+    np.savez_compressed(os.path.join(HERE, "soft_anchor.npz"), **out)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = next((a for a in sys.argv[1:] if not a.startswith("--")), "/root/reference")
+    if "--only-soft-anchor" in sys.argv:
+        soft_anchor_fixture(ref)
+    else:
+        main(ref)

@@ -28,6 +28,22 @@ def argmax(x, axis=-1):
     return np.argmax(x, axis=axis)
 
 
+def argsort(x, axis=-1):
+    # ascending; equal keys keep their index order
+    return np.argsort(x, axis=axis, kind="stable")
+
+
+def softmax(x, axis=None):
+    x = np.asarray(x)
+    m = np.max(x, axis=axis, keepdims=True)
+    e = np.exp(x - m)
+    return e / np.sum(e, axis=axis, keepdims=True)
+
+
+def sum(x, axis=None, keepdims=False):  # noqa: A001 - mlx.core.sum
+    return np.sum(x, axis=axis, keepdims=keepdims)
+
+
 def eval(*args):
     return None
 

@@ -14,16 +14,18 @@ from toy_target import ToyTarget
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("sink,window", [(64, 1024), (4, 16)])
-def test_spec_generate_equals_greedy(pkg, sink, window):
+@pytest.mark.parametrize("sink,window,soft,layered", [(64, 1024, False, False), (4, 16, False, False),
+                                                      (64, 1024, True, False), (64, 1024, True, True)])
+def test_spec_generate_equals_greedy(pkg, sink, window, soft, layered):
     G = importlib.import_module("mirror-sd_b200.generate")
     ocfg = tiny_cfg(mask_token_id=999)   # the mask id is a token of the target's vocabulary
-    target = ToyTarget(ocfg.vocab_size, ocfg.hidden_size, seed=11)
+    target = ToyTarget(ocfg.vocab_size, ocfg.hidden_size, seed=11, layered=layered)
     q8, _ = O.synth_weights(ocfg, seed=12)
     q8["lm_head"] = target.E.float().cpu()           # the draft's lm_head is the target's embedding
     model = gpu_model(pkg, ocfg, q8, max_batch=1, max_ctx=32)
     prompt = torch.randint(0, ocfg.vocab_size, (20,), generator=torch.Generator().manual_seed(13)).tolist()
-    out, stats = G.spec_generate(target, model, prompt, 40, sink_size=sink, window_size=window)
+    out, stats = G.spec_generate(target, model, prompt, 40, sink_size=sink, window_size=window,
+                                 soft_anchor=soft)
     want = target.greedy(prompt, 40)
     assert out == want
     assert stats.total_tokens == 40

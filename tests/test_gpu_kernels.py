@@ -162,3 +162,61 @@ def test_lm_head_accept_fused(K):
     want = [O.accept(d.tolist(), t.tolist()) for d, t in zip(toks, target)]
     assert acc.cpu().tolist() == [w[0] for w in want] == [B - 1, 3, 0]
     assert cor.cpu().tolist() == [w[1] for w in want]
+
+
+def _bf16_ulps(got_bf16, want_f32):
+    """max |got - bf16(want)| in units of the bf16 spacing at bf16(want)."""
+    w = torch.as_tensor(want_f32, dtype=torch.float32)
+    wb = w.to(torch.bfloat16).float()
+    g = got_bf16.float().cpu()
+    _, e = torch.frexp(torch.where(wb == 0, torch.full_like(wb, 2.0 ** -126), wb))
+    spacing = torch.ldexp(torch.ones_like(wb), (e - 8).to(torch.int32))
+    return (torch.abs(g - wb) / spacing).max().item()
+
+
+def test_soft_anchor_vs_reference_fixture(K, golden_dir):
+    """The device soft anchor against the reference's ``_make_soft_anchor``:
+    within one bf16 rounding step of the reference's fp32 sum (the device
+    sums in the same order; expf may differ from numpy's exp by an ulp)."""
+    z = np.load(os.path.join(golden_dir, "soft_anchor.npz"))
+    for c in "abcd":
+        E = torch.from_numpy(z[f"{c}.E"].astype(np.int16)).view(torch.bfloat16)
+        logits = torch.from_numpy(z[f"{c}.logits"])
+        if int(z[f"{c}.bf16_logits"]):
+            logits = logits.to(torch.bfloat16)          # exact: the values are bf16
+        out = K.soft_anchor(logits.cuda(), E.cuda(), int(z[f"{c}.k"]))
+        assert _bf16_ulps(out, z[f"{c}.anchor"]) <= 1.0, c
+
+
+@pytest.mark.parametrize("rows,V,H,k,bf16", [(1, 151936, 5120, 8, False), (4, 151936, 4096, 8, True),
+                                             (3, 32000, 256, 16, False), (2, 5, 64, 1, False),
+                                             (32, 151936, 1024, 8, False)])
+def test_soft_anchor_vs_oracle(K, rows, V, H, k, bf16):
+    g = torch.Generator().manual_seed(V + rows)
+    E = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16)
+    logits = torch.randn(rows, V, generator=g) * 4.0
+    if bf16:
+        logits = logits.to(torch.bfloat16)
+    # a duplicated top value: the lower index must come first
+    logits[0, 17] = logits[0, 9] = logits[0].max() + 1
+    out = K.soft_anchor(logits.cuda(), E.cuda(), k).cpu()
+    Ef = E.float().numpy()
+    for r in range(rows):
+        ids, w, anchor = O.soft_anchor(logits[r].float().numpy(), Ef, k)
+        if r == 0:
+            assert list(ids[:2]) == [9, 17]
+        assert _bf16_ulps(out[r], anchor) <= 1.0, r
+
+
+def test_soft_anchor_strided_rows(K):
+    """Rows of a [b, B, V] verify output at the correction position, passed
+    as a strided view (ld = B * V)."""
+    g = torch.Generator().manual_seed(5)
+    V, H, B = 3000, 128, 4
+    E = (torch.randn(V, H, generator=g) * 0.05).to(torch.bfloat16)
+    full = torch.randn(2, B, V, generator=g)
+    view = full.cuda()[:, 2, :]
+    out = K.soft_anchor(view, E.cuda(), 8).cpu()
+    for r in range(2):
+        _, _, anchor = O.soft_anchor(full[r, 2].numpy(), E.float().numpy(), 8)
+        assert _bf16_ulps(out[r], anchor) <= 1.0

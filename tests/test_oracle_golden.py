@@ -86,3 +86,17 @@ def test_accept_prefix():
 def test_greedy_first_index_on_ties():
     logits = torch.tensor([[0.0, 3.0, 3.0, 1.0], [2.0, 2.0, 2.0, 2.0]])
     assert O.greedy(logits).tolist() == [1, 0]
+
+
+def test_soft_anchor_matches_reference(golden_dir):
+    """The oracle's soft anchor equals the reference's ``_make_soft_anchor``
+    (scripts/bench_ane_pipeline.py:76-84) bit for bit, ties included (case b
+    has a tie at the k-th place, broken by the lower index)."""
+    z = np.load(os.path.join(golden_dir, "soft_anchor.npz"))
+    for c in "abcd":
+        E = bf16_value(z[f"{c}.E"]).astype(np.float32)
+        logits, k = z[f"{c}.logits"], int(z[f"{c}.k"])
+        for r in range(logits.shape[0]):
+            ids, w, anchor = O.soft_anchor(logits[r], E, k)
+            assert len(ids) == k and abs(float(w.sum()) - 1.0) < 1e-6
+            assert np.array_equal(anchor, z[f"{c}.anchor"][r])

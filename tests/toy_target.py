@@ -17,7 +17,11 @@ class ToyCache:
 
 
 class ToyTarget:
-    def __init__(self, vocab: int, hidden: int, n_feat: int = 5, seed: int = 0, device="cuda"):
+    def __init__(self, vocab: int, hidden: int, n_feat: int = 5, seed: int = 0, device="cuda",
+                 layered: bool = False):
+        """``layered``: forward returns the features as a list of n_feat
+        [1, n, hidden] layers instead of one [1, n, n_feat * hidden] concat."""
+        self.layered = layered
         g = torch.Generator().manual_seed(seed)
         self.dev = torch.device(device)
         self.E = (torch.randn(vocab, hidden, generator=g) * 0.02).to(torch.bfloat16).to(self.dev)
@@ -46,7 +50,10 @@ class ToyTarget:
             h = torch.tanh(self.W1 @ e + self.W2 @ m)
             logits.append(self.E64 @ h)
             feats.append(torch.cat([torch.tanh(a @ h) for a in self.A]))
-        return torch.stack(logits)[None], torch.stack(feats)[None].to(torch.bfloat16)
+        cat = torch.stack(feats)[None].to(torch.bfloat16)
+        if self.layered:
+            return torch.stack(logits)[None], list(cat.chunk(len(self.A), dim=-1))
+        return torch.stack(logits)[None], cat
 
     def greedy(self, prompt, n_new):
         cache = self.make_cache()
