@@ -218,6 +218,136 @@ def workload_config(args, cfgd):
             "parallelism": f"batch-sharded x{args.gpus}, no collectives"}
 
 
+def run_serving(args, pkg, rank, world, dev):
+    """--config c5: batched serving on the 8B-class draft.  256 requests with
+    contexts uniform in [512, 8192] and block 16 are sharded over the ranks
+    (longest first, no collective); each rank prefills its requests into one
+    sink 64 / window 1024 draft cache in 16K-row chunks, then times decode
+    steps of all its requests together.  A synthetic verifier accepts a
+    geometric number of drafts per request (P(accept >= k) = 0.85^k); the
+    next step brings accept + 1 context rows per request.  One step = the
+    draft forward of every request (dense tcgen05 projections and lm_head at
+    these row counts), the verifier emulation (two small torch ops), device
+    acceptance, the accepted lengths read back, and the block-row trim."""
+    import torch
+    shard = importlib.import_module("mirror-sd_b200.shard")
+    serving = importlib.import_module("mirror-sd_b200.serving")
+    cfgd = dict(CFG_8B)
+    B, H, V = cfgd["block_size"], cfgd["hidden_size"], cfgd["vocab_size"]
+    g = torch.Generator().manual_seed(5)
+    ctx_all = torch.randint(512, 8193, (args.seqs,), generator=g).tolist()
+    mine = shard.shard_requests(ctx_all, world, rank, B)
+    n = len(mine)
+    ctx = [ctx_all[i] for i in mine]
+    chunk_rows = 16384
+    cfg = pkg.DFlashConfig(**cfgd)
+    cfg.target_layer_ids = list(range(F))
+    w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+    model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=n, max_ctx=8192, max_block=B, device=dev,
+                                 max_ctx_rows=chunk_rows)
+    server = serving.DraftServer(model, n, sink_size=64, window_size=1024)
+    gd = torch.Generator(device=dev).manual_seed(17 + rank)
+    pool = torch.randn(chunk_rows, F * H, generator=gd, device=dev).to(torch.bfloat16)
+    noise = (torch.randn(n, B, H, generator=gd, device=dev) * 0.02).to(torch.bfloat16)
+    # prefill (timed separately): chunks of whole requests within the row budget
+    torch.cuda.synchronize(dev)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    i = 0
+    while i < n:
+        j, rows = i, 0
+        while j < n and rows + ctx[j] <= chunk_rows:
+            rows += ctx[j]
+            j += 1
+        server.prefill(list(range(i, j)), noise[i:j], pool[:rows], ctx[i:j])
+        i = j
+    p1.record()
+    torch.cuda.synchronize(dev)
+    prefill_ms = p0.elapsed_time(p1)
+    steps = args.warmup + args.steps
+    plan = torch.tensor(serving.geometric_accepts(n, steps + 1, 0.85, B - 1, seed=100 + rank),
+                        dtype=torch.int32, device=dev)
+    seqs = list(range(n))
+    out_t = torch.empty((n, B - 1), dtype=torch.int32, device=dev)
+    lens = [int(a) + 1 for a in plan[0].tolist()]      # the prefill step's verify outcome
+
+    def dstep(t, lens):
+        server.step(seqs, noise, pool[:sum(lens)], lens, out_tokens=out_t)
+        tgt = serving.targets_for(out_t, plan[t + 1], V)
+        a, _ = pkg.accept(out_t, tgt)
+        return [int(x) + 1 for x in a.cpu().tolist()]
+
+    for t in range(args.warmup):
+        lens = dstep(t, lens)
+    launches = model._lib.dflash_last_launch_count(model._handle)
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local_gpu_id(dev)) if rank == 0 else None
+    time.sleep(0.6 if sampler else 0)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    s.record()
+    accepted, ctx_rows = 0, 0
+    for t in range(args.warmup, steps):
+        ctx_rows += sum(lens)
+        lens = dstep(t, lens)
+        accepted += sum(x - 1 for x in lens)
+    e.record()
+    torch.cuda.synchronize(dev)
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    ms = s.elapsed_time(e) / args.steps
+    ms_max = shard.max_over_ranks(ms)
+    per_rank = shard.gather_to_rank0({"n": n, "accepted": accepted, "ctx_rows": ctx_rows,
+                                      "prefill_ms": prefill_ms, "prefill_rows": sum(ctx)})
+    if sampler:
+        sampler.stop()
+    if rank == 0:
+        hbm, tf_burst, tf_sust, src = peaks()
+        n_all = sum(r["n"] for r in per_rank)
+        acc_all = sum(r["accepted"] for r in per_rank)
+        M = n * B
+        L, NQ, NKV, I = cfgd["num_hidden_layers"], cfgd["num_attention_heads"], cfgd["num_key_value_heads"], \
+            cfgd["intermediate_size"]
+        params = (NQ + 2 * NKV) * 128 * H + H * NQ * 128 + 3 * I * H
+        cr = ctx_rows / args.steps
+        flops = 2.0 * M * (L * params + V * H) + 2.0 * cr * (F * H * H + H * L * 2 * NKV * 128)
+        line = {
+            "metric": "batched serving draft tok/s (8B-class, 256 requests, ctx U[512, 8192], block 16)",
+            "value": shard.job_throughput([r["n"] * (B - 1) for r in per_rank], ms_max),
+            "unit": "draft tok/s", "accepted_tok_s": acc_all / args.steps / (ms_max / 1e3),
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "w8a16: int8 weights (exact f16 copies on the dense path), bf16/f16 activations, "
+                     "fp32 accumulate", "data": "synthetic",
+            "config": {"workload": "c5 batched serving", "requests": args.seqs, "requests_this_rank0": n,
+                       "block": B, "ctx": "U[512, 8192] prefilled", "cache": "sink 64 / window 1024",
+                       "accept": "geometric p=0.85", "parallelism": f"requests sharded over {world} GPU(s)"},
+            "tensor_roofline": {"flops_per_step_rank0": flops, "achieved_tflops": flops / (ms / 1e3) / 1e12,
+                                "peak": tf_sust, "frac": flops / (ms / 1e3) / 1e12 / tf_sust,
+                                "peak_source": f"{src} bf16_tflops_sustained"},
+            "prefill": {"rows": sum(r["prefill_rows"] for r in per_rank),
+                        "ms_max": max(r["prefill_ms"] for r in per_rank)},
+            "mean_accept": acc_all / (args.steps * n_all),
+            "gpu_launches_per_step": launches + 2,
+            "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
+        }
+        print(json.dumps(line), flush=True)
+    server.close()
+    model.close()
+
+
+def local_gpu_id(dev):
+    import torch
+    props = torch.cuda.get_device_properties(dev)
+    uid = getattr(props, "uuid", None)
+    return f"GPU-{uid}" if uid is not None else dev.index
+
+
 def _pkg():
     import importlib
     pkg = importlib.import_module("mirror-sd_b200")
@@ -231,7 +361,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c3", "c2"], default="c3")
+    ap.add_argument("--config", choices=["c3", "c2", "c5"], default="c3")
+    ap.add_argument("--seqs", type=int, default=256, help="c5: requests over all GPUs")
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -263,6 +394,13 @@ def main():
     shard = importlib.import_module("mirror-sd_b200.shard")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.config == "c5":
+        if args.steps == 200:
+            args.steps = 20
+        run_serving(args, pkg, rank, world, dev)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     cfg, w, lm, model = build_model(pkg, cfgd, args.ctx, args.batch, dev, seed=0)
     B = cfgd["block_size"]
     # world * batch independent requests; this rank drafts its share (no collective on the data path)

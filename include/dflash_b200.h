@@ -66,7 +66,11 @@ typedef struct DFlashDims {
   float rope_theta;
   int32_t max_batch;
   int32_t max_block;
-  int32_t max_ctx;
+  int32_t max_ctx;      /* context rows of one sequence in one step */
+  int32_t max_ctx_rows; /* context rows of one step, all sequences together
+                           (0: max_batch * max_ctx).  A stateless step of b
+                           sequences also needs b * (max C_s + block) <=
+                           max_ctx_rows + max_batch * max_block. */
 } DFlashDims;
 
 /* One decoder layer in the reference's W8A16 format: row-major int8
@@ -149,6 +153,11 @@ typedef struct DFlashForwardArgs {
    * base and row pitch). */
   const uint16_t* const* target_layers;
   int64_t target_layers_ld;
+  /* With a cache: HOST array [batch] of distinct cache sequence indices
+   * (< the cache's max_batch): sequence s of this step is cache sequence
+   * cache_seqs[s], so one cache serves any subset of its sequences per step
+   * (prefill a few, decode all).  NULL: sequences 0..batch-1. */
+  const int32_t* cache_seqs;
 } DFlashForwardArgs;
 
 #define DFLASH_PHASES 8
@@ -184,8 +193,14 @@ int dflash_cache_create(void* handle, int num_layers, int max_batch, int sink_si
  * when layer < 0, for every sequence: length -> max(length - n, 0),
  * offset -> offset - n.  n <= 0 does nothing. */
 int dflash_cache_trim(void* cache, int layer, int n);
+/* trim(counts[i]) of cache sequence seqs[i] only, i < count (HOST arrays;
+ * layer -1 = every layer): per-sequence rollback in a batched decode. */
+int dflash_cache_trim_seqs(void* cache, int layer, const int32_t* seqs, const int32_t* counts, int count);
 /* Empty every sequence (offset 0).  Device contents are not touched. */
 int dflash_cache_reset(void* cache);
+/* Empty cache sequences seqs[0..count) (offset 0, no rows), e.g. to give a
+ * slot to a new request; the other sequences keep their rows. */
+int dflash_cache_reset_seqs(void* cache, const int32_t* seqs, int count);
 /* DFlashKVCache.offset and keys.shape[2] of one layer and sequence. */
 int dflash_cache_state(void* cache, int layer, int seq, int32_t* offset, int32_t* length);
 /* DFlashKVCache.keys / .values of one layer and sequence, in logical order, as

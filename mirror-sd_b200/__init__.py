@@ -10,8 +10,9 @@ from .dflash import (DFlashCache, DFlashConfig, DFlashDraftModel, DFlashKVCache,
 from .weights import synth_weights_q8, weights_from_q8_numpy
 from .generate import SpecDecodeStats, spec_generate
 from .loader import load_dflash_model, load_dflash_weights, save_q8_checkpoint
+from .serving import DraftServer
 
 __all__ = ["DFlashCache", "DFlashConfig", "DFlashDraftModel", "DFlashKVCache", "DFlashWeightsQ8", "Q8Layer",
            "accept", "build_target_layer_ids", "context_layers", "extract_context_feature", "quantize_q8", "sample",
            "synth_weights_q8", "weights_from_q8_numpy", "SpecDecodeStats", "spec_generate",
-           "load_dflash_model", "load_dflash_weights", "save_q8_checkpoint"]
+           "load_dflash_model", "load_dflash_weights", "save_q8_checkpoint", "DraftServer"]

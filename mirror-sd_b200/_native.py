@@ -29,7 +29,8 @@ class DFlashDims(ctypes.Structure):
                 ("num_key_value_heads", c_int32), ("head_dim", c_int32),
                 ("vocab_size", c_int32), ("num_target_features", c_int32),
                 ("rms_norm_eps", c_float), ("rope_theta", c_float),
-                ("max_batch", c_int32), ("max_block", c_int32), ("max_ctx", c_int32)]
+                ("max_batch", c_int32), ("max_block", c_int32), ("max_ctx", c_int32),
+                ("max_ctx_rows", c_int32)]
 
 
 class DFlashLayerWeights(ctypes.Structure):
@@ -54,7 +55,8 @@ class DFlashForwardArgs(ctypes.Structure):
                 ("cache", c_void_p),
                 ("anchor_logits", c_void_p), ("anchor_logits_ld", ctypes.c_int64),
                 ("anchor_logits_bf16", c_int32), ("anchor_top_k", c_int32),
-                ("target_layers", ctypes.POINTER(c_void_p)), ("target_layers_ld", ctypes.c_int64)]
+                ("target_layers", ctypes.POINTER(c_void_p)), ("target_layers_ld", ctypes.c_int64),
+                ("cache_seqs", ctypes.POINTER(c_int32))]
 
 
 DFLASH_PHASES = 8
@@ -75,6 +77,9 @@ EXPORTS = {
                                       ctypes.c_int, ctypes.c_int, ctypes.POINTER(c_void_p)]),
     "dflash_cache_trim": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int]),
     "dflash_cache_reset": (c_int32, [c_void_p]),
+    "dflash_cache_trim_seqs": (c_int32, [c_void_p, ctypes.c_int, ctypes.POINTER(c_int32),
+                                         ctypes.POINTER(c_int32), ctypes.c_int]),
+    "dflash_cache_reset_seqs": (c_int32, [c_void_p, ctypes.POINTER(c_int32), ctypes.c_int]),
     "dflash_cache_state": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(c_int32),
                                      ctypes.POINTER(c_int32)]),
     "dflash_cache_read": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, c_void_p, c_void_p,

@@ -68,15 +68,16 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
 
   // logical kv rows of this sequence; with a KvMap they sit at ring slots
   const bool mapped = p.kv.nseq > 0;
-  const int kv_len = mapped ? p.kv.n_att[bi] : p.kv_len;
-  const int rs = mapped ? p.kv.rs_post[bi] : 0;
+  const int kv_len = mapped ? p.kv.seq[bi].n_att : p.kv_len;
+  const int rs = mapped ? p.kv.seq[bi].rs_post : 0;
   const int kv0 = split * p.chunk;
   const int kv1 = min(kv_len, kv0 + p.chunk);
   const int ntiles = kv1 > kv0 ? (kv1 - kv0 + AT_TK - 1) / AT_TK : 0;
 
   const __half* qg = p.q + ((size_t)bi * p.nq + (size_t)kvh * G) * p.block * 128;
-  const __half* kg = p.k + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
-  const __half* vg = p.v + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+  const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
+  const __half* kg = p.k + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+  const __half* vg = p.v + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
 
   // Q tile (rows >= R zero)
   for (int idx = threadIdx.x; idx < RP * 16; idx += blockDim.x) {

@@ -156,8 +156,8 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1)
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
   const bool mapped = p.kv.nseq > 0;
-  const int kv_len = mapped ? p.kv.n_att[bi] : p.kv_len;
-  const int rs = mapped ? p.kv.rs_post[bi] : 0;
+  const int kv_len = mapped ? p.kv.seq[bi].n_att : p.kv_len;
+  const int rs = mapped ? p.kv.seq[bi].rs_post : 0;
   const int kv0 = split * p.chunk;
   const int kv1 = min(kv_len, kv0 + p.chunk);
   const int ntiles = kv1 > kv0 ? (kv1 - kv0 + TA_TK - 1) / TA_TK : 0;
@@ -207,9 +207,10 @@ __global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1)
     cp_async_wait<0>();
     fence_proxy_async_smem();
     mbar_arrive(q_ready);
-    const __half* kg = p.k + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
-    const __half* vg = p.v + ((size_t)bi * p.nkv + kvh) * (size_t)p.kv_cap * 128;
-    const int plane = bi * p.nkv + kvh;
+    const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
+    const __half* kg = p.k + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+    const __half* vg = p.v + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
+    const int plane = kseq * p.nkv + kvh;
     // Producer thread 0 alone waits for free stages and issues the TMA tiles;
     // the other producer threads sleep on a named barrier and join only for the
     // tiles copied row by row.  Nobody leaves the loop early: every producer
@@ -458,7 +459,8 @@ static cudaError_t attn_tc_launch_t(const AttnParams& p, int batch, cudaStream_t
   using C = TaCfg<NG>;
   auto kern = attn_tc_kernel<NG>;
   CUtensorMap mk, mv;
-  if (!map_kv(&mk, p.k, p.kv_cap, (uint64_t)batch * p.nkv) || !map_kv(&mv, p.v, p.kv_cap, (uint64_t)batch * p.nkv))
+  const uint64_t planes = (uint64_t)(p.kv.nseq > 0 ? p.kv_seqs : batch) * p.nkv;
+  if (planes < (uint64_t)batch * p.nkv || !map_kv(&mk, p.k, p.kv_cap, planes) || !map_kv(&mv, p.v, p.kv_cap, planes))
     return cudaErrorInvalidValue;
   DFL_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM));
   DFL_TRY(max_smem_carveout(kern));

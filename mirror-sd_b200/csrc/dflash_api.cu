@@ -64,6 +64,11 @@ struct Layer {
   int8_t* w_gu; float* s_gu;     // per 128-row tile: 64 gate rows then the matching 64 up rows
   int8_t* w_d; float* s_d;
   float *in_norm, *post_norm, *q_norm;
+  // dense block path (handles whose max_batch * max_block exceeds kW8Rows):
+  // exact f16 copies of the int8 weights, row-major [N, K]; gate|up
+  // interleaved per 256 rows (128 gate rows, then the 128 matching up rows)
+  __half *dw_qkv = nullptr, *dw_o = nullptr, *dw_gu = nullptr, *dw_d = nullptr;
+  float* ds_gu = nullptr;
 };
 
 struct Handle {
@@ -105,6 +110,10 @@ struct Handle {
   float* sa_cand_v = nullptr;        // [max_batch, kSaMaxCtas, kSaMaxK] soft anchor candidates
   int* sa_cand_i = nullptr;
   int* sa_cnt = nullptr;             // [max_batch] arrival counters (zero between launches)
+  KvSeq* kv_seq = nullptr;           // [max_batch + 1] per-sequence records of the current forward
+  bool dense = false;                // the dense block path is available (max rows > kW8Rows)
+  size_t stateless_rows = 0;         // K/V rows per layer and kv head of the stateless store
+  __half* xa = nullptr;              // dense path: normalised projection input [Mx, H] f16
   int last_launches = 0;
 };
 
@@ -135,6 +144,29 @@ struct Cache {
   SeqState& at(int l, int s) { return st[(size_t)l * max_batch + s]; }
 };
 
+// block rows one forward may carry; above kW8Rows the projections and the
+// lm_head run as dense tcgen05 GEMMs over exact f16 copies of the weights
+constexpr int kW8Rows = 64;
+constexpr int kMaxBlockRows = 16384;
+
+// DFlashKVCache.trim (dflash.py:200-208) on one sequence's state
+void trim_state(SeqState& q, int n) {
+  if (n <= 0) return;
+  const int len = std::max(q.hl + q.rl - n, 0);  // dflash.py:204
+  if (len >= q.hl) {
+    q.rl = len - q.hl;
+  } else {
+    q.rl = 0;
+    q.hl = len;
+  }
+  q.offset -= n;                                 // dflash.py:207
+}
+
+// context rows one forward may carry (all sequences)
+int ctx_rows_capacity(const DFlashDims& d) {
+  return d.max_ctx_rows > 0 ? d.max_ctx_rows : d.max_batch * d.max_ctx;
+}
+
 int check_dims(const DFlashDims* d) {
   if (!d) return fail(DFLASH_ERR_INVALID, "dims is NULL");
   if (d->head_dim != 128) return fail(DFLASH_ERR_INVALID, "head_dim must be 128 (got %d)", d->head_dim);
@@ -150,8 +182,13 @@ int check_dims(const DFlashDims* d) {
   if (d->num_hidden_layers < 1 || d->vocab_size < 1 || d->num_target_features < 1)
     return fail(DFLASH_ERR_INVALID, "layers, vocab and target features must be positive");
   if (d->max_batch < 1 || d->max_block < 2 || d->max_block > 1024 || d->max_ctx < 0 ||
-      d->max_batch * d->max_block > 64)
-    return fail(DFLASH_ERR_INVALID, "capacities: max_batch*max_block must be in [2, 64], max_ctx >= 0");
+      (long long)d->max_batch * d->max_block > kMaxBlockRows)
+    return fail(DFLASH_ERR_INVALID, "capacities: max_batch*max_block must be in [2, %d], max_ctx >= 0",
+                kMaxBlockRows);
+  if (d->max_ctx_rows < 0 || (d->max_ctx_rows == 0 && (long long)d->max_batch * d->max_ctx > (1LL << 30)) ||
+      (d->max_ctx_rows > 0 && d->max_ctx_rows < d->max_ctx))
+    return fail(DFLASH_ERR_INVALID, "max_ctx_rows %d: must be 0 (max_batch * max_ctx <= 2^30) or >= max_ctx",
+                d->max_ctx_rows);
   const int G = d->num_attention_heads / d->num_key_value_heads;
   if (G * d->max_block > 192)
     return fail(DFLASH_ERR_INVALID, "query rows per kv head (heads/kv_heads * block) must be <= 192");
@@ -281,13 +318,29 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
     CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 128, st));
+    if ((long long)d.max_batch * d.max_block > kW8Rows) {
+      CKC(A.alloc(&ly.dw_qkv, (size_t)nqkv * H));
+      CKC(i8_to_f16_launch(lw.wq, (size_t)NQ * 128 * H, ly.dw_qkv, st));
+      CKC(i8_to_f16_launch(lw.wk, (size_t)NKV * 128 * H, ly.dw_qkv + (size_t)NQ * 128 * H, st));
+      CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, ly.dw_qkv + (size_t)(NQ + NKV) * 128 * H, st));
+      CKC(A.alloc(&ly.dw_o, (size_t)H * NQ * 128));
+      CKC(i8_to_f16_launch(lw.wo, (size_t)H * NQ * 128, ly.dw_o, st));
+      CKC(A.alloc(&ly.dw_gu, (size_t)2 * I * H));
+      CKC(i8_to_f16_rows_launch(lw.wg, I, H, ly.dw_gu, 128, 256, 0, st));
+      CKC(i8_to_f16_rows_launch(lw.wu, I, H, ly.dw_gu, 128, 256, 128, st));
+      CKC(A.alloc(&ly.ds_gu, 2 * I));
+      CKC(w8_scale_launch((const __half*)lw.sg, I, ly.ds_gu, 128, 256, 0, st));
+      CKC(w8_scale_launch((const __half*)lw.su, I, ly.ds_gu, 128, 256, 128, st));
+      CKC(A.alloc(&ly.dw_d, (size_t)H * I));
+      CKC(i8_to_f16_launch(lw.wd, (size_t)H * I, ly.dw_d, st));
+    }
     hd->layers.push_back(ly);
   }
   // ---- workspace
   const int Mx = d.max_batch * d.max_block;
-  const int Cx = d.max_batch * d.max_ctx;
-  const int kvcap = d.max_ctx + d.max_block;
+  const int Cx = ctx_rows_capacity(d);
   const int G = NQ / NKV;
+  hd->stateless_rows = (size_t)Cx + Mx;
   CKC(A.alloc(&hd->rope, (size_t)(Cx + Mx) * 64));
   CKC(A.alloc(&hd->h, (size_t)Mx * H));
   CKC(A.alloc(&hd->hstat, (size_t)(H / 128) * Mx));
@@ -296,7 +349,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(A.alloc(&hd->ctx_part, (size_t)(H / 256) * Cx));
     CKC(A.alloc(&hd->ctx_n, (size_t)Cx * H));
   }
-  const size_t kv_elems = (size_t)L * d.max_batch * NKV * kvcap * 128;
+  const size_t kv_elems = (size_t)L * NKV * hd->stateless_rows * 128;
   CKC(A.alloc(&hd->K, kv_elems));
   CKC(A.alloc(&hd->V, kv_elems));
   CKC(A.alloc(&hd->Q, (size_t)Mx * NQ * 128));
@@ -313,13 +366,17 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->mpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->lpart, hd->attn_part_rows));
   CKC(A.alloc(&hd->hn, (size_t)Mx * H));
-  CKC(A.alloc(&hd->lm_val, (size_t)hd->num_sms * Mx));
-  CKC(A.alloc(&hd->lm_idx, (size_t)hd->num_sms * Mx));
+  hd->dense = Mx > kW8Rows;
+  // lm_head argmax partials: one per CTA (W8 path) or per 256-entry vocabulary block (dense path)
+  const size_t lm_parts = std::max<size_t>(hd->num_sms, hd->dense ? (d.vocab_size + 255) / 256 : 0);
+  CKC(A.alloc(&hd->lm_val, lm_parts * Mx));
+  CKC(A.alloc(&hd->lm_idx, lm_parts * Mx));
+  if (hd->dense) CKC(A.alloc(&hd->xa, (size_t)Mx * H));
   {
     const int shapes[4][2] = {{(NQ + 2 * NKV) * 128, H}, {H, NQ * 128}, {2 * I, H}, {H, I}};
     int max_tiles = 0;
     for (auto& sh : shapes) {
-      const size_t f = w8tc_part_floats(sh[0], sh[1], Mx, hd->num_sms);
+      const size_t f = w8tc_part_floats(sh[0], sh[1], std::min(Mx, kW8Rows), hd->num_sms);
       if (f > hd->w8_part_floats) hd->w8_part_floats = f;
       if (sh[0] / 128 > max_tiles) max_tiles = sh[0] / 128;
     }
@@ -335,6 +392,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(A.alloc(&hd->sa_cand_v, nc));
     CKC(A.alloc(&hd->sa_cand_i, nc));
     CKC(A.alloc(&hd->sa_cnt, (size_t)d.max_batch));
+    CKC(A.alloc(&hd->kv_seq, (size_t)d.max_batch + 1));
     CKC(cudaMemset(hd->sa_cnt, 0, (size_t)d.max_batch * sizeof(int)));
   }
   CKC(cudaDeviceSynchronize());
@@ -379,19 +437,22 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   if (B < 2 || B > d.max_block) return fail(DFLASH_ERR_INVALID, "block %d outside [2, %d]", B, d.max_block);
   if (nl < 1 || nl > d.num_hidden_layers)
     return fail(DFLASH_ERR_INVALID, "num_layers %d outside [1, %d]", nl, d.num_hidden_layers);
-  if (b > kKvMaxSeq) return fail(DFLASH_ERR_INVALID, "batch %d above %d", b, kKvMaxSeq);
   // per-sequence context rows, packed in sequence order
   KvMap m{};
   m.nseq = b;
+  m.seq = hd->kv_seq;
+  std::vector<KvSeq> sq(b + 1, KvSeq{});
   int cmax = 0;
   for (int s = 0; s < b; ++s) {
     const int c = a->ctx_lens ? a->ctx_lens[s] : a->ctx_len;
     if (c < 0 || c > d.max_ctx)
       return fail(DFLASH_ERR_INVALID, "ctx_len %d of sequence %d outside [0, %d]", c, s, d.max_ctx);
-    m.ctx_start[s + 1] = m.ctx_start[s] + c;
+    sq[s + 1].ctx_start = sq[s].ctx_start + c;
     cmax = std::max(cmax, c);
   }
-  const int Ctot = m.ctx_start[b];
+  const int Ctot = sq[b].ctx_start;
+  if (Ctot > ctx_rows_capacity(d))
+    return fail(DFLASH_ERR_INVALID, "%d context rows above the capacity %d", Ctot, ctx_rows_capacity(d));
   if (!a->noise || (Ctot > 0 && !a->target_hidden && !a->target_layers))
     return fail(DFLASH_ERR_INVALID, "noise / target_hidden must not be NULL");
   TcSources fc_src{};
@@ -429,6 +490,18 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     return fail(DFLASH_ERR_INVALID, "batch %d above the cache's %d sequences", b, cc->max_batch);
   if (cc && nl != cc->layers)
     return fail(DFLASH_ERR_INVALID, "num_layers %d differs from the cache's %d layers", nl, cc->layers);
+  if (a->cache_seqs && !cc) return fail(DFLASH_ERR_INVALID, "cache_seqs needs a cache");
+  std::vector<int> cseq(b);
+  for (int s = 0; s < b; ++s) cseq[s] = a->cache_seqs ? a->cache_seqs[s] : s;
+  if (a->cache_seqs) {
+    std::vector<char> seen(cc->max_batch, 0);
+    for (int s = 0; s < b; ++s) {
+      if (cseq[s] < 0 || cseq[s] >= cc->max_batch || seen[cseq[s]])
+        return fail(DFLASH_ERR_INVALID, "cache_seqs[%d] = %d: not a distinct sequence of [0, %d)", s, cseq[s],
+                    cc->max_batch);
+      seen[cseq[s]] = 1;
+    }
+  }
   std::lock_guard<std::mutex> lock(hd->mu);
   std::unique_lock<std::mutex> cache_lock;
   if (cc) cache_lock = std::unique_lock<std::mutex>(cc->mu);
@@ -443,12 +516,12 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     m.sink = cc->sink; m.ring = cc->ring; m.slots = cc->slots;
     next.resize(b);
     for (int s = 0; s < b; ++s) {
-      const SeqState s0 = cc->at(0, s);
+      const SeqState s0 = cc->at(0, cseq[s]);
       for (int l = 1; l < nl; ++l)
-        if (!(cc->at(l, s) == s0))
+        if (!(cc->at(l, cseq[s]) == s0))
           return fail(DFLASH_ERR_INVALID,
                       "cache layers hold different rows for sequence %d (trim every layer alike)", s);
-      const int app = m.ctx_start[s + 1] - m.ctx_start[s] + B;
+      const int app = sq[s + 1].ctx_start - sq[s].ctx_start + B;
       const int to_sink = s0.hl < cc->sink ? std::min(app, cc->sink - s0.hl) : 0;
       SeqState n1 = s0;
       n1.hl = s0.hl + to_sink;
@@ -461,11 +534,12 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
         n1.rl = cc->window_size;
       }
       n1.offset = s0.offset + app;
-      m.n0[s] = s0.hl + s0.rl;
-      m.rs_pre[s] = s0.rs;
-      m.rs_post[s] = n1.rs;
-      m.n_att[s] = n1.hl + n1.rl;
-      m.pos0[s] = s0.offset;
+      sq[s].n0 = s0.hl + s0.rl;
+      sq[s].rs_pre = s0.rs;
+      sq[s].rs_post = n1.rs;
+      sq[s].n_att = n1.hl + n1.rl;
+      sq[s].pos0 = s0.offset;
+      sq[s].cseq = cseq[s];
       next[s] = n1;
     }
     Kbase = cc->K; Vbase = cc->V;
@@ -476,20 +550,26 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     for (int s = 0; s < b; ++s) {
       const int off = a->rope_offsets ? a->rope_offsets[s] : a->rope_offset;
       if (off < 0) return fail(DFLASH_ERR_INVALID, "rope offsets must be >= 0");
-      m.n0[s] = 0; m.rs_pre[s] = 0; m.rs_post[s] = 0;
-      m.n_att[s] = m.ctx_start[s + 1] - m.ctx_start[s] + B;
-      m.pos0[s] = off;
+      sq[s].n0 = 0; sq[s].rs_pre = 0; sq[s].rs_post = 0;
+      sq[s].n_att = sq[s + 1].ctx_start - sq[s].ctx_start + B;
+      sq[s].pos0 = off;
+      sq[s].cseq = s;
     }
     Kbase = hd->K; Vbase = hd->V;
+    if ((size_t)b * m.slots > hd->stateless_rows)
+      return fail(DFLASH_ERR_INVALID, "stateless step needs %zu K/V rows (batch * (longest context + block)), "
+                  "capacity %zu", (size_t)b * m.slots, hd->stateless_rows);
     layer_stride = (size_t)b * NKV * m.slots * 128;
   }
   int kvmax = 0;
-  for (int s = 0; s < b; ++s) kvmax = std::max(kvmax, m.n_att[s]);
+  for (int s = 0; s < b; ++s) kvmax = std::max(kvmax, sq[s].n_att);
 
   CK(cudaSetDevice(hd->device));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int M = b * B;
   const int G = NQ / NKV;
+  const bool dense = M > kW8Rows;
+  if (dense && !hd->dense) return fail(DFLASH_ERR_INVALID, "%d block rows above %d", M, kW8Rows);
   const bool timing = a->phase_events && a->n_phase_events >= DFLASH_PHASES;
   auto mark = [&](int k) -> cudaError_t {
     return timing ? cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[k]), st) : cudaSuccess;
@@ -497,7 +577,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   int launches = 0;
 
   CK(mark(0));
-  CK(rope_table_map_launch(m, B, hd->inv_freq, hd->rope, st));
+  CK(rope_table_map_launch(m, sq.data(), B, hd->inv_freq, hd->rope, st));
+  if (b + 1 > kKvChunk) launches += (b + kKvChunk) / kKvChunk;   // kv_upload launches
   if (a->anchor_logits) {
     SaParams sp{};
     sp.logits = a->anchor_logits; sp.logits_bf16 = a->anchor_logits_bf16 != 0;
@@ -540,7 +621,43 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   if ((size_t)b * NKV * splits * G * B > hd->attn_part_rows)
     return fail(DFLASH_ERR_INVALID, "attention workspace too small");
   int hparts = 1;
-  for (int l = 0; l < nl; ++l) {
+  const float attn_scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+  // dense block path: every projection a persistent tcgen05 GEMM over the
+  // exact f16 weight copies, the RMSNorms as separate f16 row kernels
+  for (int l = 0; dense && l < nl; ++l) {
+    const Layer& ly = hd->layers[l];
+    __half* Kl = Kbase + l * layer_stride;
+    __half* Vl = Vbase + l * layer_stride;
+    CK(ctx_norm_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xa, st));
+    TcParams qp{};
+    qp.M = M; qp.N = (NQ + 2 * NKV) * 128; qp.K = H; qp.err = hd->dev_err;
+    qp.scale = ly.s_qkv; qp.q_norm = ly.q_norm; qp.k_norm = hd->k_norm_all + l * 128;
+    qp.rope = hd->rope; qp.rope_row0 = Ctot; qp.eps = d.rms_norm_eps;
+    qp.q_out = hd->Q; qp.k_out = Kl; qp.v_out = Vl;
+    qp.nkv = NKV; qp.n_q_heads = NQ; qp.block = B; qp.kv = m;
+    CK(tc_gemm_launch(hd->xa, ly.dw_qkv, false, kTcBlkQKV, qp, st));
+    AttnParams ap{};
+    ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kvmax;
+    ap.kv_cap = m.slots; ap.chunk = chunk; ap.splits = splits; ap.opart = hd->opart;
+    ap.mpart = hd->mpart; ap.lpart = hd->lpart; ap.scale_log2 = attn_scale_log2;
+    ap.kv = m; ap.kv_seqs = cc ? cc->max_batch : b; ap.err = hd->dev_err;
+    CK(attn_tc_launch(ap, b, hd->attn_out, st));
+    TcParams op{};
+    op.M = M; op.N = H; op.K = NQ * 128; op.err = hd->dev_err;
+    op.scale = ly.s_o; op.h = hd->h; op.sumsq_part = hd->hstat;
+    CK(tc_gemm_launch(hd->attn_out, ly.dw_o, false, kTcResid, op, st));
+    hparts = H / 256;
+    CK(ctx_norm_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xa, st));
+    TcParams gp{};
+    gp.M = M; gp.N = 2 * I; gp.K = H; gp.err = hd->dev_err; gp.scale = ly.ds_gu; gp.act = hd->act;
+    CK(tc_gemm_launch(hd->xa, ly.dw_gu, false, kTcSilu, gp, st));
+    TcParams dp{};
+    dp.M = M; dp.N = H; dp.K = I; dp.err = hd->dev_err;
+    dp.scale = ly.s_d; dp.h = hd->h; dp.sumsq_part = hd->hstat;
+    CK(tc_gemm_launch(hd->act, ly.dw_d, false, kTcResid, dp, st));
+    launches += 8;  // 2 norms, q|k|v, attention partial + combine, o, gate|up, down
+  }
+  for (int l = 0; !dense && l < nl; ++l) {
     const Layer& ly = hd->layers[l];
     __half* Kl = Kbase + l * layer_stride;
     __half* Vl = Vbase + l * layer_stride;
@@ -559,9 +676,9 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     ap.q = hd->Q; ap.k = Kl; ap.v = Vl; ap.nq = NQ; ap.nkv = NKV; ap.block = B; ap.kv_len = kvmax;
     ap.kv_cap = m.slots; ap.chunk = chunk; ap.splits = splits; ap.opart = hd->opart;
     ap.mpart = hd->mpart; ap.lpart = hd->lpart;
-    ap.scale_log2 = (float)(1.0 / std::sqrt(128.0) * 1.4426950408889634);
+    ap.scale_log2 = attn_scale_log2;
     ap.normrope = 0;
-    ap.kv = m;
+    ap.kv = m; ap.kv_seqs = cc ? cc->max_batch : b;
     ap.omax = hd->amax;
     ap.err = hd->dev_err;
     CK(attn_tc_launch(ap, b, hd->attn_out, st));
@@ -601,7 +718,15 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
     lp.best_val = hd->lm_val; lp.best_idx = hd->lm_idx;
     int grid = 0;
-    CK(lm_argmax_launch(lp, hd->lm_tiles, hd->num_sms, hd->dev_err, &grid, st));
+    if (dense) {
+      TcParams tp{};
+      tp.M = M; tp.N = (d.vocab_size + 255) / 256 * 256; tp.K = H; tp.err = hd->dev_err;
+      tp.V = d.vocab_size; tp.best_val = hd->lm_val; tp.best_idx = hd->lm_idx;
+      CK(tc_gemm_launch(hd->hn, hd->lm_tiles, true, kTcArgmax, tp, st));
+      grid = tp.N / 256;
+    } else {
+      CK(lm_argmax_launch(lp, hd->lm_tiles, hd->num_sms, hd->dev_err, &grid, st));
+    }
     CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, M, B, b, a->out_tokens,
                             a->target_tokens, a->acc_len, a->correction, st));
     launches += 2;
@@ -609,7 +734,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   CK(mark(7));
   if (cc)
     for (int l = 0; l < nl; ++l)
-      for (int s = 0; s < b; ++s) cc->at(l, s) = next[s];
+      for (int s = 0; s < b; ++s) cc->at(l, cseq[s]) = next[s];
   hd->last_launches = launches;
   return DFLASH_OK;
 }
@@ -670,17 +795,21 @@ int dflash_cache_trim(void* cache, int layer, int n) {
   std::lock_guard<std::mutex> lock(c->mu);
   const int l0 = layer < 0 ? 0 : layer, l1 = layer < 0 ? c->layers : layer + 1;
   for (int l = l0; l < l1; ++l)
-    for (int s = 0; s < c->max_batch; ++s) {
-      SeqState& q = c->at(l, s);
-      const int len = std::max(q.hl + q.rl - n, 0);  // dflash.py:204
-      if (len >= q.hl) {
-        q.rl = len - q.hl;
-      } else {
-        q.rl = 0;
-        q.hl = len;
-      }
-      q.offset -= n;                                 // dflash.py:207
-    }
+    for (int s = 0; s < c->max_batch; ++s) trim_state(c->at(l, s), n);
+  return DFLASH_OK;
+}
+
+int dflash_cache_trim_seqs(void* cache, int layer, const int32_t* seqs, const int32_t* counts, int count) {
+  if (!cache || (count > 0 && (!seqs || !counts))) return fail(DFLASH_ERR_INVALID, "NULL argument");
+  Cache* c = static_cast<Cache*>(cache);
+  if (layer >= c->layers) return fail(DFLASH_ERR_INVALID, "layer %d outside [0, %d)", layer, c->layers);
+  for (int i = 0; i < count; ++i)
+    if (seqs[i] < 0 || seqs[i] >= c->max_batch || counts[i] < 0)
+      return fail(DFLASH_ERR_INVALID, "trim entry %d: sequence %d / count %d", i, seqs[i], counts[i]);
+  std::lock_guard<std::mutex> lock(c->mu);
+  const int l0 = layer < 0 ? 0 : layer, l1 = layer < 0 ? c->layers : layer + 1;
+  for (int l = l0; l < l1; ++l)
+    for (int i = 0; i < count; ++i) trim_state(c->at(l, seqs[i]), counts[i]);
   return DFLASH_OK;
 }
 
@@ -689,6 +818,18 @@ int dflash_cache_reset(void* cache) {
   Cache* c = static_cast<Cache*>(cache);
   std::lock_guard<std::mutex> lock(c->mu);
   for (auto& q : c->st) q = SeqState{};
+  return DFLASH_OK;
+}
+
+int dflash_cache_reset_seqs(void* cache, const int32_t* seqs, int count) {
+  if (!cache || (count > 0 && !seqs)) return fail(DFLASH_ERR_INVALID, "NULL argument");
+  Cache* c = static_cast<Cache*>(cache);
+  for (int i = 0; i < count; ++i)
+    if (seqs[i] < 0 || seqs[i] >= c->max_batch)
+      return fail(DFLASH_ERR_INVALID, "sequence %d outside [0, %d)", seqs[i], c->max_batch);
+  std::lock_guard<std::mutex> lock(c->mu);
+  for (int l = 0; l < c->layers; ++l)
+    for (int i = 0; i < count; ++i) c->at(l, seqs[i]) = SeqState{};
   return DFLASH_OK;
 }
 

@@ -19,17 +19,30 @@ namespace dfl {
 // position pos0[s] + i.  Context rows are packed across sequences
 // ([ctx_start[s], ctx_start[s+1]) in the fc / context GEMMs); the RoPE table
 // holds the packed context rows first and then the nseq * block block rows.
-constexpr int kKvMaxSeq = 32;
+// Per-sequence record of one forward (host-built, device-resident).
+struct KvSeq {
+  int ctx_start;   // first packed context row of the sequence (entry nseq: total rows)
+  int n0;          // logical rows stored before this forward
+  int rs_pre;      // ring start while appending
+  int rs_post;     // ring start after eviction (what attention reads)
+  int n_att;       // logical rows attention reads
+  int pos0;        // RoPE position of appended row 0
+  int cseq;        // the sequence's index in the K/V store (its cache slot)
+};
 
 struct KvMap {
   int nseq;                        // 0: plain [seq][kv head][slots] layout, rows 0..kv_len-1
   int sink, ring, slots;           // slots = sink + ring
-  int ctx_start[kKvMaxSeq + 1];    // packed context rows of sequence s
-  int n0[kKvMaxSeq];               // logical rows stored before this forward
-  int rs_pre[kKvMaxSeq];           // ring start while appending
-  int rs_post[kKvMaxSeq];          // ring start after eviction (what attention reads)
-  int n_att[kKvMaxSeq];            // logical rows attention reads
-  int pos0[kKvMaxSeq];             // RoPE position of appended row 0
+  const KvSeq* seq;                // device [nseq + 1]; read only after griddep_wait
+};
+
+// the records travel to the device as a kernel parameter of the first kernel
+// of a forward (rope_table_map) or, beyond kKvChunk records, of kv_upload
+// launches before it
+constexpr int kKvChunk = 150;
+struct KvUpload {
+  int n, off;                      // records [off, off + n) of the map
+  KvSeq s[kKvChunk];
 };
 
 __host__ __device__ __forceinline__ int kv_slot(const KvMap& m, int p, int rs) {
@@ -39,12 +52,12 @@ __host__ __device__ __forceinline__ int kv_slot(const KvMap& m, int p, int rs) {
   return m.sink + j;
 }
 
-// sequence owning packed context row `row` (the last s with ctx_start[s] <= row)
-__host__ __device__ __forceinline__ int kv_seq_of_ctx_row(const KvMap& m, int row) {
-  int lo = 0, hi = m.nseq - 1;
+// sequence owning packed context row `row` (the last s with seq[s].ctx_start <= row)
+__host__ __device__ __forceinline__ int kv_seq_of_ctx_row(const KvSeq* seq, int nseq, int row) {
+  int lo = 0, hi = nseq - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (m.ctx_start[mid] <= row) lo = mid; else hi = mid - 1;
+    if (seq[mid].ctx_start <= row) lo = mid; else hi = mid - 1;
   }
   return lo;
 }
@@ -105,11 +118,27 @@ struct AttnParams {
   float eps;
   int q_row0, k_row0;   // table rows: q row j -> q_row0 + j, k row i -> k_row0 + i
   KvMap kv;             // nseq > 0: sequence s reads logical rows [0, n_att[s]) at rs_post[s]
+                        // of K/V store sequence cseq[s]
+  int kv_seqs;          // nseq > 0: sequences in the K/V store (k, v hold kv_seqs * NKV planes)
   float* omax;          // combine: [NQ, b * block] max |out| per head and row (or NULL)
   int* err;             // device error word for bounded waits (tcgen05 kernel), or NULL
 };
 
-enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2 };
+// Persistent tcgen05 GEMM epilogues (tc_gemm.cu).  The last four serve the
+// block rows once batch * block is a dense contraction (above the W8A16
+// kernel's 64 rows): weights as exact f16 copies of the int8 values, the
+// per-channel scale applied here.
+//   kTcFc     : fp32 store + per-256-column sums of squares (hidden_norm input)
+//   kTcCtxKV  : context K | V of every layer: scale, k RMSNorm + RoPE, KvMap slots
+//   kTcStoreF32 : plain fp32 store
+//   kTcBlkQKV : block q | k | v heads: scale, q/k RMSNorm + RoPE, q -> q_out,
+//               k / v -> KvMap slots (dflash.py:290-305)
+//   kTcResid  : h += acc * scale, per-256-column sums of h^2 (dflash.py:356, :361)
+//   kTcSilu   : 128 gate then 128 up columns per tile -> silu(g) * u (dflash.py:330)
+//   kTcArgmax : B = lm_head vocabulary tiles (lm_pack layout); per-tile row
+//               argmax partials (generate.py:604-606)
+enum TcMode : int { kTcFc = 0, kTcCtxKV = 1, kTcStoreF32 = 2, kTcBlkQKV = 3, kTcResid = 4, kTcSilu = 5,
+                    kTcArgmax = 6 };
 
 struct TcParams {
   int M, N, K;
@@ -128,6 +157,18 @@ struct TcParams {
   int nkv;
   float eps;
   KvMap kv;                 // packed context row -> (sequence, logical row, slot)
+  // kTcBlkQKV (k_out / v_out: this layer's store, k_norm: this layer's [128])
+  __half* q_out;            // [b, NQ, block, 128]
+  const float* q_norm;      // [128]
+  int n_q_heads, block, rope_row0;   // block row m uses table row rope_row0 + m
+  // kTcResid (sumsq_part: [N/256, M])
+  float* h;                 // [M, N] residual stream, updated in place
+  // kTcSilu
+  __half* act;              // [M, N/2]
+  // kTcArgmax
+  int V;                    // vocabulary size (columns >= V are ignored)
+  float* best_val;          // [N/256, M]
+  int* best_idx;
 };
 
 struct LmParams {
@@ -214,9 +255,10 @@ struct SaParams {
 int soft_anchor_ctas(int V, int rows, int num_sms);
 cudaError_t soft_anchor_launch(const SaParams& p, int rows, bool e_tiled, int num_sms, cudaStream_t st);
 cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st);
-// table rows of one forward: packed context rows, then nseq * block block rows (KvMap)
-cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
-                                  cudaStream_t st);
+// table rows of one forward: packed context rows, then nseq * block block rows.
+// Also stores the map's records (host array `seq`, nseq + 1 entries) at m.seq.
+cudaError_t rope_table_map_launch(const KvMap& m, const KvSeq* seq, int block, const float* inv_freq,
+                                  float2* out, cudaStream_t st);
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
                           const float* w, float* hmax, const __nv_bfloat16* anchor, int block,
                           cudaStream_t st);
@@ -225,6 +267,8 @@ cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
                               cudaStream_t st);
+cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* dst, int grp, int period,
+                                   int off, cudaStream_t st);
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st);
 cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st);
 

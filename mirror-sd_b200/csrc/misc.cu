@@ -7,6 +7,8 @@
 //   final_norm   : final RMSNorm (dflash.py:403) -> bf16 for the lm_head and
 //                  the optional hidden-state output
 //   i8_to_f16    : exact f16 copy of int8 weights (context K/V GEMM operand)
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace dfl {
@@ -22,23 +24,36 @@ __global__ void rope_table_kernel(int pos0, int rows, const float* __restrict__ 
   out[idx] = make_float2(c, s);
 }
 
-// rows of one forward: packed context rows (sequence s: positions pos0[s] + i),
-// then block row m = s * block + j at pos0[s] + ctx_s + j
-__global__ void rope_table_map_kernel(const KvMap m, int block, int rows,
-                                      const float* __restrict__ inv_freq, float2* __restrict__ out) {
+// map records of a forward too long to travel with rope_table_map
+__global__ void kv_upload_kernel(const __grid_constant__ KvUpload up, KvSeq* __restrict__ dst) {
   griddep_wait();
   griddep_launch_dependents();
+  for (int i = threadIdx.x; i < up.n; i += blockDim.x) dst[up.off + i] = up.s[i];
+}
+
+// rows of one forward: packed context rows (sequence s: positions pos0[s] + i),
+// then block row m = s * block + j at pos0[s] + ctx_s + j.  With up.n > 0 the
+// whole map travels in `up` (block 0 stores it at m.seq); otherwise earlier
+// kv_upload launches stored it.
+__global__ void rope_table_map_kernel(const __grid_constant__ KvUpload up, const KvMap m, int block,
+                                      int rows, const float* __restrict__ inv_freq,
+                                      float2* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < up.n; i += blockDim.x) const_cast<KvSeq*>(m.seq)[i] = up.s[i];
+  const KvSeq* seq = up.n > 0 ? up.s : m.seq;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * 64) return;
   const int r = idx >> 6, i = idx & 63;
-  const int nctx = m.ctx_start[m.nseq];
+  const int nctx = seq[m.nseq].ctx_start;
   int pos;
   if (r < nctx) {
-    const int s = kv_seq_of_ctx_row(m, r);
-    pos = m.pos0[s] + (r - m.ctx_start[s]);
+    const int s = kv_seq_of_ctx_row(seq, m.nseq, r);
+    pos = seq[s].pos0 + (r - seq[s].ctx_start);
   } else {
     const int s = (r - nctx) / block, j = (r - nctx) - s * block;
-    pos = m.pos0[s] + (m.ctx_start[s + 1] - m.ctx_start[s]) + j;
+    pos = seq[s].pos0 + (seq[s + 1].ctx_start - seq[s].ctx_start) + j;
   }
   const float ang = static_cast<float>(pos) * inv_freq[i];
   float sn, cs;
@@ -174,6 +189,17 @@ __global__ void i8_to_f16_kernel(const int8_t* __restrict__ src, size_t n, __hal
     dst[i] = __int2half_rn(static_cast<int>(src[i]));
 }
 
+// row r of int8 [rows, K] -> f16 row (r / grp) * period + off + r % grp of dst
+__global__ void i8_to_f16_rows_kernel(const int8_t* __restrict__ src, int rows, int K, __half* __restrict__ dst,
+                                      int grp, int period, int off) {
+  const size_t n = (size_t)rows * K;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / K), k = (int)(i - (size_t)r * K);
+    const size_t dr = (size_t)(r / grp) * period + off + r % grp;
+    dst[dr * K + k] = __int2half_rn(static_cast<int>(src[i]));
+  }
+}
+
 __global__ void f16_to_f32_kernel(const __half* __restrict__ src, size_t n, float* __restrict__ dst) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
@@ -187,12 +213,29 @@ cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2*
   return cudaGetLastError();
 }
 
-cudaError_t rope_table_map_launch(const KvMap& m, int block, const float* inv_freq, float2* out,
-                                  cudaStream_t st) {
-  if (m.nseq < 1 || m.nseq > kKvMaxSeq || block < 1) return cudaErrorInvalidValue;
-  const int rows = m.ctx_start[m.nseq] + m.nseq * block;
+cudaError_t rope_table_map_launch(const KvMap& m, const KvSeq* seq, int block, const float* inv_freq,
+                                  float2* out, cudaStream_t st) {
+  if (m.nseq < 1 || block < 1 || !m.seq) return cudaErrorInvalidValue;
+  const int n = m.nseq + 1;
+  const int rows = seq[m.nseq].ctx_start + m.nseq * block;
+  KvUpload up;
+  up.n = 0;
+  up.off = 0;
+  if (n <= kKvChunk) {
+    up.n = n;
+    for (int i = 0; i < n; ++i) up.s[i] = seq[i];
+  } else {
+    DFL_TRY(max_smem_carveout(kv_upload_kernel));
+    for (int off = 0; off < n; off += kKvChunk) {
+      KvUpload c;
+      c.off = off;
+      c.n = std::min(kKvChunk, n - off);
+      for (int i = 0; i < c.n; ++i) c.s[i] = seq[off + i];
+      DFL_TRY(launch_pdl(kv_upload_kernel, dim3(1), dim3(256), 0, st, c, const_cast<KvSeq*>(m.seq)));
+    }
+  }
   DFL_TRY(max_smem_carveout(rope_table_map_kernel));
-  return launch_pdl(rope_table_map_kernel, dim3((rows * 64 + 255) / 256), dim3(256), 0, st, m, block,
+  return launch_pdl(rope_table_map_kernel, dim3((rows * 64 + 255) / 256), dim3(256), 0, st, up, m, block,
                     rows, inv_freq, out);
 }
 cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, float* hstat,
@@ -224,6 +267,12 @@ cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, in
 }
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st) {
   i8_to_f16_kernel<<<1024, 256, 0, st>>>(src, n, dst);
+  return cudaGetLastError();
+}
+cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* dst, int grp, int period,
+                                   int off, cudaStream_t st) {
+  if (rows < 1 || K < 1 || grp < 1) return cudaErrorInvalidValue;
+  i8_to_f16_rows_kernel<<<2048, 256, 0, st>>>(src, rows, K, dst, grp, period, off);
   return cudaGetLastError();
 }
 cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st) {

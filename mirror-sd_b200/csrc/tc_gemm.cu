@@ -49,6 +49,71 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 
 
 
+// One 128-column head of this thread's accumulator row (TMEM columns tcol ..
+// tcol+127): y = acc * scale, then, when nw is given, RMSNorm over the head
+// (weight nw) and neox RoPE from the (cos, sin) table row cs; f16 store to
+// dst.  Every lane of the warp calls it (tcgen05.ld is warp-wide); only rows
+// with row_ok store.
+__device__ __forceinline__ void tc_store_head(uint32_t tcol, const float* __restrict__ sc,
+                                              const float* __restrict__ nw, const float2* __restrict__ cs,
+                                              float eps, __half* dst, bool row_ok) {
+  float rstd = 1.f;
+  if (nw) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t r[32];
+      tmem_ld32(tcol + ch * 32, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
+        ss += y * y;
+      }
+    }
+    rstd = rsqrtf(ss / 128.0f + eps);
+  }
+#pragma unroll 1
+  for (int half = 0; half < 2; ++half) {
+    uint32_t r1[32], r2[32];
+    tmem_ld32(tcol + half * 32, r1);
+    tmem_ld32(tcol + 64 + half * 32, r2);
+    tmem_ld_wait();
+    if (row_ok) {
+      uint32_t o1[16], o2[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float a[2], b[2];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int d = half * 32 + e + t;
+          float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
+          float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
+          if (nw) {
+            y1 = y1 * rstd * __ldg(nw + d);
+            y2 = y2 * rstd * __ldg(nw + d + 64);
+            const float2 t2 = __ldg(cs + d);
+            a[t] = y1 * t2.x - y2 * t2.y;
+            b[t] = y1 * t2.y + y2 * t2.x;
+          } else {
+            a[t] = y1;
+            b[t] = y2;
+          }
+        }
+        o1[e / 2] = pack_f16x2(a[0], a[1]);
+        o2[e / 2] = pack_f16x2(b[0], b[1]);
+      }
+      uint4* d1 = reinterpret_cast<uint4*>(dst + half * 32);
+      uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + half * 32);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        d1[v] = make_uint4(o1[4 * v], o1[4 * v + 1], o1[4 * v + 2], o1[4 * v + 3]);
+        d2[v] = make_uint4(o2[4 * v], o2[4 * v + 1], o2[4 * v + 2], o2[4 * v + 3]);
+      }
+    }
+  }
+}
+
 // tensor maps of the A column blocks (one, or one per source array)
 template <int NSRC>
 struct TcAMaps {
@@ -118,7 +183,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             col -= f * p.a_cols;
           }
           tma_load_2d(sa, &maps_a.m[f], &full[s], col, mb * TC_BM);
-          tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, nb * TC_BN);
+          if (MODE == kTcArgmax) {
+            // B = the lm_head's pre-swizzled vocabulary tiles: 16 KB blocks
+            // [vt][kb][128 rows][128 B], two 128-row tiles per n-block
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+              tma_load_2d(sa + TC_A_BYTES + t * (TC_B_BYTES / 2), &map_b, &full[s], 0,
+                          ((2 * nb + t) * nk + kb) * 128);
+          } else {
+            tma_load_2d(sa + TC_A_BYTES, &map_b, &full[s], kb * TC_BK, nb * TC_BN);
+          }
         }
       }
     }
@@ -184,11 +258,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
           }
           if (MODE == kTcFc && row_ok) p.sumsq_part[(size_t)nb * p.M + row] = ss;
-        } else {  // kTcCtxKV: two 128-wide heads per tile
+        } else if (MODE == kTcCtxKV) {  // two 128-wide heads per tile
           // sequence and slot of this packed context row (rows >= M are never stored)
           const int crow = row_ok ? row : 0;
-          const int bi = kv_seq_of_ctx_row(p.kv, crow);
-          const int slot = kv_slot(p.kv, p.kv.n0[bi] + crow - p.kv.ctx_start[bi], p.kv.rs_pre[bi]);
+          const int bi = kv_seq_of_ctx_row(p.kv.seq, p.kv.nseq, crow);
+          const KvSeq sq = p.kv.seq[bi];
+          const int slot = kv_slot(p.kv, sq.n0 + crow - sq.ctx_start, sq.rs_pre);
           const int per_layer = 2 * p.nkv * 128;
 #pragma unroll 1
           for (int hh = 0; hh < 2; ++hh) {
@@ -197,67 +272,107 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int within = col0 - layer * per_layer;
             const bool is_v = within >= p.nkv * 128;
             const int kvh = (within % (p.nkv * 128)) / 128;
-            const float* sc = p.scale + col0;
-            float rstd = 1.f;
-            if (!is_v) {
-              float ss = 0.f;
-#pragma unroll 1
-              for (int ch = 0; ch < 4; ++ch) {
-                uint32_t r[32];
-                tmem_ld32(tbase + hh * 128 + ch * 32, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                  const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
-                  ss += y * y;
-                }
-              }
-              rstd = rsqrtf(ss / 128.0f + p.eps);
-            }
             __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
-                          (((size_t)bi * p.nkv + kvh) * p.kv.slots + slot) * 128;
-            const float* kn = p.k_norm + layer * 128;
-            const float2* cs = p.rope + (size_t)crow * 64;
+                          (((size_t)sq.cseq * p.nkv + kvh) * p.kv.slots + slot) * 128;
+            tc_store_head(tbase + hh * 128, p.scale + col0, is_v ? nullptr : p.k_norm + layer * 128,
+                          p.rope + (size_t)crow * 64, p.eps, dst, row_ok);
+          }
+        } else if (MODE == kTcBlkQKV) {  // block rows: q | k | v heads, two per tile
+          const int m = row_ok ? row : 0;
+          const int bi = m / p.block, j = m - bi * p.block;
+          const KvSeq sq = p.kv.seq[bi];
+          const int lrow = sq.n0 + (p.kv.seq[bi + 1].ctx_start - sq.ctx_start) + j;
+          const int slot = kv_slot(p.kv, lrow, sq.rs_pre);
 #pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-              uint32_t r1[32], r2[32];
-              tmem_ld32(tbase + hh * 128 + half * 32, r1);
-              tmem_ld32(tbase + hh * 128 + 64 + half * 32, r2);
-              tmem_ld_wait();
-              if (row_ok) {
-                uint32_t o1[16], o2[16];
+          for (int hh = 0; hh < 2; ++hh) {
+            const int col0 = n0 + hh * 128;
+            const int head = col0 / 128;
+            __half* dst;
+            const float* nw;
+            if (head < p.n_q_heads) {
+              dst = p.q_out + (((size_t)bi * p.n_q_heads + head) * p.block + j) * 128;
+              nw = p.q_norm;
+            } else {
+              const bool is_k = head < p.n_q_heads + p.nkv;
+              const int kvh = head - p.n_q_heads - (is_k ? 0 : p.nkv);
+              dst = (is_k ? p.k_out : p.v_out) + (((size_t)sq.cseq * p.nkv + kvh) * p.kv.slots + slot) * 128;
+              nw = is_k ? p.k_norm : nullptr;
+            }
+            tc_store_head(tbase + hh * 128, p.scale + col0, nw, p.rope + (size_t)(p.rope_row0 + m) * 64,
+                          p.eps, dst, row_ok);
+          }
+        } else if (MODE == kTcResid) {  // h += acc * scale, per-256-column sum of h^2
+          float ss = 0.f;
+#pragma unroll 1
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tbase + ch * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              float4* hp = reinterpret_cast<float4*>(p.h + (size_t)row * p.N + n0 + ch * 32);
+              const float4* sc = reinterpret_cast<const float4*>(p.scale + n0 + ch * 32);
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                  float a[2], b[2];
-#pragma unroll
-                  for (int t = 0; t < 2; ++t) {
-                    const int d = half * 32 + e + t;
-                    float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
-                    float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
-                    if (!is_v) {
-                      y1 = y1 * rstd * __ldg(kn + d);
-                      y2 = y2 * rstd * __ldg(kn + d + 64);
-                      const float2 t2 = __ldg(cs + d);
-                      const float cth = t2.x, sth = t2.y;
-                      a[t] = y1 * cth - y2 * sth;
-                      b[t] = y1 * sth + y2 * cth;
-                    } else {
-                      a[t] = y1;
-                      b[t] = y2;
-                    }
-                  }
-                  o1[e / 2] = pack_f16x2(a[0], a[1]);
-                  o2[e / 2] = pack_f16x2(b[0], b[1]);
-                }
-                uint4* d1 = reinterpret_cast<uint4*>(dst + half * 32);
-                uint4* d2 = reinterpret_cast<uint4*>(dst + 64 + half * 32);
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                  d1[v] = make_uint4(o1[4 * v], o1[4 * v + 1], o1[4 * v + 2], o1[4 * v + 3]);
-                  d2[v] = make_uint4(o2[4 * v], o2[4 * v + 1], o2[4 * v + 2], o2[4 * v + 3]);
-                }
+              for (int v = 0; v < 8; ++v) {
+                const float4 s4 = __ldg(sc + v);
+                float4 h4 = hp[v];
+                h4.x += __uint_as_float(r[4 * v]) * s4.x;
+                h4.y += __uint_as_float(r[4 * v + 1]) * s4.y;
+                h4.z += __uint_as_float(r[4 * v + 2]) * s4.z;
+                h4.w += __uint_as_float(r[4 * v + 3]) * s4.w;
+                ss += h4.x * h4.x + h4.y * h4.y + h4.z * h4.z + h4.w * h4.w;
+                hp[v] = h4;
               }
             }
+          }
+          if (row_ok) p.sumsq_part[(size_t)nb * p.M + row] = ss;
+        } else if (MODE == kTcSilu) {  // 128 gate columns, then the 128 matching up columns
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ++ch) {
+            uint32_t rg[32], ru[32];
+            tmem_ld32(tbase + ch * 32, rg);
+            tmem_ld32(tbase + 128 + ch * 32, ru);
+            tmem_ld_wait();
+            if (row_ok) {
+              const float* sg = p.scale + n0 + ch * 32;
+              const float* su = sg + 128;
+              uint32_t o[16];
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                float a[2];
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                  const float g = __uint_as_float(rg[e + t]) * __ldg(sg + e + t);
+                  const float u = __uint_as_float(ru[e + t]) * __ldg(su + e + t);
+                  a[t] = (g / (1.0f + expf(-g))) * u;
+                }
+                o[e / 2] = pack_f16x2(a[0], a[1]);
+              }
+              uint4* dst = reinterpret_cast<uint4*>(p.act + (size_t)row * (p.N / 2) + nb * 128 + ch * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
+          }
+        } else {  // kTcArgmax: first index of the row maximum over the tile's columns < V
+          float best = -INFINITY;
+          int bidx = 0x7fffffff;
+#pragma unroll 1
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tbase + ch * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = n0 + ch * 32 + e;
+              const float x = __uint_as_float(r[e]);
+              if (col < p.V && x > best) {
+                best = x;
+                bidx = col;
+              }
+            }
+          }
+          if (row_ok) {
+            p.best_val[(size_t)nb * p.M + row] = best;
+            p.best_idx[(size_t)nb * p.M + row] = bidx;
           }
         }
       }
@@ -294,9 +409,9 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // 2-D K-major map: inner dim `inner` (elements), outer dim rows `ld` elements
-// apart; box 64 x box_rows, 128B swizzle
+// apart; box 64 x box_rows, 128B swizzle (or none, for data stored pre-swizzled)
 static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inner, uint64_t rows,
-                     uint32_t box_rows, uint64_t ld) {
+                     uint32_t box_rows, uint64_t ld, bool swizzle = true) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   if (!base || (reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || ld < inner) return false;
@@ -306,8 +421,8 @@ static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inn
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -331,16 +446,24 @@ static cudaError_t tc_dispatch(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, b
   if (bf16) {
     if (mode == kTcFc) return tc_launch_t<1, kTcFc, NSRC>(ma, mb, p, st);
     if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32, NSRC>(ma, mb, p, st);
+    if constexpr (NSRC == 1) {
+      if (mode == kTcArgmax) return tc_launch_t<1, kTcArgmax, 1>(ma, mb, p, st);
+    }
   } else {
     if constexpr (NSRC == 1) {
       if (mode == kTcCtxKV) return tc_launch_t<0, kTcCtxKV, 1>(ma, mb, p, st);
+      if (mode == kTcBlkQKV) return tc_launch_t<0, kTcBlkQKV, 1>(ma, mb, p, st);
+      if (mode == kTcResid) return tc_launch_t<0, kTcResid, 1>(ma, mb, p, st);
+      if (mode == kTcSilu) return tc_launch_t<0, kTcSilu, 1>(ma, mb, p, st);
     }
     if (mode == kTcStoreF32) return tc_launch_t<0, kTcStoreF32, NSRC>(ma, mb, p, st);
   }
   return cudaErrorInvalidValue;
 }
 
-// A [M, K] and B [N, K] K-major, both bf16 or both f16.  mode: TcMode.
+// A [M, K] and B [N, K] K-major, both bf16 or both f16.  mode: TcMode.  For
+// kTcArgmax, B is the lm_pack tile array of a vocabulary of p.V rows and N is
+// p.V rounded up to 256.
 cudaError_t tc_gemm_launch_src(const TcSources& a, const void* B, bool bf16, int mode, TcParams p,
                                cudaStream_t st) {
   if (p.M < 1 || p.N % TC_BN || p.K % TC_BK || p.K < TC_BK) return cudaErrorInvalidValue;
@@ -348,13 +471,19 @@ cudaError_t tc_gemm_launch_src(const TcSources& a, const void* B, bool bf16, int
     return cudaErrorInvalidValue;
   p.a_cols = a.cols;
   CUtensorMap mb;
-  if (!make_map(&mb, B, bf16, p.K, p.N, TC_BN, p.K)) return cudaErrorInvalidValue;
+  if (mode == kTcArgmax) {
+    const uint64_t vt = ((uint64_t)p.V + 127) / 128;
+    if (!bf16 || p.V < 1 || (uint64_t)p.N < vt * 128 || (uint64_t)p.N > vt * 128 + 128) return cudaErrorInvalidValue;
+    if (!make_map(&mb, B, true, TC_BK, vt * (p.K / TC_BK) * 128, 128, TC_BK, false)) return cudaErrorInvalidValue;
+  } else if (!make_map(&mb, B, bf16, p.K, p.N, TC_BN, p.K)) {
+    return cudaErrorInvalidValue;
+  }
   if (a.n == 1) {
     TcAMaps<1> ma;
     if (!make_map(&ma.m[0], a.ptr[0], bf16, a.cols, p.M, TC_BM, a.ld[0])) return cudaErrorInvalidValue;
     return tc_dispatch<1>(ma, mb, bf16, mode, p, st);
   }
-  if (mode == kTcCtxKV) return cudaErrorInvalidValue;
+  if (mode != kTcFc && mode != kTcStoreF32) return cudaErrorInvalidValue;
   TcAMaps<kTcMaxSrc> ma;
   for (int f = 0; f < a.n; ++f)
     if (!make_map(&ma.m[f], a.ptr[f], bf16, a.cols, p.M, TC_BM, a.ld[f])) return cudaErrorInvalidValue;

@@ -239,9 +239,10 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
     } else {
       const int kvh = is_k ? head - p.n_q_heads : head - p.n_q_heads - p.n_kv_heads;
       __half* base = is_k ? p.k_out : p.v_out;
-      const int lrow = p.kv.n0[bi] + (p.kv.ctx_start[bi + 1] - p.kv.ctx_start[bi]) + j;
-      const int slot = kv_slot(p.kv, lrow, p.kv.rs_pre[bi]);
-      dstp = base + (((size_t)bi * p.n_kv_heads + kvh) * p.kv.slots + slot) * 128;
+      const KvSeq sq = p.kv.seq[bi];
+      const int lrow = sq.n0 + (p.kv.seq[bi + 1].ctx_start - sq.ctx_start) + j;
+      const int slot = kv_slot(p.kv, lrow, sq.rs_pre);
+      dstp = base + (((size_t)sq.cseq * p.n_kv_heads + kvh) * p.kv.slots + slot) * 128;
     }
     *reinterpret_cast<uint2*>(dstp + lane * 4) = o;
   }

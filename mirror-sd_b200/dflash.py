@@ -218,8 +218,21 @@ class _CacheStore:
     def trim(self, layer, n):
         N.check(self._lib.dflash_cache_trim(self.ptr, layer, int(n)), "dflash_cache_trim")
 
+    def trim_seqs(self, layer, seqs, counts):
+        seqs, counts = [int(s) for s in seqs], [int(c) for c in counts]
+        if len(seqs) != len(counts):
+            raise ValueError("seqs and counts differ in length")
+        sa = (ctypes.c_int32 * len(seqs))(*seqs)
+        ca = (ctypes.c_int32 * len(counts))(*counts)
+        N.check(self._lib.dflash_cache_trim_seqs(self.ptr, layer, sa, ca, len(seqs)), "dflash_cache_trim_seqs")
+
     def reset(self):
         N.check(self._lib.dflash_cache_reset(self.ptr), "dflash_cache_reset")
+
+    def reset_seqs(self, seqs):
+        seqs = [int(s) for s in seqs]
+        sa = (ctypes.c_int32 * len(seqs))(*seqs)
+        N.check(self._lib.dflash_cache_reset_seqs(self.ptr, sa, len(seqs)), "dflash_cache_reset_seqs")
 
     def read(self, layer):
         """(keys, values) f16 [b, NKV, len, 128] in logical order, or a list of
@@ -290,6 +303,15 @@ class DFlashCache(list):
     def reset(self):
         self.store.reset()
 
+    def trim_seqs(self, seqs, counts):
+        """Per-sequence rollback on every layer: cache sequence seqs[i] drops
+        its last counts[i] rows (one entry per sequence of a batched decode)."""
+        self.store.trim_seqs(-1, seqs, counts)
+
+    def reset_seqs(self, seqs):
+        """Empty the listed sequences (offset 0, no rows)."""
+        self.store.reset_seqs(seqs)
+
 
 # ----------------------------------------------------------------------------
 # the draft model
@@ -299,11 +321,17 @@ class DFlashDraftModel:
 
     ``lm_head`` is the target's (tied) embedding matrix [V, H] in bf16; it is
     referenced, not copied (generate.py:435-436: the draft does not own it).
+
+    Capacities: ``max_batch`` sequences of up to ``max_block`` block rows and
+    ``max_ctx`` new context rows each per step; ``max_ctx_rows`` bounds the
+    context rows of one step over all sequences (0: max_batch * max_ctx).
+    Above 64 block rows per step the projections run as dense tensor-core
+    GEMMs over f16 copies of the int8 weights (twice their memory).
     """
 
     def __init__(self, config: DFlashConfig, weights: DFlashWeightsQ8, lm_head: torch.Tensor,
                  max_batch: int = 1, max_ctx: int = 4096, max_block: Optional[int] = None,
-                 device=None):
+                 device=None, max_ctx_rows: int = 0):
         self.config = config
         self.block_size = config.block_size
         self.mask_token_id = config.mask_token_id
@@ -329,7 +357,8 @@ class DFlashDraftModel:
             num_key_value_heads=config.num_key_value_heads, head_dim=config.head_dim,
             vocab_size=config.vocab_size, num_target_features=F,
             rms_norm_eps=config.rms_norm_eps, rope_theta=config.rope_theta,
-            max_batch=self.max_batch, max_block=self.max_block, max_ctx=self.max_ctx)
+            max_batch=self.max_batch, max_block=self.max_block, max_ctx=self.max_ctx,
+            max_ctx_rows=int(max_ctx_rows))
         keep = []  # tensors whose pointers the create call reads
 
         def dev(t, dtype):
@@ -421,7 +450,7 @@ class DFlashDraftModel:
                    target_tokens=None, want_hidden: bool = True, want_tokens: bool = True,
                    out_hidden=None, out_tokens=None, acc_len=None, correction=None,
                    hidden_fp32: bool = False, phase_events=None, cache=None, ctx_lens=None,
-                   rope_offsets=None, anchor_logits=None, anchor_top_k: int = 8):
+                   rope_offsets=None, anchor_logits=None, anchor_top_k: int = 8, cache_seqs=None):
         """One draft step on the device: final-normed hidden states (bf16, or
         fp32 with ``hidden_fp32``), greedy draft ids for rows 1..q-1 and, given
         the verifier's posterior ``target_tokens`` [b, q], the accepted length
@@ -438,7 +467,12 @@ class DFlashDraftModel:
         logits at each sequence's correction position) replaces row 0 of every
         block with the soft anchor: the softmax-weighted sum of the
         ``anchor_top_k`` most likely tokens' embeddings (generate.py:1422-1436),
-        computed on the device inside the step."""
+        computed on the device inside the step.
+
+        ``cache_seqs`` (with ``cache``): the cache sequence each of the b
+        sequences of this step reads and extends (distinct indices below the
+        cache's max_batch), so a step may cover any subset of the cache's
+        sequences; default 0..b-1."""
         noise = self._as_dev(noise_embedding, torch.bfloat16)
         if noise.dim() != 3:
             raise ValueError("noise_embedding [b, q, H] expected")
@@ -536,6 +570,12 @@ class DFlashDraftModel:
             ptrs = (ctypes.c_void_p * F)(*[t.data_ptr() for t in layers])
             args.target_layers = ctypes.cast(ptrs, ctypes.POINTER(ctypes.c_void_p))
             args.target_layers_ld = layers[0].stride(0)
+        if cache_seqs is not None:
+            cs = [int(c) for c in cache_seqs]
+            if len(cs) != b:
+                raise ValueError(f"cache_seqs needs {b} entries")
+            cs_arr = (ctypes.c_int32 * b)(*cs)
+            args.cache_seqs = cs_arr
         if phase_events is not None:
             if len(phase_events) < N.DFLASH_PHASES:
                 raise ValueError(f"phase_events needs {N.DFLASH_PHASES} events")
@@ -545,7 +585,7 @@ class DFlashDraftModel:
         N.check(self._lib.dflash_forward(self._handle, ctypes.byref(args), self._stream()),
                 "dflash_forward")
         if store is not None:
-            store.batch = b
+            store.batch = max(store.batch, b if cache_seqs is None else max(int(c) for c in cache_seqs) + 1)
         return out_hidden, out_tokens, acc_len, correction
 
     def __call__(self, noise_embedding, target_hidden, mask=None, cache=None, **kwargs):

@@ -197,13 +197,13 @@ def test_soft_anchor_vs_oracle(K, rows, V, H, k, bf16):
     logits = torch.randn(rows, V, generator=g) * 4.0
     if bf16:
         logits = logits.to(torch.bfloat16)
-    # a duplicated top value: the lower index must come first
-    logits[0, 17] = logits[0, 9] = logits[0].max() + 1
+    if V > 17:   # a duplicated top value: the lower index must come first
+        logits[0, 17] = logits[0, 9] = logits[0].max() + 1
     out = K.soft_anchor(logits.cuda(), E.cuda(), k).cpu()
     Ef = E.float().numpy()
     for r in range(rows):
         ids, w, anchor = O.soft_anchor(logits[r].float().numpy(), Ef, k)
-        if r == 0:
+        if r == 0 and V > 17 and k > 1:
             assert list(ids[:2]) == [9, 17]
         assert _bf16_ulps(out[r], anchor) <= 1.0, r
 
