@@ -46,9 +46,14 @@ constexpr int TA_STAGE = 2 * TA_KV_BYTES;  // K then V
 constexpr int TA_QG = 128 * 256;           // one query group: 128 rows x 128 f16
 constexpr float TA_RESCALE = 8.0f;         // log2 of the largest P before O is rescaled
 
-template <int NG>
+// NS_ 0: the deepest K/V ring shared memory allows (one CTA per SM); 2: a
+// double buffer small enough for two CTAs per SM, for grids with many CTAs
+// per SM (many sequences), where the second CTA hides the per-tile latency
+template <int NG, int NS_ = 0>
 struct TaCfg {
-  static constexpr int NS = NG == 1 ? 6 : 5;  // K/V stages (shared memory allows)
+  static constexpr int NS = NS_ ? NS_ : (NG == 1 ? 6 : 5);  // K/V stages
+  // registers per thread: two CTAs of THREADS threads must fit in 64K
+  static constexpr int MAX_REGS = NS_ == 2 ? 112 : 255;
   static constexpr int SOFT_WARPS = 4 * NG;
   static constexpr int PROD_WARP0 = SOFT_WARPS;
   static constexpr int MMA_WARP = SOFT_WARPS + TA_PROD;
@@ -132,11 +137,11 @@ __device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
   return y;
 }
 
-template <int NG>
-__global__ void __launch_bounds__(TaCfg<NG>::THREADS, 1)
+template <int NG, int NS_>
+__global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG, NS_>::MAX_REGS))
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                    const AttnParams p) {
-  using C = TaCfg<NG>;
+  using C = TaCfg<NG, NS_>;
   constexpr int TA_NS = C::NS;
   griddep_wait();
   griddep_launch_dependents();
@@ -454,10 +459,10 @@ static bool map_kv(CUtensorMap* m, const void* base, uint64_t slots, uint64_t pl
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NG>
+template <int NG, int NS_>
 static cudaError_t attn_tc_launch_t(const AttnParams& p, int batch, cudaStream_t st) {
-  using C = TaCfg<NG>;
-  auto kern = attn_tc_kernel<NG>;
+  using C = TaCfg<NG, NS_>;
+  auto kern = attn_tc_kernel<NG, NS_>;
   CUtensorMap mk, mv;
   const uint64_t planes = (uint64_t)(p.kv.nseq > 0 ? p.kv_seqs : batch) * p.nkv;
   if (planes < (uint64_t)batch * p.nkv || !map_kv(&mk, p.k, p.kv_cap, planes) || !map_kv(&mv, p.v, p.kv_cap, planes))
@@ -472,7 +477,18 @@ cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStre
   const int R = G * p.block;
   if (p.nq % p.nkv || R < 1 || R > 256 || p.kv_len < 1 || p.chunk % TA_TK || p.normrope)
     return cudaErrorInvalidValue;
-  DFL_TRY(R <= 128 ? attn_tc_launch_t<1>(p, batch, st) : attn_tc_launch_t<2>(p, batch, st));
+  int dev = 0, sms = 148;
+  DFL_TRY(cudaGetDevice(&dev));
+  DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const long long ctas = (long long)p.splits * p.nkv * batch;
+  cudaError_t e;
+  if (R > 128)
+    e = attn_tc_launch_t<2, 0>(p, batch, st);
+  else if (ctas >= 2LL * sms)
+    e = attn_tc_launch_t<1, 2>(p, batch, st);
+  else
+    e = attn_tc_launch_t<1, 0>(p, batch, st);
+  DFL_TRY(e);
   return attn_combine_launch(p, batch, out, st);
 }
 

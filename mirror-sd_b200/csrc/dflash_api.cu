@@ -709,8 +709,9 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     launches += 10;  // 2 norms + 2 limb splits, qkv, attention partial + combine, o, gate|up, down
   }
   CK(mark(5));
+  // dense path: the lm_head reads only rows 1..B-1 of every block, packed
   CK(final_norm_launch(hd->h, hd->hstat, hparts, M, H, hd->norm, d.rms_norm_eps, hd->hn,
-                       a->out_hidden, a->out_hidden_fp32 != 0, st));
+                       a->out_hidden, a->out_hidden_fp32 != 0, st, B, dense ? 1 : 0));
   launches += 1;
   CK(mark(6));
   if (a->out_tokens || a->target_tokens) {
@@ -720,15 +721,15 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     int grid = 0;
     if (dense) {
       TcParams tp{};
-      tp.M = M; tp.N = (d.vocab_size + 255) / 256 * 256; tp.K = H; tp.err = hd->dev_err;
+      tp.M = b * (B - 1); tp.N = (d.vocab_size + 255) / 256 * 256; tp.K = H; tp.err = hd->dev_err;
       tp.V = d.vocab_size; tp.best_val = hd->lm_val; tp.best_idx = hd->lm_idx;
       CK(tc_gemm_launch(hd->hn, hd->lm_tiles, true, kTcArgmax, tp, st));
       grid = tp.N / 256;
     } else {
       CK(lm_argmax_launch(lp, hd->lm_tiles, hd->num_sms, hd->dev_err, &grid, st));
     }
-    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, M, B, b, a->out_tokens,
-                            a->target_tokens, a->acc_len, a->correction, st));
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, dense ? b * (B - 1) : M, B, b, a->out_tokens,
+                            a->target_tokens, a->acc_len, a->correction, st, dense ? 1 : 0));
     launches += 2;
   }
   CK(mark(7));

@@ -229,9 +229,12 @@ size_t lm_pack_bytes(int V, int H);
 cudaError_t lm_pack_launch(const __nv_bfloat16* E, int V, int H, uint8_t* out, cudaStream_t st);
 cudaError_t lm_argmax_launch(const LmParams& p, const uint8_t* e_tiles, int num_sms, int* err,
                              int* grid_out, cudaStream_t st);
+// per-row argmax partials [nparts, M] -> draft ids of rows 1..block-1 and
+// acceptance; first = 1 when the partial rows omit row 0 of every block
+// (M = batch * (block - 1))
 cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int M, int block,
                                  int batch, int32_t* out_tokens, const int32_t* target,
-                                 int32_t* acc_len, int32_t* correction, cudaStream_t st);
+                                 int32_t* acc_len, int32_t* correction, cudaStream_t st, int first = 0);
 cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch, int block,
                           int32_t* acc_len, int32_t* correction, cudaStream_t st);
 
@@ -264,9 +267,11 @@ cudaError_t init_h_launch(const __nv_bfloat16* noise, int M, int H, float* h, fl
                           cudaStream_t st);
 cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int rows, int H,
                             const float* w, float eps, __half* out, cudaStream_t st);
+// hn: bf16 [M, H], or with drop_first the rows j >= 1 of every block of
+// `block` rows, packed (row 0 of each block is not written)
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
-                              cudaStream_t st);
+                              cudaStream_t st, int block = 1, int drop_first = 0);
 cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* dst, int grp, int period,
                                    int off, cudaStream_t st);
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st);

@@ -218,7 +218,7 @@ __global__ void lm_pack_kernel(const __nv_bfloat16* __restrict__ E, int V, int H
 // longest matching prefix and the correction token (generate.py:722-728).
 __global__ void argmax_accept_kernel(const float* __restrict__ best_val,
                                      const int* __restrict__ best_idx, int nparts, int M, int block,
-                                     int32_t* __restrict__ out_tokens,
+                                     int first, int32_t* __restrict__ out_tokens,
                                      const int32_t* __restrict__ target, int32_t* __restrict__ acc_len,
                                      int32_t* __restrict__ correction) {
   griddep_wait();
@@ -227,7 +227,7 @@ __global__ void argmax_accept_kernel(const float* __restrict__ best_val,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ int toks[1024];
   for (int j = 1 + warp; j < block; j += blockDim.x >> 5) {
-    const int m = b * block + j;
+    const int m = b * (block - first) + j - first;   // partial row (rows j < first are absent)
     float v = -INFINITY;
     int idx = 0x7fffffff;
     for (int q = lane; q < nparts; q += 32) {
@@ -339,11 +339,11 @@ cudaError_t lm_pack_launch(const __nv_bfloat16* E, int V, int H, uint8_t* out, c
 
 cudaError_t argmax_accept_launch(const float* bv, const int* bi, int nparts, int M, int block,
                                  int batch, int32_t* out_tokens, const int32_t* target,
-                                 int32_t* acc_len, int32_t* correction, cudaStream_t st) {
-  if (block < 2 || block > 1024) return cudaErrorInvalidValue;
+                                 int32_t* acc_len, int32_t* correction, cudaStream_t st, int first) {
+  if (block < 2 || block > 1024 || first < 0 || first > 1) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(argmax_accept_kernel));
   return launch_pdl(argmax_accept_kernel, dim3(batch), dim3(32 * (block - 1 < 32 ? block - 1 : 32)), 0,
-                    st, bv, bi, nparts, M, block, out_tokens, target, acc_len, correction);
+                    st, bv, bi, nparts, M, block, first, out_tokens, target, acc_len, correction);
 }
 
 cudaError_t accept_launch(const int32_t* draft, const int32_t* target, int batch, int block,

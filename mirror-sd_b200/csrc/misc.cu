@@ -153,10 +153,14 @@ __global__ void ctx_norm_kernel(const float* __restrict__ raw, const float* __re
 template <bool OUT_F32>
 __global__ void final_norm_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
                                   int hparts, int M, int H, const float* __restrict__ w, float eps,
-                                  __nv_bfloat16* __restrict__ hn, void* __restrict__ out) {
+                                  __nv_bfloat16* __restrict__ hn, void* __restrict__ out, int block,
+                                  int drop_first) {
   griddep_wait();
   griddep_launch_dependents();
   const int row = blockIdx.x;
+  const int j = row % block;
+  const bool keep = !drop_first || j > 0;
+  const int hrow = drop_first ? (row / block) * (block - 1) + j - 1 : row;
   __shared__ float rs;
   if (threadIdx.x == 0) {
     float ss = 0.f;
@@ -173,7 +177,7 @@ __global__ void final_norm_kernel(const float* __restrict__ h, const float* __re
     uint2 o;
     o.x = pack_bf16x2(y.x, y.y);
     o.y = pack_bf16x2(y.z, y.w);
-    *reinterpret_cast<uint2*>(hn + (size_t)row * H + k) = o;
+    if (keep) *reinterpret_cast<uint2*>(hn + (size_t)hrow * H + k) = o;
     if (out) {
       if (OUT_F32)
         *reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)row * H + k) = y;
@@ -254,16 +258,16 @@ cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int
 }
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,
-                              cudaStream_t st) {
-  if (H % 4) return cudaErrorInvalidValue;
+                              cudaStream_t st, int block, int drop_first) {
+  if (H % 4 || block < 1 || (drop_first && (block < 2 || M % block))) return cudaErrorInvalidValue;
   const cudaError_t ce = out_f32 ? max_smem_carveout(final_norm_kernel<true>)
                                  : max_smem_carveout(final_norm_kernel<false>);
   if (ce != cudaSuccess) return ce;
   if (out_f32)
     return launch_pdl(final_norm_kernel<true>, dim3(M), dim3(256), 0, st, h, hstat, hparts, M, H, w, eps,
-                      hn, out);
+                      hn, out, block, drop_first);
   return launch_pdl(final_norm_kernel<false>, dim3(M), dim3(256), 0, st, h, hstat, hparts, M, H, w, eps,
-                    hn, out);
+                    hn, out, block, drop_first);
 }
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st) {
   i8_to_f16_kernel<<<1024, 256, 0, st>>>(src, n, dst);

@@ -16,6 +16,9 @@ Cases (27B-class draft dims, 32 block rows):
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
   attn_sweep  block attention, 40/8 heads, 32 queries, ctx 1K..32K, batch 1 and 16
               (prints a markdown table: time, bandwidth, fraction of measured HBM)
+  serve    one stateless draft step of --seqs sequences (default 64) of block 16,
+           ctx 64 each, 8B-class dims: the dense block path (tcgen05 projections
+           and lm_head over f16 weight copies); about 6 GB on the device
 Prints the mean launch time measured with CUDA events and the achieved
 bandwidth (or TFLOP/s for fc).
 """
@@ -74,6 +77,7 @@ def main():
     ap.add_argument("case")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--seqs", type=int, default=64)
     a = ap.parse_args()
     importlib.import_module("mirror-sd_b200")
     K = importlib.import_module("mirror-sd_b200.kernels")
@@ -110,6 +114,23 @@ def main():
         ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.attention(qq, kk, vv, workspace=ws)
         nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * 40 * M * L * 128
+    elif a.case == "serve":
+        pkg = importlib.import_module("mirror-sd_b200")
+        cfg = pkg.DFlashConfig(hidden_size=4096, num_hidden_layers=5, intermediate_size=12288,
+                               num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                               vocab_size=151936, block_size=16)
+        cfg.target_layer_ids = list(range(5))
+        w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+        n, C, B, H = a.seqs, 64, 16, 4096
+        model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=n, max_ctx=C, max_block=B, device=dev)
+        noise = (torch.randn(n, B, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        th = torch.randn(n, C, 5 * H, generator=g, device=dev).to(torch.bfloat16)
+        toks = torch.empty((n, B - 1), dtype=torch.int32, device=dev)
+        fn = lambda: model.draft_step(noise, th, want_hidden=False, out_tokens=toks)
+        Mb = n * B
+        params = 5 * ((32 + 16) * 128 * H + H * 32 * 128 + 3 * 12288 * H)
+        nbytes = params * 2 + 151936 * H * 2
+        flops = 2 * Mb * (params + 151936 * H) + 2 * n * C * (5 * H * H + H * 5 * 2 * 8 * 128)
     elif a.case == "fc":
         Mr, Kd, N = 4096, 25600, 5120
         A = torch.randn(Mr, Kd, generator=g, device=dev).to(torch.bfloat16)
