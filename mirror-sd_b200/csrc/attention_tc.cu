@@ -67,20 +67,6 @@ struct TaCfg {
   static constexpr uint32_t TMEM_COLS = NG == 1 ? 256 : 512;
 };
 
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
-      " {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-      "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 // D (TMEM) += A (TMEM, K-major, f16 pairs per column) . B (shared-memory descriptor)
 __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
                                             uint32_t idesc, uint32_t accumulate) {
@@ -113,11 +99,8 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
 }
 
 // map_k / map_v: [batch * NKV planes][kv_cap slots][128] f16, box 64 x 64 x 1
-// non-aligned named barrier: threads of one warp may arrive at different times
-// (producer lane 0 can still be waiting on a stage while its warp-mates arrive)
-__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
-  asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
+// (the producer's named barrier is the non-aligned form: lane 0 can still be
+// waiting on a stage while its warp-mates arrive)
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -399,12 +382,46 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
     if (!active) {
       // padding rows only: nothing to write
     } else if (ntiles == 0 || !ok) {
-      if (valid) {
+      if (valid && p.out) {
+        const int hq = qrow / p.block, jr = qrow - hq * p.block;
+        __half* dst = p.out + ((size_t)bi * p.block + jr) * ((size_t)p.nq * 128) + (size_t)(kvh * G + hq) * 128;
+        for (int d = 0; d < 128; d += 8) *reinterpret_cast<uint4*>(dst + d) = make_uint4(0, 0, 0, 0);
+        if (p.omax) p.omax[(size_t)(kvh * G + hq) * gridDim.z * p.block + (size_t)bi * p.block + jr] = 0.f;
+      } else if (valid) {
         for (int d = 0; d < 128; d += 4) *reinterpret_cast<float4*>(orow + d) = make_float4(0.f, 0.f, 0.f, 0.f);
         p.mpart[pbase + qrow] = -INFINITY;
         p.lpart[pbase + qrow] = 0.f;
       }
-    } else if (mbar_wait(&o_ready[g], 0, p.err, abort_flag)) {
+    } else if (p.out && mbar_wait(&o_ready[g], 0, p.err, abort_flag)) {
+      // one split: O / l is the attention row, stored as f16 where the
+      // combine would put it (row bi * block + j, columns head * 128 ..),
+      // with the head's max |out| for the o-projection's limb split
+      tc_fence_after();
+      const int hq = qrow / p.block, jr = qrow - hq * p.block;
+      const int head = kvh * G + hq;
+      __half* dst = p.out + ((size_t)bi * p.block + jr) * ((size_t)p.nq * 128) + (size_t)head * 128;
+      const float inv = 1.0f / l;
+      float amax = 0.f;
+#pragma unroll 1
+      for (int cblk = 0; cblk < 4; ++cblk) {
+        uint32_t o[32];
+        tmem_ld32(o_t + cblk * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+          uint32_t h2[16];
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            h2[e / 2] = pack_f16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+            const float2 back = __half22float2(*reinterpret_cast<const __half2*>(&h2[e / 2]));
+            amax = fmaxf(amax, fmaxf(fabsf(back.x), fabsf(back.y)));
+          }
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cblk * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) d4[v] = make_uint4(h2[4 * v], h2[4 * v + 1], h2[4 * v + 2], h2[4 * v + 3]);
+        }
+      }
+      if (valid && p.omax) p.omax[(size_t)head * gridDim.z * p.block + (size_t)bi * p.block + jr] = amax;
+    } else if (!p.out && mbar_wait(&o_ready[g], 0, p.err, abort_flag)) {
       tc_fence_after();
 #pragma unroll 1
       for (int cblk = 0; cblk < 4; ++cblk) {
@@ -481,15 +498,17 @@ cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStre
   DFL_TRY(cudaGetDevice(&dev));
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const long long ctas = (long long)p.splits * p.nkv * batch;
+  AttnParams q = p;
+  q.out = p.splits == 1 ? out : nullptr;   // one split: the kernel writes the rows itself
   cudaError_t e;
   if (R > 128)
-    e = attn_tc_launch_t<2, 0>(p, batch, st);
+    e = attn_tc_launch_t<2, 0>(q, batch, st);
   else if (ctas >= 2LL * sms)
-    e = attn_tc_launch_t<1, 2>(p, batch, st);
+    e = attn_tc_launch_t<1, 2>(q, batch, st);
   else
-    e = attn_tc_launch_t<1, 0>(p, batch, st);
+    e = attn_tc_launch_t<1, 0>(q, batch, st);
   DFL_TRY(e);
-  return attn_combine_launch(p, batch, out, st);
+  return q.out ? cudaSuccess : attn_combine_launch(p, batch, out, st);
 }
 
 }  // namespace dfl

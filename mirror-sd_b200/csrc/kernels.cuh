@@ -121,6 +121,8 @@ struct AttnParams {
                         // of K/V store sequence cseq[s]
   int kv_seqs;          // nseq > 0: sequences in the K/V store (k, v hold kv_seqs * NKV planes)
   float* omax;          // combine: [NQ, b * block] max |out| per head and row (or NULL)
+  __half* out;          // tcgen05 kernel with one split: the final rows, written directly
+                        // (no partials, no combine); set by attn_tc_launch
   int* err;             // device error word for bounded waits (tcgen05 kernel), or NULL
 };
 
@@ -144,6 +146,12 @@ struct TcParams {
   int M, N, K;
   int a_cols;               // K columns per A source (tc_gemm_launch_src); K for one source
   int* err;
+  // tail split (set by the launcher): the partial last round of tiles is cut
+  // along K into `split` parts; workspace tail_part [grid][128 * 256] fp32,
+  // tail_cnt [grid] zero between launches.  NULL workspace: no split.
+  float* tail_part;
+  int* tail_cnt;
+  int split;
   // kTcFc and kTcStoreF32
   float* out_f32;           // [M, N]
   float* sumsq_part;        // kTcFc: [N/256, M] partial sums of squares per row

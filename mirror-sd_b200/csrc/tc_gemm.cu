@@ -49,6 +49,33 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 
 
 
+// Work of CTA c (grid G, T tiles): tiles c, c + G, ... of the first
+// R = T / G rounds; with a tail split S > 0 the T - R*G tiles of the last,
+// partial round are cut along K into S parts each, and CTA c < (T - R*G) * S
+// adds one part (tail tile R*G + c / S, part c % S).  A tail part writes its
+// fp32 partial accumulator to the workspace; the last part of a tile to
+// finish sums the parts in fixed order and runs the epilogue.
+struct TcItem {
+  int tile, kb0, kb1, part;   // part < 0: a whole tile
+};
+__device__ __forceinline__ TcItem tc_item(int ti, int T, int nk, int split) {
+  const int G = gridDim.x, c = blockIdx.x;
+  const int R = T / G;
+  if (split > 0 && ti == R) {
+    const int part = c % split;
+    return {R * G + c / split, part * nk / split, (part + 1) * nk / split, part};
+  }
+  return {c + ti * G, 0, nk, -1};
+}
+__device__ __forceinline__ int tc_items(int T, int split) {
+  const int G = gridDim.x, c = blockIdx.x;
+  if (split > 0) {
+    const int R = T / G;
+    return R + (c < (T - R * G) * split ? 1 : 0);
+  }
+  return T > c ? (T - c + G - 1) / G : 0;
+}
+
 // One 128-column head of this thread's accumulator row (TMEM columns tcol ..
 // tcol+127): y = acc * scale, then, when nw is given, RMSNorm over the head
 // (weight nw) and neox RoPE from the (cos, sin) table row cs; f16 store to
@@ -134,12 +161,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* acce = accf + 2;           // [2] accumulator drained by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* tail_flag = abort_flag + 1;   // this CTA's tail part is a tile's last
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = p.K / TC_BK;
   const int nmb = (p.M + TC_BM - 1) / TC_BM, nnb = p.N / TC_BN;
   const int ntiles = nmb * nnb;
-  const int my_tiles = ntiles > (int)blockIdx.x ? (ntiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  const int my_tiles = tc_items(ntiles, p.split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -169,9 +197,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < my_tiles && ok; ++ti) {
+        const TcItem w = tc_item(ti, ntiles, nk, p.split);
         int mb, nb;
-        tc_tile(blockIdx.x + ti * gridDim.x, nmb, nnb, mb, nb);
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        tc_tile(w.tile, nmb, nnb, mb, nb);
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % TC_STAGES;
           const uint32_t ph = (it / TC_STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) { ok = false; break; }
@@ -206,7 +235,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!mbar_wait(&acce[b], ((ti >> 1) & 1) ^ 1, p.err, abort_flag)) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * TC_BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const TcItem w = tc_item(ti, ntiles, nk, p.split);
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % TC_STAGES;
           const uint32_t ph = (it / TC_STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
@@ -217,7 +247,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < TC_BK / 16; ++k) {
             // advance 16 elements (32 bytes) inside the swizzle atom: +2 in 16-byte units
-            umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb | k) != 0);
+            umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != w.kb0 || k != 0));
           }
           umma_commit(&empty[s]);
         }
@@ -230,15 +260,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row_local = q * 32 + lane;
     for (int ti = 0; ti < my_tiles; ++ti) {
       const int buf = ti & 1;
+      const TcItem w = tc_item(ti, ntiles, nk, p.split);
       int mb, nb;
-      tc_tile(blockIdx.x + ti * gridDim.x, nmb, nnb, mb, nb);
+      tc_tile(w.tile, nmb, nnb, mb, nb);
       const int n0 = nb * TC_BN;
       const int row = mb * TC_BM + row_local;
       const bool row_ok = row < p.M;
       if (!mbar_wait(&accf[buf], (ti >> 1) & 1, p.err, abort_flag) || *abort_flag) break;
       tc_fence_after();
       const uint32_t tbase = tmem + buf * TC_BN + ((uint32_t)(q * 32) << 16);
-      {
+      bool run = true;
+      if (w.part >= 0) {
+        // tail part (the CTA's last item).  Once its accumulator is complete
+        // no wait of this CTA is left that could still time out, so either
+        // all four epilogue warps get here or none do: the named barriers
+        // below always fill.
+        const int slot = w.tile - (ntiles / gridDim.x) * gridDim.x;
+        float* mine = p.tail_part + ((size_t)slot * p.split + w.part) * (TC_BM * TC_BN);
+#pragma unroll 1
+        for (int ch = 0; ch < TC_BN / 32; ++ch) {
+          uint32_t r[32];
+          tmem_ld32(tbase + ch * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mine[(size_t)(ch * 32 + e) * TC_BM + row_local] = __uint_as_float(r[e]);
+        }
+        __threadfence();
+        named_bar_sync(2, 128);
+        if (threadIdx.x == 64) *tail_flag = atomicAdd(p.tail_cnt + slot, 1) == p.split - 1;
+        named_bar_sync(2, 128);
+        run = *tail_flag != 0;
+        if (run) {
+          // the last part: sum the parts in fixed order into the accumulator
+          __threadfence();
+          if (threadIdx.x == 64) p.tail_cnt[slot] = 0;
+          const float* base = p.tail_part + (size_t)slot * p.split * (TC_BM * TC_BN);
+#pragma unroll 1
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            // 32 independent loads per part, so they are all in flight at once
+            const float* col = base + (size_t)(ch * 32) * TC_BM + row_local;
+            float a[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) a[e] = __ldcg(col + (size_t)e * TC_BM);
+            for (int q2 = 1; q2 < p.split; ++q2) {
+              const float* cq = col + (size_t)q2 * (TC_BM * TC_BN);
+              float v[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) v[e] = __ldcg(cq + (size_t)e * TC_BM);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) a[e] += v[e];
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(a[e]);
+            tmem_st32(tbase + ch * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      if (run) {
         if (MODE == kTcFc || MODE == kTcStoreF32) {
           float ss = 0.f;
 #pragma unroll 1
@@ -426,9 +506,20 @@ static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inn
   return r == CUDA_SUCCESS;
 }
 
+// parts per tail tile: the tail round's tiles spread over the grid, each part
+// at least 4 k-blocks; 0 (no split) when the tiles fill whole rounds or a part
+// would be too short to pay for its partial write
+int tc_tail_split(int tiles, int grid, int nk, bool have_workspace) {
+  if (!have_workspace || grid < 1) return 0;
+  const int tail = tiles - (tiles / grid) * grid;
+  if (tail == 0) return 0;
+  int s = grid / tail;
+  if (s > nk / 4) s = nk / 4;
+  return s >= 2 ? s : 0;
+}
+
 template <int FMT, int MODE, int NSRC>
-static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, const TcParams& p,
-                               cudaStream_t st) {
+static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, TcParams p, cudaStream_t st) {
   auto kern = tc_gemm_kernel<FMT, MODE, NSRC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
   if (e != cudaSuccess) return e;
@@ -436,8 +527,10 @@ static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, c
   DFL_TRY(cudaGetDevice(&dev));
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
+  const int grid = tiles < sms ? tiles : sms;
+  p.split = tc_tail_split(tiles, grid, p.K / TC_BK, p.tail_part != nullptr && p.tail_cnt != nullptr);
   DFL_TRY(max_smem_carveout(kern));
-  return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
+  return launch_pdl(kern, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
 }
 
 template <int NSRC>

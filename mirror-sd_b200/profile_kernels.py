@@ -13,6 +13,8 @@ Cases (27B-class draft dims, 32 block rows):
   lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
   attn     block attention            40/8 heads, 32 queries, kv 4128
   attn16   the same at batch 16, kv 32800 (2.1 GB of K/V)
+  attn_c5  the batched serving shape: 256 sequences, 32 q / 8 kv heads, 16
+           queries, kv 1104 (a sink 64 / window 1024 cache plus the block)
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
   attn_sweep  block attention, 40/8 heads, 32 queries, ctx 1K..32K, batch 1 and 16
               (prints a markdown table: time, bandwidth, fraction of measured HBM)
@@ -106,14 +108,15 @@ def main():
         ws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.lm_head_argmax(hn, E, workspace=ws)
         nbytes, flops = V * H * 2, 2 * (M - 1) * V * H
-    elif a.case in ("attn", "attn16"):
-        bsz, L = (1, 4128) if a.case == "attn" else (16, 32800)
-        qq = torch.randn(bsz, 40, M, 128, generator=g, device=dev).to(torch.float16)
+    elif a.case in ("attn", "attn16", "attn_c5"):
+        bsz, L, nq, Mq = {"attn": (1, 4128, 40, M), "attn16": (16, 32800, 40, M),
+                          "attn_c5": (256, 1104, 32, 16)}[a.case]
+        qq = torch.randn(bsz, nq, Mq, 128, generator=g, device=dev).to(torch.float16)
         kk = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
         vv = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
-        ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+        ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.attention(qq, kk, vv, workspace=ws)
-        nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * 40 * M * L * 128
+        nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * nq * Mq * L * 128
     elif a.case == "serve":
         pkg = importlib.import_module("mirror-sd_b200")
         cfg = pkg.DFlashConfig(hidden_size=4096, num_hidden_layers=5, intermediate_size=12288,

@@ -55,7 +55,10 @@ def test_w8_linear_vs_fp32(K, M, N, Kd):
 
 @pytest.mark.parametrize("M,N,Kd,bf16", [(128, 256, 64, True), (200, 512, 1024, True),
                                          (64, 256, 256, False), (300, 768, 512, False),
-                                         (1000, 256, 25600, True)])
+                                         (1000, 256, 25600, True),
+                                         # more tiles than SMs: the partial last round is split
+                                         # along K (12 tiles x 8 parts; 4 tiles x 16 parts)
+                                         (1280, 4096, 2048, True), (1000, 4864, 4096, False)])
 def test_tc_gemm_vs_fp32(K, M, N, Kd, bf16):
     dt = torch.bfloat16 if bf16 else torch.float16
     g = torch.Generator().manual_seed(M + N + Kd)
