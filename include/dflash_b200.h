@@ -128,7 +128,8 @@ typedef struct DFlashForwardArgs {
   /* Optional phase timing: when n_phase_events >= DFLASH_PHASES, event k
    * (a cudaEvent_t) is recorded on `stream` at phase boundary k:
    * 0 start, 1 after RoPE table + residual init, 2 after the fc GEMM,
-   * 3 after hidden_norm, 4 after the context K/V GEMM, 5 after the decoder
+   * 3 after hidden_norm (fused into the two GEMMs: recorded with 2),
+   * 4 after the context K/V GEMM, 5 after the decoder
    * layers, 6 after the final norm, 7 after lm_head + argmax (+ accept). */
   void* const* phase_events;
   int32_t n_phase_events;

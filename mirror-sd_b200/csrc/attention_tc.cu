@@ -195,6 +195,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
     cp_async_wait<0>();
     fence_proxy_async_smem();
     mbar_arrive(q_ready);
+
     const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
     const __half* kg = p.k + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
     const __half* vg = p.v + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;

@@ -89,7 +89,6 @@ struct Handle {
   // workspace
   float2* rope = nullptr;
   float *h = nullptr, *hstat = nullptr;
-  float* ctx_raw = nullptr;          // fc output, fp32 (hidden_norm input)
   float* ctx_part = nullptr;
   __half* ctx_n = nullptr;
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
@@ -347,7 +346,6 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->h, (size_t)Mx * H));
   CKC(A.alloc(&hd->hstat, (size_t)(H / 128) * Mx));
   if (Cx > 0) {
-    CKC(A.alloc(&hd->ctx_raw, (size_t)Cx * H));
     CKC(A.alloc(&hd->ctx_part, (size_t)(H / 256) * Cx));
     CKC(A.alloc(&hd->ctx_n, (size_t)Cx * H));
   }
@@ -602,11 +600,12 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     TcParams fp{};
     fp.tail_part = hd->tc_part; fp.tail_cnt = hd->tc_cnt;
     fp.M = Ctot; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
-    fp.out_f32 = hd->ctx_raw; fp.sumsq_part = hd->ctx_part;
+    // hidden_norm (dflash.py:392) is split over the two GEMMs: the fc epilogue
+    // stores f16(fc * w) with per-row sums of squares, and the context K|V
+    // GEMM scales each row by its 1/rms
+    fp.out_h16 = hd->ctx_n; fp.colw = hd->hidden_norm; fp.sumsq_part = hd->ctx_part;
     CK(tc_gemm_launch_src(fc_src, hd->fc, true, kTcFc, fp, st));
     CK(mark(2));
-    CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, Ctot, H, hd->hidden_norm, d.rms_norm_eps,
-                       hd->ctx_n, st));
     CK(mark(3));
     TcParams kp{};
     kp.tail_part = hd->tc_part; kp.tail_cnt = hd->tc_cnt;
@@ -614,9 +613,10 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     kp.scale = hd->s_kv_ctx; kp.k_norm = hd->k_norm_all; kp.rope = hd->rope;
     kp.k_out = Kbase; kp.v_out = Vbase; kp.layer_stride = layer_stride;
     kp.nkv = NKV; kp.eps = d.rms_norm_eps; kp.kv = m;
+    kp.row_sumsq = hd->ctx_part; kp.row_parts = H / 256; kp.row_dim = H;
     CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, false, kTcCtxKV, kp, st));
     CK(mark(4));
-    launches += 3;
+    launches += 2;   // fc (+ hidden_norm's f16 half), context K|V (+ its 1/rms)
   } else {
     CK(mark(2));
     CK(mark(3));

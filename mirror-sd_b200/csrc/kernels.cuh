@@ -155,6 +155,14 @@ struct TcParams {
   // kTcFc and kTcStoreF32
   float* out_f32;           // [M, N]
   float* sumsq_part;        // kTcFc: [N/256, M] partial sums of squares per row
+  // kTcFc with out_h16: f16(acc * colw[col]) instead of the fp32 store (the
+  // fc output times the hidden_norm weight; the row's 1/rms is applied by the
+  // GEMM that reads it, kTcCtxKV with row_sumsq)
+  __half* out_h16;
+  const float* colw;
+  // kTcCtxKV: when set, rows are scaled by rsqrt(sum_q row_sumsq[q, row] / row_dim + eps)
+  const float* row_sumsq;   // [row_parts, M]
+  int row_parts, row_dim;
   // kTcCtxKV
   const float* scale;       // [N]
   const float* k_norm;      // [L, 128]

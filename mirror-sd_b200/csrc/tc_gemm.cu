@@ -83,7 +83,7 @@ __device__ __forceinline__ int tc_items(int T, int split) {
 // with row_ok store.
 __device__ __forceinline__ void tc_store_head(uint32_t tcol, const float* __restrict__ sc,
                                               const float* __restrict__ nw, const float2* __restrict__ cs,
-                                              float eps, __half* dst, bool row_ok) {
+                                              float eps, __half* dst, bool row_ok, float rowscale = 1.f) {
   float rstd = 1.f;
   if (nw) {
     float ss = 0.f;
@@ -94,7 +94,7 @@ __device__ __forceinline__ void tc_store_head(uint32_t tcol, const float* __rest
       tmem_ld_wait();
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e);
+        const float y = __uint_as_float(r[e]) * __ldg(sc + ch * 32 + e) * rowscale;
         ss += y * y;
       }
     }
@@ -114,8 +114,8 @@ __device__ __forceinline__ void tc_store_head(uint32_t tcol, const float* __rest
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           const int d = half * 32 + e + t;
-          float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d);
-          float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64);
+          float y1 = __uint_as_float(r1[e + t]) * __ldg(sc + d) * rowscale;
+          float y2 = __uint_as_float(r2[e + t]) * __ldg(sc + d + 64) * rowscale;
           if (nw) {
             y1 = y1 * rstd * __ldg(nw + d);
             y2 = y2 * rstd * __ldg(nw + d + 64);
@@ -319,7 +319,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       if (run) {
-        if (MODE == kTcFc || MODE == kTcStoreF32) {
+        if (MODE == kTcFc && p.out_h16) {
+          // hidden_norm fused: f16(fc * w) here, 1/rms per row in the context K|V GEMM
+          float ss = 0.f;
+#pragma unroll 1
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tbase + ch * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              const float* w = p.colw + n0 + ch * 32;
+              uint32_t o[16];
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                const float a = __uint_as_float(r[e]), b = __uint_as_float(r[e + 1]);
+                ss += a * a + b * b;
+                o[e / 2] = pack_f16x2(a * __ldg(w + e), b * __ldg(w + e + 1));
+              }
+              uint4* dst = reinterpret_cast<uint4*>(p.out_h16 + (size_t)row * p.N + n0 + ch * 32);
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+            }
+          }
+          if (row_ok) p.sumsq_part[(size_t)nb * p.M + row] = ss;
+        } else if (MODE == kTcFc || MODE == kTcStoreF32) {
           float ss = 0.f;
 #pragma unroll 1
           for (int ch = 0; ch < TC_BN / 32; ++ch) {
@@ -345,6 +368,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const KvSeq sq = p.kv.seq[bi];
           const int slot = kv_slot(p.kv, sq.n0 + crow - sq.ctx_start, sq.rs_pre);
           const int per_layer = 2 * p.nkv * 128;
+          float rowscale = 1.f;   // hidden_norm's 1/rms of this context row
+          if (p.row_sumsq) {
+            float ssr = 0.f;
+            for (int q3 = 0; q3 < p.row_parts; ++q3) ssr += __ldg(p.row_sumsq + (size_t)q3 * p.M + crow);
+            rowscale = rsqrtf(ssr / static_cast<float>(p.row_dim) + p.eps);
+          }
 #pragma unroll 1
           for (int hh = 0; hh < 2; ++hh) {
             const int col0 = n0 + hh * 128;
@@ -355,7 +384,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             __half* dst = (is_v ? p.v_out : p.k_out) + (size_t)layer * p.layer_stride +
                           (((size_t)sq.cseq * p.nkv + kvh) * p.kv.slots + slot) * 128;
             tc_store_head(tbase + hh * 128, p.scale + col0, is_v ? nullptr : p.k_norm + layer * 128,
-                          p.rope + (size_t)crow * 64, p.eps, dst, row_ok);
+                          p.rope + (size_t)crow * 64, p.eps, dst, row_ok, rowscale);
           }
         } else if (MODE == kTcBlkQKV) {  // block rows: q | k | v heads, two per tile
           const int m = row_ok ? row : 0;
