@@ -48,8 +48,14 @@ constexpr float TA_RESCALE = 8.0f;         // log2 of the largest P before O is 
 
 // NS_ 0: the deepest K/V ring shared memory allows (one CTA per SM); 2: a
 // double buffer small enough for two CTAs per SM, for grids with many CTAs
-// per SM (many sequences), where the second CTA hides the per-tile latency
-template <int NG, int NS_ = 0>
+// per SM (many sequences), where the second CTA hides the per-tile latency.
+// HALVES 2 (one group of at most 64 query rows): the group's rows are loaded
+// twice, as MMA rows 0-63 and 64-127, and the softmax warps of the upper copy
+// take kv columns 32-63 of every tile while the lower copy takes columns
+// 0-31, each with its own running max and sum (P is zero in the other
+// half's columns); the two halves are merged once at the end.  All four
+// softmax warps work instead of two, on half the columns each.
+template <int NG, int NS_ = 0, int HALVES = 1>
 struct TaCfg {
   static constexpr int NS = NS_ ? NS_ : (NG == 1 ? 6 : 5);  // K/V stages
   // registers per thread: two CTAs of THREADS threads must fit in 64K
@@ -120,12 +126,13 @@ __device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
   return y;
 }
 
-template <int NG, int NS_>
-__global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG, NS_>::MAX_REGS))
+template <int NG, int NS_, int HALVES>
+__global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((TaCfg<NG, NS_, HALVES>::MAX_REGS))
     attn_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                    const AttnParams p) {
-  using C = TaCfg<NG, NS_>;
+  using C = TaCfg<NG, NS_, HALVES>;
   constexpr int TA_NS = C::NS;
+  static_assert(HALVES == 1 || NG == 1, "column halves need a single query group");
   griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
@@ -159,8 +166,9 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
     }
     for (int g = 0; g < NG; ++g) {
       // softmax threads of group g: its warps holding at least one real row
+      // (with halves: rows 0-63 twice)
       const int rows = min(128, R - g * 128);
-      const int nthr = 32 * ((rows + 31) / 32);
+      const int nthr = HALVES == 2 ? 64 * ((rows + 31) / 32) : 32 * ((rows + 31) / 32);
       for (int b = 0; b < 2; ++b) {
         mbar_init(&s_ready[2 * g + b], 1);
         mbar_init(&p_ready[2 * g + b], nthr);
@@ -189,7 +197,8 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
       const int r = idx >> 4, c = idx & 15;  // 16-byte piece c of the 256-byte row r
       const int g = r >> 7, rr = r & 127, ch = c >> 3, cc = c & 7;
       uint8_t* dst = smem + C::Q_OFF + g * TA_QG + ch * (128 * 128) + rr * 128 + ((cc ^ (rr & 7)) << 4);
-      cp_async16_zfill(smem_u32(dst), qg + (size_t)min(r, R - 1) * 128 + c * 8, r < R);
+      const int src = HALVES == 2 ? (r & 63) : r;   // halves: MMA rows 64-127 repeat rows 0-63
+      cp_async16_zfill(smem_u32(dst), qg + (size_t)min(src, R - 1) * 128 + c * 8, src < R);
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -295,12 +304,18 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
       }
     }
   } else {
-    // ---- softmax: thread = query row g * 128 + r (TMEM lane r of group g)
+    // ---- softmax: thread = TMEM lane r of group g.  Without halves it owns
+    // query row g * 128 + r; with halves, lanes r and r + 64 own row r & 63,
+    // lanes below 64 taking kv columns 0-31 of every tile and the others 32-63
     const int g = warp >> 2;
     const int r = 32 * (warp & 3) + lane;
-    const int qrow = g * 128 + r;
+    constexpr int CW = TA_TK / HALVES;  // kv columns per thread and tile
+    const int half = HALVES == 2 ? (r >> 6) : 0;
+    const int coff = half * CW;
+    const int qrow = HALVES == 2 ? (r & 63) : g * 128 + r;
     const bool valid = qrow < R;
-    const bool active = g * 128 + 32 * (warp & 3) < R;  // the warp holds a real row
+    // the warp holds a real row
+    const bool active = (HALVES == 2 ? ((32 * (warp & 3)) & 63) : g * 128 + 32 * (warp & 3)) < R;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t o_t = tmem + C::O_COL + g * 128 + lane_off;
     const float c = p.scale_log2;
@@ -310,9 +325,15 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
       const int b = j & 1;
       if (!mbar_wait(&s_ready[2 * g + b], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sv[TA_TK];
+      uint32_t sv[CW];
       const uint32_t s_t = tmem + C::S_COL + (2 * g + b) * TA_TK + lane_off;
-      {
+      if (HALVES == 2) {
+        uint32_t a[32];
+        tmem_ld32(s_t + coff, a);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < CW; ++e) sv[e] = a[e];
+      } else {
         uint32_t a[32], bb[32];
         tmem_ld32(s_t, a);
         tmem_ld32(s_t + 32, bb);
@@ -320,17 +341,18 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           sv[e] = a[e];
-          sv[32 + e] = bb[e];
+          sv[(32 + e) % CW] = bb[e];
         }
       }
-      const int nvalid = kv1 - (kv0 + j * TA_TK);  // >= 1
+      // valid columns in this thread's range (can be <= 0 for the upper half of a short tile)
+      const int nvalid = kv1 - (kv0 + j * TA_TK) - coff;
       float mx = -INFINITY;
-      if (nvalid >= TA_TK) {
+      if (nvalid >= CW) {
 #pragma unroll
-        for (int e = 0; e < TA_TK; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+        for (int e = 0; e < CW; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
       } else {
 #pragma unroll
-        for (int e = 0; e < TA_TK; ++e)
+        for (int e = 0; e < CW; ++e)
           if (e < nvalid) mx = fmaxf(mx, __uint_as_float(sv[e]));
       }
       // scores in base-2 units: s * c with c = log2(e) / sqrt(128) > 0, so the
@@ -357,16 +379,20 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
       }
       m_used = m_new;
       // P = 2^(s c - m) two at a time in f16 (the MMA consumes f16 P anyway);
-      // masked columns get -inf, hence 0.  The row sum adds f16 pairs in
-      // groups of 8 (at most 8 * 256, exact to 2^-10) and then in fp32.
-      uint32_t pk[TA_TK / 2];
+      // masked columns get -inf, hence 0, and with halves the other half's
+      // columns are 0.  The row sum adds f16 pairs in groups of 8 (at most
+      // 8 * 256, exact to 2^-10) and then in fp32.
+      uint32_t own[CW / 2];
       const float neg_m = -m_used;
 #pragma unroll
-      for (int e = 0; e < TA_TK; e += 2) {
+      for (int e = 0; e < CW; e += 2) {
         const float x0 = e < nvalid ? fmaf(__uint_as_float(sv[e]), c, neg_m) : -INFINITY;
         const float x1 = e + 1 < nvalid ? fmaf(__uint_as_float(sv[e + 1]), c, neg_m) : -INFINITY;
-        pk[e / 2] = ex2_f16x2(x0, x1);
+        own[e / 2] = ex2_f16x2(x0, x1);
       }
+      uint32_t pk[TA_TK / 2];
+#pragma unroll
+      for (int i = 0; i < TA_TK / 2; ++i) pk[i] = (i / (CW / 2) == half) ? own[i % (CW / 2)] : 0u;
 #pragma unroll
       for (int q = 0; q < TA_TK / 2; q += 4) {
         const uint32_t s4 = hadd2_u(hadd2_u(pk[q], pk[q + 1]), hadd2_u(pk[q + 2], pk[q + 3]));
@@ -379,6 +405,84 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
       tc_fence_before();
       mbar_arrive(&p_ready[2 * g + b]);
     }
+    if (HALVES == 2) {
+      // merge the halves: the upper copy hands (O, m, l) to the lower one
+      // through shared memory (the K/V stages: every MMA that read them has
+      // completed once O is final), laid out [column][row] for the banks
+      float* xo = reinterpret_cast<float*>(smem + C::KV_OFF);
+      float* xm = xo + 128 * 64;
+      float* xl = xm + 64;
+      const bool have = __all_sync(0xffffffffu, active && ntiles > 0 && ok &&
+                                                    mbar_wait(&o_ready[g], 0, p.err, abort_flag));
+      if (have) tc_fence_after();
+      if (half == 1 && active) {
+#pragma unroll 1
+        for (int cblk = 0; cblk < 4; ++cblk) {
+          uint32_t o[32];
+          if (have) {
+            tmem_ld32(o_t + cblk * 32, o);
+            tmem_ld_wait();
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) xo[(cblk * 32 + e) * 64 + qrow] = have ? __uint_as_float(o[e]) : 0.f;
+        }
+        xm[qrow] = have ? m_used : -INFINITY;
+        xl[qrow] = have ? l : 0.f;
+      }
+      named_bar_sync(3, 128);
+      if (half == 0 && active) {
+        const float ma = have ? m_used : -INFINITY, mb = xm[qrow];
+        const float mm = fmaxf(ma, mb);
+        const float wa = ma == -INFINITY ? 0.f : exp2f(ma - mm);
+        const float wb = mb == -INFINITY ? 0.f : exp2f(mb - mm);
+        const float lsum = (have ? l : 0.f) * wa + xl[qrow] * wb;
+        const int hq = qrow / p.block, jr = qrow - hq * p.block;
+        const int head = kvh * G + hq;
+        __half* dst = p.out ? p.out + ((size_t)bi * p.block + jr) * ((size_t)p.nq * 128) + (size_t)head * 128
+                            : nullptr;
+        float* orow = p.opart + (pbase + (valid ? qrow : 0)) * 128;
+        const float inv = lsum > 0.f ? 1.0f / lsum : 0.f;
+        float amax = 0.f;
+#pragma unroll 1
+        for (int cblk = 0; cblk < 4; ++cblk) {
+          uint32_t o[32];
+          if (have) {
+            tmem_ld32(o_t + cblk * 32, o);
+            tmem_ld_wait();
+          }
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            v[e] = (have ? __uint_as_float(o[e]) * wa : 0.f) + xo[(cblk * 32 + e) * 64 + qrow] * wb;
+          if (!valid) continue;
+          if (dst) {
+            uint32_t h2[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              h2[e / 2] = pack_f16x2(v[e] * inv, v[e + 1] * inv);
+              const float2 back = __half22float2(*reinterpret_cast<const __half2*>(&h2[e / 2]));
+              amax = fmaxf(amax, fmaxf(fabsf(back.x), fabsf(back.y)));
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst + cblk * 32);
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4)
+              d4[w4] = make_uint4(h2[4 * w4], h2[4 * w4 + 1], h2[4 * w4 + 2], h2[4 * w4 + 3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              *reinterpret_cast<float4*>(orow + cblk * 32 + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+          }
+        }
+        if (valid) {
+          if (dst) {
+            if (p.omax) p.omax[(size_t)head * gridDim.z * p.block + (size_t)bi * p.block + jr] = amax;
+          } else {
+            p.mpart[pbase + qrow] = mm;
+            p.lpart[pbase + qrow] = lsum;
+          }
+        }
+      }
+    } else {
     float* orow = p.opart + (pbase + (valid ? qrow : 0)) * 128;
     if (!active) {
       // padding rows only: nothing to write
@@ -442,6 +546,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_>::THREADS) __maxnreg__((TaCfg<NG
         p.lpart[pbase + qrow] = l;
       }
     }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -477,10 +582,10 @@ static bool map_kv(CUtensorMap* m, const void* base, uint64_t slots, uint64_t pl
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int NG, int NS_>
+template <int NG, int NS_, int HALVES>
 static cudaError_t attn_tc_launch_t(const AttnParams& p, int batch, cudaStream_t st) {
-  using C = TaCfg<NG, NS_>;
-  auto kern = attn_tc_kernel<NG, NS_>;
+  using C = TaCfg<NG, NS_, HALVES>;
+  auto kern = attn_tc_kernel<NG, NS_, HALVES>;
   CUtensorMap mk, mv;
   const uint64_t planes = (uint64_t)(p.kv.nseq > 0 ? p.kv_seqs : batch) * p.nkv;
   if (planes < (uint64_t)batch * p.nkv || !map_kv(&mk, p.k, p.kv_cap, planes) || !map_kv(&mv, p.v, p.kv_cap, planes))
@@ -501,13 +606,14 @@ cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStre
   const long long ctas = (long long)p.splits * p.nkv * batch;
   AttnParams q = p;
   q.out = p.splits == 1 ? out : nullptr;   // one split: the kernel writes the rows itself
+  const bool many = ctas >= 2LL * sms;   // two CTAs per SM pay off
   cudaError_t e;
   if (R > 128)
-    e = attn_tc_launch_t<2, 0>(q, batch, st);
-  else if (ctas >= 2LL * sms)
-    e = attn_tc_launch_t<1, 2>(q, batch, st);
+    e = attn_tc_launch_t<2, 0, 1>(q, batch, st);
+  else if (R <= 64)
+    e = many ? attn_tc_launch_t<1, 2, 2>(q, batch, st) : attn_tc_launch_t<1, 0, 2>(q, batch, st);
   else
-    e = attn_tc_launch_t<1, 0>(q, batch, st);
+    e = many ? attn_tc_launch_t<1, 2, 1>(q, batch, st) : attn_tc_launch_t<1, 0, 1>(q, batch, st);
   DFL_TRY(e);
   return q.out ? cudaSuccess : attn_combine_launch(p, batch, out, st);
 }

@@ -81,7 +81,11 @@ def _attn_ref(q, k, v, G):
 
 
 @pytest.mark.parametrize("b,nq,nkv,B,L", [(1, 40, 8, 32, 96), (1, 32, 8, 16, 2064), (2, 4, 2, 8, 20),
-                                          (1, 40, 8, 32, 4128), (3, 8, 1, 16, 700)])
+                                          (1, 40, 8, 32, 4128), (3, 8, 1, 16, 700),
+                                          # many (sequence, head) CTAs: two per SM, column halves
+                                          (80, 32, 8, 16, 300), (40, 16, 8, 8, 1111),
+                                          # 64 < query rows <= 128 with many CTAs
+                                          (60, 40, 8, 16, 257)])
 def test_attention_vs_fp32(K, b, nq, nkv, B, L):
     g = torch.Generator().manual_seed(b * 1000 + L)
     q = torch.randn(b, nq, B, 128, generator=g).to(torch.float16)
