@@ -368,7 +368,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->hn, (size_t)Mx * H));
   hd->dense = Mx > kW8Rows;
   // lm_head argmax partials: one per CTA (W8 path) or per 256-entry vocabulary block (dense path)
-  const size_t lm_parts = std::max<size_t>(hd->num_sms, hd->dense ? (d.vocab_size + 255) / 256 : 0);
+  const size_t lm_parts = std::max<size_t>(hd->num_sms, (d.vocab_size + 255) / 256);
   CKC(A.alloc(&hd->lm_val, lm_parts * Mx));
   CKC(A.alloc(&hd->lm_idx, lm_parts * Mx));
   if (hd->dense) CKC(A.alloc(&hd->xa, (size_t)Mx * H));
@@ -572,6 +572,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   const int M = b * B;
   const int G = NQ / NKV;
   const bool dense = M > kW8Rows;
+  const bool lm_dense = dense;   // the lm_head as a dense tcgen05 GEMM above kW8Rows rows
   if (dense && !hd->dense) return fail(DFLASH_ERR_INVALID, "%d block rows above %d", M, kW8Rows);
   const bool timing = a->phase_events && a->n_phase_events >= DFLASH_PHASES;
   auto mark = [&](int k) -> cudaError_t {
@@ -722,7 +723,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   CK(mark(5));
   // dense path: the lm_head reads only rows 1..B-1 of every block, packed
   CK(final_norm_launch(hd->h, hd->hstat, hparts, M, H, hd->norm, d.rms_norm_eps, hd->hn,
-                       a->out_hidden, a->out_hidden_fp32 != 0, st, B, dense ? 1 : 0));
+                       a->out_hidden, a->out_hidden_fp32 != 0, st, B, lm_dense ? 1 : 0));
   launches += 1;
   CK(mark(6));
   if (a->out_tokens || a->target_tokens) {
@@ -730,7 +731,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     lp.hn = hd->hn; lp.V = d.vocab_size; lp.H = H; lp.M = M;
     lp.best_val = hd->lm_val; lp.best_idx = hd->lm_idx;
     int grid = 0;
-    if (dense) {
+    if (lm_dense) {
       TcParams tp{};
     tp.tail_part = hd->tc_part; tp.tail_cnt = hd->tc_cnt;
       tp.M = b * (B - 1); tp.N = (d.vocab_size + 255) / 256 * 256; tp.K = H; tp.err = hd->dev_err;
@@ -740,8 +741,8 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     } else {
       CK(lm_argmax_launch(lp, hd->lm_tiles, hd->num_sms, hd->dev_err, &grid, st));
     }
-    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, dense ? b * (B - 1) : M, B, b, a->out_tokens,
-                            a->target_tokens, a->acc_len, a->correction, st, dense ? 1 : 0));
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, grid, lm_dense ? b * (B - 1) : M, B, b, a->out_tokens,
+                            a->target_tokens, a->acc_len, a->correction, st, lm_dense ? 1 : 0));
     launches += 2;
   }
   CK(mark(7));

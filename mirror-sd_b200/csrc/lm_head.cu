@@ -35,14 +35,20 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 // tcgen05.mma M=128 (vocab) x N=MP (block rows) x K=16 into one of two TMEM
 // accumulators; warps 2..5 take the argmax of the other accumulator while
 // the next tile streams in.
-constexpr int LT_NS = 6;
 constexpr int LT_THREADS = 192;
 constexpr int LT_E_BYTES = 128 * 128;
+// ring depth: as many stages as about 210 KB of shared memory holds, so one
+// CTA keeps enough bytes in flight to draw its share of HBM bandwidth
+template <int MP>
+struct LtCfg {
+  static constexpr int STAGE = LT_E_BYTES + MP * 128;
+  static constexpr int NS = (210 * 1024) / STAGE < 12 ? (210 * 1024) / STAGE : 12;
+};
 
 template <int MP>
 __global__ void __launch_bounds__(LT_THREADS, 1)
     lm_tc_kernel(const __grid_constant__ CUtensorMap map_h, const LmParams p, const uint8_t* e_tiles,
-                 int tiles_per_cta, int* err) {
+                 int vt_total, int* err) {
   griddep_wait();
   griddep_launch_dependents();
   constexpr int H_BYTES = MP * 128;
@@ -52,6 +58,7 @@ __global__ void __launch_bounds__(LT_THREADS, 1)
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int LT_NS = LtCfg<MP>::NS;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + LT_NS * STAGE);
   uint64_t* empty = full + LT_NS;
   uint64_t* acc_full = empty + LT_NS;   // [2]
@@ -64,8 +71,9 @@ __global__ void __launch_bounds__(LT_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int VT = (p.V + 127) / 128;
   const int nkb = p.H / 64;
-  const int t0 = blockIdx.x * tiles_per_cta;
-  const int t1 = min(VT, t0 + tiles_per_cta);
+  // balanced contiguous ranges: every CTA owns floor or ceil(VT / grid) tiles
+  const int t0 = (int)(((long long)blockIdx.x * vt_total) / gridDim.x);
+  const int t1 = min(VT, (int)(((long long)(blockIdx.x + 1) * vt_total) / gridDim.x));
   const int ntile = max(0, t1 - t0);
 
   if (threadIdx.x == 0) {
@@ -296,6 +304,9 @@ static bool map_rows_sw128(CUtensorMap* m, const void* base, uint64_t K, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// CTAs: as few as keep the per-CTA tile count at ceil(VT / SMs) (132 of 148
+// SMs for the 1187 tiles of a 151936 vocabulary; measured faster than
+// spreading 8-9 tiles over all 148 SMs at both 4096 and 5120 hidden)
 int lm_grid(int V, int num_sms) {
   const int VT = (V + 127) / 128;
   const int per = (VT + num_sms - 1) / num_sms;
@@ -304,12 +315,12 @@ int lm_grid(int V, int num_sms) {
 
 template <int MP>
 static cudaError_t lm_tc_t(const CUtensorMap& mh, const LmParams& p, const uint8_t* et, int grid,
-                           int per, int* err, cudaStream_t st) {
-  const size_t smem = (size_t)LT_NS * (LT_E_BYTES + MP * 128) + 1024 + 256 + 8 * 64 * 4;
+                           int vt_total, int* err, cudaStream_t st) {
+  const size_t smem = (size_t)LtCfg<MP>::NS * LtCfg<MP>::STAGE + 1024 + 256 + 8 * 64 * 4;
   cudaError_t e = cudaFuncSetAttribute(lm_tc_kernel<MP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   DFL_TRY(max_smem_carveout(lm_tc_kernel<MP>));
-  return launch_pdl(lm_tc_kernel<MP>, dim3(grid), dim3(LT_THREADS), smem, st, mh, p, et, per, err);
+  return launch_pdl(lm_tc_kernel<MP>, dim3(grid), dim3(LT_THREADS), smem, st, mh, p, et, vt_total, err);
 }
 
 // returns the grid used (partials written for that many CTAs) via *grid_out
@@ -318,15 +329,14 @@ cudaError_t lm_argmax_launch(const LmParams& p, const uint8_t* e_tiles, int num_
   if (p.H % 64 || p.M < 1 || p.M > 64 || p.V < 1) return cudaErrorInvalidValue;
   const int VT = (p.V + 127) / 128;
   const int grid = lm_grid(p.V, num_sms);
-  const int per = (VT + grid - 1) / grid;
   *grid_out = grid;
   const int mp = (p.M + 15) / 16 * 16;
   CUtensorMap mh;
   if (!map_rows_sw128(&mh, p.hn, p.H, p.M, mp)) return cudaErrorInvalidValue;
-  if (mp == 16) return lm_tc_t<16>(mh, p, e_tiles, grid, per, err, st);
-  if (mp == 32) return lm_tc_t<32>(mh, p, e_tiles, grid, per, err, st);
-  if (mp == 48) return lm_tc_t<48>(mh, p, e_tiles, grid, per, err, st);
-  return lm_tc_t<64>(mh, p, e_tiles, grid, per, err, st);
+  if (mp == 16) return lm_tc_t<16>(mh, p, e_tiles, grid, VT, err, st);
+  if (mp == 32) return lm_tc_t<32>(mh, p, e_tiles, grid, VT, err, st);
+  if (mp == 48) return lm_tc_t<48>(mh, p, e_tiles, grid, VT, err, st);
+  return lm_tc_t<64>(mh, p, e_tiles, grid, VT, err, st);
 }
 
 size_t lm_pack_bytes(int V, int H) { return (size_t)((V + 127) / 128) * 128 * H * 2; }
