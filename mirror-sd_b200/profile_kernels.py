@@ -18,6 +18,9 @@ Cases (27B-class draft dims, 32 block rows):
   fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
   attn_sweep  block attention, 40/8 heads, 32 queries, ctx 1K..32K, batch 1 and 16
               (prints a markdown table: time, bandwidth, fraction of measured HBM)
+  step1    one draft step at the bench's 27B dims (block 32, ctx 4096, batch 1) with
+           one decoder layer, so the fc and context K|V GEMMs run exactly as in
+           the bench with about 4 GB on the device
   serve    one stateless draft step of --seqs sequences (default 64) of block 16,
            ctx 64 each, 8B-class dims: the dense block path (tcgen05 projections
            and lm_head over f16 weight copies); about 6 GB on the device
@@ -117,6 +120,21 @@ def main():
         ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
         fn = lambda: K.attention(qq, kk, vv, workspace=ws)
         nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * nq * Mq * L * 128
+    elif a.case == "step1":
+        pkg = importlib.import_module("mirror-sd_b200")
+        cfg = pkg.DFlashConfig(hidden_size=5120, num_hidden_layers=1, intermediate_size=17408,
+                               num_attention_heads=40, num_key_value_heads=8, head_dim=128,
+                               vocab_size=151936, block_size=32)
+        cfg.target_layer_ids = list(range(5))
+        w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+        C, B, H = 4096, 32, 5120
+        model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=1, max_ctx=C, max_block=B, device=dev)
+        noise = (torch.randn(1, B, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        th = torch.randn(1, C, 5 * H, generator=g, device=dev).to(torch.bfloat16)
+        toks = torch.empty((1, B - 1), dtype=torch.int32, device=dev)
+        fn = lambda: model.draft_step(noise, th, want_hidden=False, out_tokens=toks)
+        nbytes = C * 5 * H * 2 + H * 5 * H * 2
+        flops = 2 * C * 5 * H * H + 2 * C * H * 2 * 8 * 128
     elif a.case == "serve":
         pkg = importlib.import_module("mirror-sd_b200")
         cfg = pkg.DFlashConfig(hidden_size=4096, num_hidden_layers=5, intermediate_size=12288,
