@@ -272,11 +272,22 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
       L += p.lpart[idx] * w;
     }
     const int n = min(32, p.splits - s0);
-#pragma unroll 4
-    for (int t = 0; t < n; ++t) {
-      const float wt = __shfl_sync(0xffffffffu, w, t);
-      const float4 ov = *reinterpret_cast<const float4*>(p.opart + (base + (size_t)(s0 + t) * R) * 128 + lane * 4);
-      acc[0] += ov.x * wt; acc[1] += ov.y * wt; acc[2] += ov.z * wt; acc[3] += ov.w * wt;
+    // the partial rows of up to 16 splits are loaded before any is used, so
+    // their L2 round trips overlap (splits run to ~20 at one sequence)
+    for (int t0 = 0; t0 < n; t0 += 16) {
+      float4 ov[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        ov[t] = t0 + t < n ? __ldcg(reinterpret_cast<const float4*>(
+                                  p.opart + (base + (size_t)(s0 + t0 + t) * R) * 128 + lane * 4))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const float wt = __shfl_sync(0xffffffffu, w, (t0 + t) & 31);
+        if (t0 + t < n) {
+          acc[0] += ov[t].x * wt; acc[1] += ov[t].y * wt; acc[2] += ov[t].z * wt; acc[3] += ov[t].w * wt;
+        }
+      }
     }
   }
   L = warp_sum(L);

@@ -79,6 +79,31 @@ def test_forward_27b_dims_one_layer(pkg):
     model.close()
 
 
+@pytest.mark.parametrize("layers", [1, 2])
+def test_forward_4b_dims_c1_shape(pkg, layers):
+    """The CPU-plumbing config's dims (Qwen3-4B class: hidden 2560, 32/8
+    heads, FFN 9728, full vocab, block 16, ctx 64, batch 1) through the W8A16
+    device path; the oracle gets the exact dequantised weights."""
+    ocfg = O.OracleConfig(hidden_size=2560, num_hidden_layers=layers, intermediate_size=9728,
+                          num_attention_heads=32, num_key_value_heads=8, vocab_size=151936,
+                          block_size=16)
+    pcfg = pkg_config(pkg, ocfg)
+    w, lm = pkg.synth_weights_q8(pcfg, seed=13, random_norms=True)
+    model = pkg.DFlashDraftModel(pcfg, w, lm, max_batch=1, max_ctx=64, max_block=16)
+    noise, th = O.synth_inputs(ocfg, 1, 64, 16, seed=14)
+    hid, toks, _, _ = model.draft_step(noise.cuda(), th.cuda(), hidden_fp32=True)
+    torch.cuda.synchronize()
+    deq = lambda l, k: (l.q[k].float() * l.s[k].float()[:, None]).cpu()
+    ls = [O.OracleLayer(**{k: deq(l, k) for k in ["wq", "wk", "wv", "wo", "wg", "wu", "wd"]},
+                        in_norm=l.input_layernorm.cpu(), post_norm=l.post_attention_layernorm.cpu(),
+                        q_norm=l.q_norm.cpu(), k_norm=l.k_norm.cpu()) for l in w.layers]
+    dense = O.OracleWeights(w.fc.float().cpu(), w.hidden_norm.cpu(), w.norm.cpu(), lm.float().cpu(), ls)
+    ref = O.draft_forward(ocfg, dense, noise, th)
+    check_hidden(hid, ref)
+    check_tokens(toks, O.draft_logits(dense, ref, 16), MARGIN)
+    model.close()
+
+
 def test_forward_accept_fused(pkg):
     ocfg = tiny_cfg()
     q8, dense = O.synth_weights(ocfg, seed=21)
