@@ -173,6 +173,12 @@ int dflash_quantize_q8(const float* w, int oc, int ic, int8_t* q, uint16_t* scal
 /* Reads and clears the handle's device error word (DFLASH_ERR_DEVICE when a
  * kernel gave up on a bounded wait).  Synchronises the given stream. */
 int dflash_device_status(void* handle, void* stream);
+/* Failure-reporting self test (no reference counterpart): enqueues one
+ * bounded mbarrier wait that nothing completes, `polls` tries long.  It gives
+ * up, records the timeout in the handle's error word like any expired wait of
+ * the library, and returns; the next dflash_device_status reports
+ * DFLASH_ERR_DEVICE and clears it, and the context stays usable. */
+int dflash_probe_bounded_wait(void* handle, uint32_t polls, void* stream);
 int dflash_destroy(void* handle);
 /* Number of kernel launches the last dflash_forward on this handle issued. */
 int dflash_last_launch_count(void* handle);

@@ -73,6 +73,7 @@ EXPORTS = {
     "dflash_quantize_q8": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, c_void_p, c_void_p,
                                      c_void_p]),
     "dflash_device_status": (c_int32, [c_void_p, c_void_p]),
+    "dflash_probe_bounded_wait": (c_int32, [c_void_p, ctypes.c_uint32, c_void_p]),
     "dflash_cache_create": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_int, ctypes.POINTER(c_void_p)]),
     "dflash_cache_trim": (c_int32, [c_void_p, ctypes.c_int, ctypes.c_int]),

@@ -429,6 +429,14 @@ int dflash_device_status(void* handle, void* stream) {
   return DFLASH_OK;
 }
 
+int dflash_probe_bounded_wait(void* handle, uint32_t polls, void* stream) {
+  if (!handle) return fail(DFLASH_ERR_INVALID, "NULL handle");
+  Handle* hd = static_cast<Handle*>(handle);
+  CK(cudaSetDevice(hd->device));
+  CK(bounded_wait_probe_launch(polls, hd->dev_err, static_cast<cudaStream_t>(stream)));
+  return DFLASH_OK;
+}
+
 int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   if (!handle || !a) return fail(DFLASH_ERR_INVALID, "NULL handle or args");
   Handle* hd = static_cast<Handle*>(handle);

@@ -290,7 +290,7 @@ cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, in
                               cudaStream_t st, int block = 1, int drop_first = 0);
 cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* dst, int grp, int period,
                                    int off, cudaStream_t st);
+// one bounded mbarrier wait that nothing completes: raises kDevMbarTimeout in *err
+cudaError_t bounded_wait_probe_launch(uint32_t polls, int* err, cudaStream_t st);
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st);
-cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st);
-
 }  // namespace dfl

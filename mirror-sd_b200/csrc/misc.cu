@@ -193,6 +193,26 @@ __global__ void i8_to_f16_kernel(const int8_t* __restrict__ src, size_t n, __hal
     dst[i] = __int2half_rn(static_cast<int>(src[i]));
 }
 
+// A bounded wait that is meant to run out: one thread waits on an mbarrier
+// that nothing arrives on, for `polls` tries, then records the timeout in the
+// error word the way every bounded wait of the library does, and the kernel
+// returns.  Used to test failure reporting without faulting anything.
+__global__ void bounded_wait_probe_kernel(uint32_t polls, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    bool done = false;
+    for (uint32_t i = 0; i < polls && !done; ++i) done = mbar_try_wait(&bar, 0);
+    if (!done) atomicExch(err, kDevMbarTimeout);
+  }
+}
+
+cudaError_t bounded_wait_probe_launch(uint32_t polls, int* err, cudaStream_t st) {
+  bounded_wait_probe_kernel<<<1, 32, 0, st>>>(polls, err);
+  return cudaGetLastError();
+}
+
 // row r of int8 [rows, K] -> f16 row (r / grp) * period + off + r % grp of dst
 __global__ void i8_to_f16_rows_kernel(const int8_t* __restrict__ src, int rows, int K, __half* __restrict__ dst,
                                       int grp, int period, int off) {
@@ -202,12 +222,6 @@ __global__ void i8_to_f16_rows_kernel(const int8_t* __restrict__ src, int rows, 
     const size_t dr = (size_t)(r / grp) * period + off + r % grp;
     dst[dr * K + k] = __int2half_rn(static_cast<int>(src[i]));
   }
-}
-
-__global__ void f16_to_f32_kernel(const __half* __restrict__ src, size_t n, float* __restrict__ dst) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x)
-    dst[i] = __half2float(src[i]);
 }
 
 cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st) {
@@ -277,10 +291,6 @@ cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* ds
                                    int off, cudaStream_t st) {
   if (rows < 1 || K < 1 || grp < 1) return cudaErrorInvalidValue;
   i8_to_f16_rows_kernel<<<2048, 256, 0, st>>>(src, rows, K, dst, grp, period, off);
-  return cudaGetLastError();
-}
-cudaError_t f16_to_f32_launch(const __half* src, size_t n, float* dst, cudaStream_t st) {
-  f16_to_f32_kernel<<<256, 256, 0, st>>>(src, n, dst);
   return cudaGetLastError();
 }
 

@@ -415,6 +415,19 @@ class DFlashDraftModel:
                             max_batch or self.max_batch)
         return DFlashCache(store, sink_size, window_size)
 
+    def device_status(self) -> None:
+        """Reads and clears the handle's device error word: raises
+        RuntimeError when a bounded device-side wait gave up since the last
+        check (every mbarrier wait of the kernels is bounded)."""
+        N.check(self._lib.dflash_device_status(self._handle, self._stream()), "dflash_device_status")
+
+    def probe_bounded_wait(self, polls: int = 1 << 14) -> None:
+        """Failure-reporting self test: enqueue one bounded wait that nothing
+        completes; the next device_status() raises, and the context stays
+        usable."""
+        N.check(self._lib.dflash_probe_bounded_wait(self._handle, int(polls), self._stream()),
+                "dflash_probe_bounded_wait")
+
     def set_block_size(self, new_block: int) -> None:
         """Change the active block size (ane_model.py:611-630: ValueError
         outside [1, capacity])."""

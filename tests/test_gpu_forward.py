@@ -228,3 +228,29 @@ def test_forward_rejects_bad_shapes(pkg):
     with pytest.raises(ValueError):
         model.set_block_size(ocfg.block_size + 1)
     model.close()
+
+
+def test_bounded_wait_expiry_is_reported_and_the_context_survives(pkg):
+    """Failure detection without a fault: a bounded mbarrier wait that
+    nothing completes gives up after its poll limit, records the timeout in
+    the handle's error word (device_status raises, then reads clean), and the
+    next draft step on the same context is still correct."""
+    import time
+    ocfg = tiny_cfg()
+    q8, dense = O.synth_weights(ocfg, seed=81)
+    model = gpu_model(pkg, ocfg, q8, max_batch=1, max_ctx=16)
+    noise, th = O.synth_inputs(ocfg, 1, 16, ocfg.block_size, seed=82)
+    model.device_status()                     # clean before
+    t0 = time.time()
+    model.probe_bounded_wait(1 << 14)
+    with pytest.raises(RuntimeError, match="wait limit"):
+        model.device_status()
+    assert time.time() - t0 < 10.0
+    model.device_status()                     # cleared by the read
+    hid, toks, _, _ = model.draft_step(noise.cuda(), th.cuda(), hidden_fp32=True)
+    torch.cuda.synchronize()
+    ref = O.draft_forward(ocfg, dense, noise, th)
+    check_hidden(hid, ref)
+    check_tokens(toks, O.draft_logits(dense, ref, ocfg.block_size), MARGIN)
+    model.device_status()
+    model.close()
