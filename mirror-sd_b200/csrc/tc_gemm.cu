@@ -52,7 +52,8 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 // Work of CTA c (grid G, T tiles): tiles c, c + G, ... of the first
 // R = T / G rounds; with a tail split S > 0 the T - R*G tiles of the last,
 // partial round are cut along K into S parts each, and CTA c < (T - R*G) * S
-// adds one part (tail tile R*G + c / S, part c % S).  A tail part writes its
+// adds one part (tail tile R*G + c / S, part c % S).  With G = T * S (few
+// tiles) R is 0 and every tile is split.  A tail part writes its
 // fp32 partial accumulator to the workspace; the last part of a tile to
 // finish sums the parts in fixed order and runs the epilogue.
 struct TcItem {
@@ -556,8 +557,19 @@ static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, T
   DFL_TRY(cudaGetDevice(&dev));
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
-  const int grid = tiles < sms ? tiles : sms;
-  p.split = tc_tail_split(tiles, grid, p.K / TC_BK, p.tail_part != nullptr && p.tail_cnt != nullptr);
+  const bool ws = p.tail_part != nullptr && p.tail_cnt != nullptr;
+  int grid = tiles < sms ? tiles : sms;
+  p.split = tc_tail_split(tiles, grid, p.K / TC_BK, ws);
+  if (ws && 2 * tiles <= sms) {
+    // fewer tiles than half the SMs (a short context): every tile is cut
+    // along K, so the grid covers the SMs (all tiles are then "tail" tiles)
+    int s = sms / tiles;
+    if (s > p.K / TC_BK / 4) s = p.K / TC_BK / 4;
+    if (s >= 2) {
+      grid = tiles * s;
+      p.split = s;
+    }
+  }
   DFL_TRY(max_smem_carveout(kern));
   return launch_pdl(kern, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
 }
