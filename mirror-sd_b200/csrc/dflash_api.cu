@@ -83,14 +83,14 @@ struct Handle {
   uint8_t* lm_tiles = nullptr;      // lm_head packed by lm_pack_launch (128-row swizzled tiles)
   float *hidden_norm = nullptr, *norm = nullptr, *inv_freq = nullptr;
   float* k_norm_all = nullptr;     // [L, 128]
-  __half* w_kv_ctx = nullptr;      // [L*2*NKV*128, H] exact f16 of the int8 K|V weights
+  __nv_bfloat16* w_kv_ctx = nullptr;  // [L*2*NKV*128, H] exact bf16 of the int8 K|V weights
   float* s_kv_ctx = nullptr;       // [L*2*NKV*128]
   std::vector<Layer> layers;
   // workspace
   float2* rope = nullptr;
   float *h = nullptr, *hstat = nullptr;
   float* ctx_part = nullptr;
-  __half* ctx_n = nullptr;
+  __nv_bfloat16* ctx_n = nullptr;   // bf16(fc * hidden_norm weight): the context K|V GEMM's A
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
   int8_t* xl = nullptr;             // projection input limbs [3][64][max(H, NQ*128, I)]
   float* xs = nullptr;              // their row scales [64]
@@ -313,10 +313,10 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(cudaMemcpyAsync(ly.post_norm, lw.post_attention_layernorm, H * 4, cudaMemcpyDeviceToDevice, st));
     CKC(cudaMemcpyAsync(ly.q_norm, lw.q_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
     CKC(cudaMemcpyAsync(hd->k_norm_all + l * 128, lw.k_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
-    // context K|V operand: exact f16 of the int8 values, scales applied in the epilogue
-    __half* kv = hd->w_kv_ctx + (size_t)l * nkvc * H;
-    CKC(i8_to_f16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
-    CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
+    // context K|V operand: exact bf16 of the int8 values, scales applied in the epilogue
+    __nv_bfloat16* kv = hd->w_kv_ctx + (size_t)l * nkvc * H;
+    CKC(i8_to_bf16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
+    CKC(i8_to_bf16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
     CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 128, st));
     if ((long long)d.max_batch * d.max_block > kW8Rows) {
@@ -612,7 +612,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     // hidden_norm (dflash.py:392) is split over the two GEMMs: the fc epilogue
     // stores f16(fc * w) with per-row sums of squares, and the context K|V
     // GEMM scales each row by its 1/rms
-    fp.out_h16 = hd->ctx_n; fp.colw = hd->hidden_norm; fp.sumsq_part = hd->ctx_part;
+    fp.out_b16 = hd->ctx_n; fp.colw = hd->hidden_norm; fp.sumsq_part = hd->ctx_part;
     CK(tc_gemm_launch_src(fc_src, hd->fc, true, kTcFc, fp, st));
     CK(mark(2));
     CK(mark(3));
@@ -623,7 +623,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     kp.k_out = Kbase; kp.v_out = Vbase; kp.layer_stride = layer_stride;
     kp.nkv = NKV; kp.eps = d.rms_norm_eps; kp.kv = m;
     kp.row_sumsq = hd->ctx_part; kp.row_parts = H / 256; kp.row_dim = H;
-    CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, false, kTcCtxKV, kp, st));
+    CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, true, kTcCtxKV, kp, st));
     CK(mark(4));
     launches += 2;   // fc (+ hidden_norm's f16 half), context K|V (+ its 1/rms)
   } else {

@@ -155,10 +155,11 @@ struct TcParams {
   // kTcFc and kTcStoreF32
   float* out_f32;           // [M, N]
   float* sumsq_part;        // kTcFc: [N/256, M] partial sums of squares per row
-  // kTcFc with out_h16: f16(acc * colw[col]) instead of the fp32 store (the
-  // fc output times the hidden_norm weight; the row's 1/rms is applied by the
-  // GEMM that reads it, kTcCtxKV with row_sumsq)
-  __half* out_h16;
+  // kTcFc with out_b16: bf16(acc * colw[col]) instead of the fp32 store (the
+  // fc output times the hidden_norm weight, in the reference's activation
+  // type so an unnormalised row cannot overflow; the row's 1/rms is applied
+  // by the GEMM that reads it, kTcCtxKV with row_sumsq)
+  __nv_bfloat16* out_b16;
   const float* colw;
   // kTcCtxKV: when set, rows are scaled by rsqrt(sum_q row_sumsq[q, row] / row_dim + eps)
   const float* row_sumsq;   // [row_parts, M]
@@ -292,5 +293,6 @@ cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* ds
                                    int off, cudaStream_t st);
 // one bounded mbarrier wait that nothing completes: raises kDevMbarTimeout in *err
 cudaError_t bounded_wait_probe_launch(uint32_t polls, int* err, cudaStream_t st);
+cudaError_t i8_to_bf16_launch(const int8_t* src, size_t n, __nv_bfloat16* dst, cudaStream_t st);
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st);
 }  // namespace dfl

@@ -193,6 +193,17 @@ __global__ void i8_to_f16_kernel(const int8_t* __restrict__ src, size_t n, __hal
     dst[i] = __int2half_rn(static_cast<int>(src[i]));
 }
 
+__global__ void i8_to_bf16_kernel(const int8_t* __restrict__ src, size_t n, __nv_bfloat16* __restrict__ dst) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __float2bfloat16_rn(static_cast<float>(src[i]));   // |q| <= 127: exact in bf16
+}
+
+cudaError_t i8_to_bf16_launch(const int8_t* src, size_t n, __nv_bfloat16* dst, cudaStream_t st) {
+  i8_to_bf16_kernel<<<1024, 256, 0, st>>>(src, n, dst);
+  return cudaGetLastError();
+}
+
 // A bounded wait that is meant to run out: one thread waits on an mbarrier
 // that nothing arrives on, for `polls` tries, then records the timeout in the
 // error word the way every bounded wait of the library does, and the kernel

@@ -320,8 +320,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
       }
       if (run) {
-        if (MODE == kTcFc && p.out_h16) {
-          // hidden_norm fused: f16(fc * w) here, 1/rms per row in the context K|V GEMM
+        if (MODE == kTcFc && p.out_b16) {
+          // hidden_norm fused: bf16(fc * w) here, 1/rms per row in the context K|V GEMM
           float ss = 0.f;
 #pragma unroll 1
           for (int ch = 0; ch < TC_BN / 32; ++ch) {
@@ -335,9 +335,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
               for (int e = 0; e < 32; e += 2) {
                 const float a = __uint_as_float(r[e]), b = __uint_as_float(r[e + 1]);
                 ss += a * a + b * b;
-                o[e / 2] = pack_f16x2(a * __ldg(w + e), b * __ldg(w + e + 1));
+                o[e / 2] = pack_bf16x2(a * __ldg(w + e), b * __ldg(w + e + 1));
               }
-              uint4* dst = reinterpret_cast<uint4*>(p.out_h16 + (size_t)row * p.N + n0 + ch * 32);
+              uint4* dst = reinterpret_cast<uint4*>(p.out_b16 + (size_t)row * p.N + n0 + ch * 32);
 #pragma unroll
               for (int v = 0; v < 4; ++v) dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
             }
@@ -582,6 +582,7 @@ static cudaError_t tc_dispatch(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, b
     if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32, NSRC>(ma, mb, p, st);
     if constexpr (NSRC == 1) {
       if (mode == kTcArgmax) return tc_launch_t<1, kTcArgmax, 1>(ma, mb, p, st);
+      if (mode == kTcCtxKV) return tc_launch_t<1, kTcCtxKV, 1>(ma, mb, p, st);
     }
   } else {
     if constexpr (NSRC == 1) {
