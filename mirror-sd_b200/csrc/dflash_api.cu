@@ -110,7 +110,8 @@ struct Handle {
   int* sa_cand_i = nullptr;
   int* sa_cnt = nullptr;             // [max_batch] arrival counters (zero between launches)
   KvSeq* kv_seq = nullptr;           // [max_batch + 1] per-sequence records of the current forward
-  float* tc_part = nullptr;          // tcgen05 GEMM tail-split partials [num_sms][128 * 256]
+  float* tc_part = nullptr;          // tcgen05 GEMM tail-split partials [tc_cap][128 * 256]
+  int tc_cap = 0;
   int* tc_cnt = nullptr;             // their arrival counters [num_sms] (zero between launches)
   bool dense = false;                // the dense block path is available (max rows > kW8Rows)
   size_t stateless_rows = 0;         // K/V rows per layer and kv head of the stateless store
@@ -393,7 +394,8 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(A.alloc(&hd->sa_cand_i, nc));
     CKC(A.alloc(&hd->sa_cnt, (size_t)d.max_batch));
     CKC(A.alloc(&hd->kv_seq, (size_t)d.max_batch + 1));
-    CKC(A.alloc(&hd->tc_part, (size_t)hd->num_sms * 128 * 256));
+    hd->tc_cap = 4 * hd->num_sms;   // up to ~4 tail parts per CTA
+    CKC(A.alloc(&hd->tc_part, (size_t)hd->tc_cap * 128 * 256));
     CKC(A.alloc(&hd->tc_cnt, (size_t)hd->num_sms));
     CKC(cudaMemset(hd->tc_cnt, 0, (size_t)hd->num_sms * sizeof(int)));
     CKC(cudaMemset(hd->sa_cnt, 0, (size_t)d.max_batch * sizeof(int)));
@@ -607,7 +609,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
 
   if (Ctot > 0) {
     TcParams fp{};
-    fp.tail_part = hd->tc_part; fp.tail_cnt = hd->tc_cnt;
+    fp.tail_part = hd->tc_part; fp.tail_cnt = hd->tc_cnt; fp.tail_cap = hd->tc_cap;
     fp.M = Ctot; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
     // hidden_norm (dflash.py:392) is split over the two GEMMs: the fc epilogue
     // stores f16(fc * w) with per-row sums of squares, and the context K|V
@@ -617,7 +619,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     CK(mark(2));
     CK(mark(3));
     TcParams kp{};
-    kp.tail_part = hd->tc_part; kp.tail_cnt = hd->tc_cnt;
+    kp.tail_part = hd->tc_part; kp.tail_cnt = hd->tc_cnt; kp.tail_cap = hd->tc_cap;
     kp.M = Ctot; kp.N = nl * 2 * NKV * 128; kp.K = H; kp.err = hd->dev_err;
     kp.scale = hd->s_kv_ctx; kp.k_norm = hd->k_norm_all; kp.rope = hd->rope;
     kp.k_out = Kbase; kp.v_out = Vbase; kp.layer_stride = layer_stride;
@@ -646,7 +648,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     __half* Vl = Vbase + l * layer_stride;
     CK(ctx_norm_launch(hd->h, hd->hstat, hparts, M, H, ly.in_norm, d.rms_norm_eps, hd->xa, st));
     TcParams qp{};
-    qp.tail_part = hd->tc_part; qp.tail_cnt = hd->tc_cnt;
+    qp.tail_part = hd->tc_part; qp.tail_cnt = hd->tc_cnt; qp.tail_cap = hd->tc_cap;
     qp.M = M; qp.N = (NQ + 2 * NKV) * 128; qp.K = H; qp.err = hd->dev_err;
     qp.scale = ly.s_qkv; qp.q_norm = ly.q_norm; qp.k_norm = hd->k_norm_all + l * 128;
     qp.rope = hd->rope; qp.rope_row0 = Ctot; qp.eps = d.rms_norm_eps;
@@ -660,18 +662,18 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     ap.kv = m; ap.kv_seqs = cc ? cc->max_batch : b; ap.err = hd->dev_err;
     CK(attn_tc_launch(ap, b, hd->attn_out, st));
     TcParams op{};
-    op.tail_part = hd->tc_part; op.tail_cnt = hd->tc_cnt;
+    op.tail_part = hd->tc_part; op.tail_cnt = hd->tc_cnt; op.tail_cap = hd->tc_cap;
     op.M = M; op.N = H; op.K = NQ * 128; op.err = hd->dev_err;
     op.scale = ly.s_o; op.h = hd->h; op.sumsq_part = hd->hstat;
     CK(tc_gemm_launch(hd->attn_out, ly.dw_o, false, kTcResid, op, st));
     hparts = H / 256;
     CK(ctx_norm_launch(hd->h, hd->hstat, hparts, M, H, ly.post_norm, d.rms_norm_eps, hd->xa, st));
     TcParams gp{};
-    gp.tail_part = hd->tc_part; gp.tail_cnt = hd->tc_cnt;
+    gp.tail_part = hd->tc_part; gp.tail_cnt = hd->tc_cnt; gp.tail_cap = hd->tc_cap;
     gp.M = M; gp.N = 2 * I; gp.K = H; gp.err = hd->dev_err; gp.scale = ly.ds_gu; gp.act = hd->act;
     CK(tc_gemm_launch(hd->xa, ly.dw_gu, false, kTcSilu, gp, st));
     TcParams dp{};
-    dp.tail_part = hd->tc_part; dp.tail_cnt = hd->tc_cnt;
+    dp.tail_part = hd->tc_part; dp.tail_cnt = hd->tc_cnt; dp.tail_cap = hd->tc_cap;
     dp.M = M; dp.N = H; dp.K = I; dp.err = hd->dev_err;
     dp.scale = ly.s_d; dp.h = hd->h; dp.sumsq_part = hd->hstat;
     CK(tc_gemm_launch(hd->act, ly.dw_d, false, kTcResid, dp, st));
@@ -741,7 +743,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     int grid = 0;
     if (lm_dense) {
       TcParams tp{};
-    tp.tail_part = hd->tc_part; tp.tail_cnt = hd->tc_cnt;
+    tp.tail_part = hd->tc_part; tp.tail_cnt = hd->tc_cnt; tp.tail_cap = hd->tc_cap;
       tp.M = b * (B - 1); tp.N = (d.vocab_size + 255) / 256 * 256; tp.K = H; tp.err = hd->dev_err;
       tp.V = d.vocab_size; tp.best_val = hd->lm_val; tp.best_idx = hd->lm_idx;
       CK(tc_gemm_launch(hd->hn, hd->lm_tiles, true, kTcArgmax, tp, st));
@@ -995,7 +997,8 @@ int dflash_tc_gemm(const uint16_t* A, const uint16_t* B, int M, int N, int K, in
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  CK(cudaMallocAsync(&p.tail_part, (size_t)sms * 128 * 256 * sizeof(float), st));
+  p.tail_cap = 4 * sms;
+  CK(cudaMallocAsync(&p.tail_part, (size_t)p.tail_cap * 128 * 256 * sizeof(float), st));
   CK(cudaMallocAsync(&p.tail_cnt, (size_t)sms * sizeof(int), st));
   CK(cudaMemsetAsync(p.tail_cnt, 0, (size_t)sms * sizeof(int), st));
   cudaError_t e = tc_gemm_launch(A, B, ab_bf16 != 0, kTcStoreF32, p, st);

@@ -147,10 +147,11 @@ struct TcParams {
   int a_cols;               // K columns per A source (tc_gemm_launch_src); K for one source
   int* err;
   // tail split (set by the launcher): the partial last round of tiles is cut
-  // along K into `split` parts; workspace tail_part [grid][128 * 256] fp32,
-  // tail_cnt [grid] zero between launches.  NULL workspace: no split.
+  // along K into `split` parts; workspace tail_part [tail_cap][128 * 256]
+  // fp32, tail_cnt [SMs] zero between launches.  NULL workspace: no split.
   float* tail_part;
   int* tail_cnt;
+  int tail_cap;             // partial slots of 128 * 256 floats in tail_part
   int split;
   // kTcFc and kTcStoreF32
   float* out_f32;           // [M, N]

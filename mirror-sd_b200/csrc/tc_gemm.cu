@@ -51,9 +51,9 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 
 // Work of CTA c (grid G, T tiles): tiles c, c + G, ... of the first
 // R = T / G rounds; with a tail split S > 0 the T - R*G tiles of the last,
-// partial round are cut along K into S parts each, and CTA c < (T - R*G) * S
-// adds one part (tail tile R*G + c / S, part c % S).  With G = T * S (few
-// tiles) R is 0 and every tile is split.  A tail part writes its
+// partial round are cut along K into S parts each, P = (T - R*G) * S parts
+// in all, and CTA c adds parts c, c + G, ... < P (part q: tail tile
+// R*G + q / S, K part q % S).  With few tiles R is 0 and every tile is split.  A tail part writes its
 // fp32 partial accumulator to the workspace; the last part of a tile to
 // finish sums the parts in fixed order and runs the epilogue.
 struct TcItem {
@@ -62,9 +62,10 @@ struct TcItem {
 __device__ __forceinline__ TcItem tc_item(int ti, int T, int nk, int split) {
   const int G = gridDim.x, c = blockIdx.x;
   const int R = T / G;
-  if (split > 0 && ti == R) {
-    const int part = c % split;
-    return {R * G + c / split, part * nk / split, (part + 1) * nk / split, part};
+  if (split > 0 && ti >= R) {
+    const int q = c + (ti - R) * G;
+    const int part = q % split;
+    return {R * G + q / split, part * nk / split, (part + 1) * nk / split, part};
   }
   return {c + ti * G, 0, nk, -1};
 }
@@ -72,7 +73,8 @@ __device__ __forceinline__ int tc_items(int T, int split) {
   const int G = gridDim.x, c = blockIdx.x;
   if (split > 0) {
     const int R = T / G;
-    return R + (c < (T - R * G) * split ? 1 : 0);
+    const int P = (T - R * G) * split;
+    return R + (P > c ? (P - c + G - 1) / G : 0);
   }
   return T > c ? (T - c + G - 1) / G : 0;
 }
@@ -267,34 +269,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int n0 = nb * TC_BN;
       const int row = mb * TC_BM + row_local;
       const bool row_ok = row < p.M;
-      if (!mbar_wait(&accf[buf], (ti >> 1) & 1, p.err, abort_flag) || *abort_flag) break;
-      tc_fence_after();
+      // No epilogue warp leaves the loop early: after a timeout (the abort
+      // flag) the items are walked without work, so every named barrier of
+      // the tail parts below is reached by all four warps.
+      const bool live = mbar_wait(&accf[buf], (ti >> 1) & 1, p.err, abort_flag) && !*abort_flag;
+      if (live) tc_fence_after();
       const uint32_t tbase = tmem + buf * TC_BN + ((uint32_t)(q * 32) << 16);
-      bool run = true;
+      bool run = live;
       if (w.part >= 0) {
-        // tail part (the CTA's last item).  Once its accumulator is complete
-        // no wait of this CTA is left that could still time out, so either
-        // all four epilogue warps get here or none do: the named barriers
-        // below always fill.
         const int slot = w.tile - (ntiles / gridDim.x) * gridDim.x;
         float* mine = p.tail_part + ((size_t)slot * p.split + w.part) * (TC_BM * TC_BN);
+        if (live) {
 #pragma unroll 1
-        for (int ch = 0; ch < TC_BN / 32; ++ch) {
-          uint32_t r[32];
-          tmem_ld32(tbase + ch * 32, r);
-          tmem_ld_wait();
+          for (int ch = 0; ch < TC_BN / 32; ++ch) {
+            uint32_t r[32];
+            tmem_ld32(tbase + ch * 32, r);
+            tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mine[(size_t)(ch * 32 + e) * TC_BM + row_local] = __uint_as_float(r[e]);
+            for (int e = 0; e < 32; ++e) mine[(size_t)(ch * 32 + e) * TC_BM + row_local] = __uint_as_float(r[e]);
+          }
         }
         __threadfence();
         named_bar_sync(2, 128);
-        if (threadIdx.x == 64) *tail_flag = atomicAdd(p.tail_cnt + slot, 1) == p.split - 1;
+        if (threadIdx.x == 64) {
+          // every part counts, after an abort too, so the counter always
+          // returns to zero for the next launch
+          const bool last = atomicAdd(p.tail_cnt + slot, 1) == p.split - 1;
+          if (last) p.tail_cnt[slot] = 0;
+          *tail_flag = last;
+        }
         named_bar_sync(2, 128);
-        run = *tail_flag != 0;
+        run = live && *tail_flag != 0;
         if (run) {
           // the last part: sum the parts in fixed order into the accumulator
           __threadfence();
-          if (threadIdx.x == 64) p.tail_cnt[slot] = 0;
           const float* base = p.tail_part + (size_t)slot * p.split * (TC_BM * TC_BN);
 #pragma unroll 1
           for (int ch = 0; ch < TC_BN / 32; ++ch) {
@@ -536,16 +544,33 @@ static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inn
   return r == CUDA_SUCCESS;
 }
 
-// parts per tail tile: the tail round's tiles spread over the grid, each part
-// at least 4 k-blocks; 0 (no split) when the tiles fill whole rounds or a part
-// would be too short to pay for its partial write
-int tc_tail_split(int tiles, int grid, int nk, bool have_workspace) {
-  if (!have_workspace || grid < 1) return 0;
-  const int tail = tiles - (tiles / grid) * grid;
+// Tail split: the tiles of the partial last round (all tiles when there are
+// fewer than SMs) are cut along K into S parts spread over the grid.  S
+// minimises the makespan in tile units, R + ceil(tail * S / G) * (1 / S + c),
+// where c, the cost of writing and merging a partial accumulator, is taken
+// as 10 k-blocks of MMA; each part has at least 4 k-blocks and the parts fit
+// cap_parts partial slots.  0 (no split) when the tiles fill whole rounds or
+// no S >= 2 saves at least 5%.  Returns S and the grid to launch.
+int tc_tail_split(int tiles, int sms, int nk, int cap_parts, int* grid_out) {
+  int grid = tiles < sms ? tiles : sms;
+  *grid_out = grid;
+  if (cap_parts <= 0 || sms < 1) return 0;
+  const int R = tiles / sms, tail = tiles - R * sms;
   if (tail == 0) return 0;
-  int s = grid / tail;
-  if (s > nk / 4) s = nk / 4;
-  return s >= 2 ? s : 0;
+  const double whole = R + 1.0, c = 10.0 / nk;
+  double best = whole;
+  int bs = 0;
+  for (int s = 2; s <= nk / 4 && (long long)tail * s <= cap_parts; ++s) {
+    const double m = R + (double)((tail * s + sms - 1) / sms) * (1.0 / s + c);
+    if (m < best - 1e-9) {
+      best = m;
+      bs = s;
+    }
+  }
+  if (bs == 0 || best > 0.95 * whole) return 0;
+  // with full rounds the grid is every SM; otherwise as many CTAs as parts, up to the SMs
+  *grid_out = R > 0 ? sms : (tail * bs < sms ? tail * bs : sms);
+  return bs;
 }
 
 template <int FMT, int MODE, int NSRC>
@@ -558,18 +583,8 @@ static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, T
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
   const bool ws = p.tail_part != nullptr && p.tail_cnt != nullptr;
-  int grid = tiles < sms ? tiles : sms;
-  p.split = tc_tail_split(tiles, grid, p.K / TC_BK, ws);
-  if (ws && 2 * tiles <= sms) {
-    // fewer tiles than half the SMs (a short context): every tile is cut
-    // along K, so the grid covers the SMs (all tiles are then "tail" tiles)
-    int s = sms / tiles;
-    if (s > p.K / TC_BK / 4) s = p.K / TC_BK / 4;
-    if (s >= 2) {
-      grid = tiles * s;
-      p.split = s;
-    }
-  }
+  int grid = 0;
+  p.split = tc_tail_split(tiles, sms, p.K / TC_BK, ws ? p.tail_cap : 0, &grid);
   DFL_TRY(max_smem_carveout(kern));
   return launch_pdl(kern, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
 }

@@ -58,7 +58,9 @@ def test_w8_linear_vs_fp32(K, M, N, Kd):
                                          (1000, 256, 25600, True),
                                          # more tiles than SMs: the partial last round is split
                                          # along K (12 tiles x 8 parts; 4 tiles x 16 parts)
-                                         (1280, 4096, 2048, True), (1000, 4864, 4096, False)])
+                                         (1280, 4096, 2048, True), (1000, 4864, 4096, False),
+                                         # 96 tiles (fewer than SMs) in 3 K-parts: two parts per CTA
+                                         (384, 8192, 2048, True)])
 def test_tc_gemm_vs_fp32(K, M, N, Kd, bf16):
     dt = torch.bfloat16 if bf16 else torch.float16
     g = torch.Generator().manual_seed(M + N + Kd)
