@@ -357,18 +357,23 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
     const int q = warp & 3;
     const int et = threadIdx.x - 64;  // 0..127
     constexpr int EPC = (MODE == kSiluMul) ? 2 : 4;
+    // No epilogue warp leaves the loop early: after a timeout (the abort flag)
+    // the segments are walked without work, so every named barrier below is
+    // reached by all four warps and every tile counter returns to zero.
     for (int seg = 0; seg < nseg; ++seg) {
       const int b = seg & 1;
       const Seg sg = sch.get(c, seg);
       const int tile = sg.tile;
       const bool whole = sg.n == 1;
-      if (!mbar_wait(&accf[b], (seg >> 1) & 1, args.err, abort_flag)) break;
-      tc_fence_after();
+      const bool live = mbar_wait(&accf[b], (seg >> 1) & 1, args.err, abort_flag) && !*abort_flag;
+      if (live) tc_fence_after();
       // accumulator column l * MP + m holds limb l of row m: recombine
       float r[MP];
+#pragma unroll
+      for (int m = 0; m < MP; ++m) r[m] = 0.f;
       const uint32_t tb = tmem + b * C::ACC_COLS + ((uint32_t)(q * 32) << 16);
 #pragma unroll
-      for (int c0 = 0; c0 < MP; c0 += 32) {
+      for (int c0 = 0; c0 < MP && live; c0 += 32) {
         uint32_t a0[32], a1[32], a2[32];
         tmem_ld32(tb + c0, a0);
         tmem_ld32(tb + MP + c0, a1);
@@ -388,7 +393,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
 #pragma unroll
         for (int m = 0; m < MP; ++m) red[m * 129 + ch] = r[m];
         named_bar(1, 128);
-        for (int m = q; m < p.M; m += 4) {
+        for (int m = q; m < p.M && live; m += 4) {
           float v[4], u[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -412,7 +417,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
           __threadfence();
           const float* src = args.part + (size_t)tile * args.maxseg * MP * 128;
           // two rows per pass, every slot's partial loaded before any add
-          for (int m0 = q; m0 < p.M; m0 += 8) {
+          for (int m0 = q; m0 < p.M && live; m0 += 8) {
             float4 va[2][8], ua[2][8];
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr)
