@@ -677,7 +677,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     dp.M = M; dp.N = H; dp.K = I; dp.err = hd->dev_err;
     dp.scale = ly.s_d; dp.h = hd->h; dp.sumsq_part = hd->hstat;
     CK(tc_gemm_launch(hd->act, ly.dw_d, false, kTcResid, dp, st));
-    launches += 8;  // 2 norms, q|k|v, attention partial + combine, o, gate|up, down
+    launches += 7 + (splits > 1);  // 2 norms, q|k|v, attention (+ combine), o, gate|up, down
   }
   for (int l = 0; !dense && l < nl; ++l) {
     const Layer& ly = hd->layers[l];
@@ -728,7 +728,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
       dn.next_norm = hd->layers[l + 1].in_norm;
     }
     CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
-    launches += 10;  // 2 norms + 2 limb splits, qkv, attention partial + combine, o, gate|up, down
+    launches += 9 + (splits > 1);  // 2 norms + 2 limb splits, qkv, attention (+ combine), o, gate|up, down
   }
   CK(mark(5));
   // dense path: the lm_head reads only rows 1..B-1 of every block, packed
