@@ -240,19 +240,12 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
   }
 }
 
-// merge split partials -> out [b*B, NQ*128] f16 (row = bi*B + j, col = head*128 + d);
-// one warp per (batch, head, block row), lanes split the splits for the
-// max / denominator and the head dims for the weighted sum.
-__global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out) {
-  griddep_wait();
-  griddep_launch_dependents();
+// Merge of the split partials of one (sequence bi, head, block row j): one
+// warp, lanes split the splits for the max / denominator and the head dims
+// for the weighted sum.  Returns lane's 4 output dims as f16.
+__device__ __forceinline__ uint2 attn_merge_row(const AttnParams& p, int bi, int head, int j, int lane) {
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int bi = blockIdx.y;
-  if (row >= p.nq * p.block) return;
-  const int head = row / p.block, j = row % p.block;
   const int kvh = head / G;
   const int r = (head - kvh * G) * p.block + j;
   const size_t base = (((size_t)bi * p.nkv + kvh) * p.splits) * (size_t)R + r;
@@ -295,6 +288,20 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
   uint2 pk;
   pk.x = pack_f16x2(acc[0] * inv, acc[1] * inv);
   pk.y = pack_f16x2(acc[2] * inv, acc[3] * inv);
+  return pk;
+}
+
+// merge split partials -> out [b*B, NQ*128] f16 (row = bi*B + j, col = head*128 + d);
+// one warp per (batch, head, block row)
+__global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int bi = blockIdx.y;
+  if (row >= p.nq * p.block) return;
+  const int head = row / p.block, j = row % p.block;
+  const uint2 pk = attn_merge_row(p, bi, head, j, lane);
   *reinterpret_cast<uint2*>(out + ((size_t)bi * p.block + j) * ((size_t)p.nq * 128) +
                             (size_t)head * 128 + lane * 4) = pk;
   if (p.omax) {  // per (head, row) max |out| for the o-projection's limb split
@@ -303,6 +310,73 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
     const float mx = warp_max(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
     if (lane == 0) p.omax[(size_t)head * gridDim.y * p.block + (size_t)bi * p.block + j] = mx;
   }
+}
+
+// The merge fused with the o-projection's limb split.  One cluster of
+// C = ceil(NQ / 8) CTAs per activation row m = bi * B + j; CTA c merges heads
+// 8c .. 8c + 7 (a warp each), and the cluster exchanges the maxima of the f16
+// rows through distributed shared memory, so every CTA splits its own
+// columns with the row's power-of-two scale.  The limbs and scales are those
+// that attn_combine_kernel followed by the standalone limb split produce.
+__global__ void __launch_bounds__(256) attn_combine_limbs_kernel(const AttnParams p, int M, int MP,
+                                                                 int8_t* __restrict__ xl,
+                                                                 float* __restrict__ xscale) {
+  griddep_wait();
+  griddep_launch_dependents();
+  __shared__ float wmax[8];
+  __shared__ float cmax;
+  const int K = p.nq * 128;
+  const int c = blockIdx.x, m = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = c * 8 + warp;
+  const size_t col = (size_t)head * 128 + lane * 4;
+  int8_t* o0 = xl + (size_t)m * K + col;
+  int8_t* o1 = o0 + (size_t)MP * K;
+  int8_t* o2 = o1 + (size_t)MP * K;
+  if (m >= M) {  // padding rows: the whole cluster takes this branch
+    if (head < p.nq) {
+      *reinterpret_cast<uint32_t*>(o0) = 0u;
+      *reinterpret_cast<uint32_t*>(o1) = 0u;
+      *reinterpret_cast<uint32_t*>(o2) = 0u;
+    }
+    if (c == 0 && threadIdx.x == 0) xscale[m] = 1.f;
+    return;
+  }
+  const int bi = m / p.block, j = m - bi * p.block;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (head < p.nq) {
+    const uint2 pk = attn_merge_row(p, bi, head, j, lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&pk.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&pk.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+  const float mx = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+  if (lane == 0) wmax[warp] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t = fmaxf(t, wmax[w]);
+    cmax = t;
+  }
+  cluster_arrive_release();
+  cluster_wait_acquire();  // every CTA of the row has its maximum in place
+  float rmx = 0.f;
+  for (uint32_t r = 0; r < gridDim.x; ++r) rmx = fmaxf(rmx, ld_cluster_f32(&cmax, r));
+  cluster_arrive_release();  // done reading the peers' shared memory
+  int e;
+  frexpf(rmx, &e);  // every |x| <= rmx < 2^e
+  const float up = ldexpf(1.f, 20 - e);
+  if (c == 0 && threadIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
+  if (head < p.nq) {
+    int8_t l[3][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) limbs_of(v[t], up, l[0][t], l[1][t], l[2][t]);
+    *reinterpret_cast<char4*>(o0) = make_char4(l[0][0], l[0][1], l[0][2], l[0][3]);
+    *reinterpret_cast<char4*>(o1) = make_char4(l[1][0], l[1][1], l[1][2], l[1][3]);
+    *reinterpret_cast<char4*>(o2) = make_char4(l[2][0], l[2][1], l[2][2], l[2][3]);
+  }
+  cluster_wait_acquire();  // no CTA leaves while a peer may still read its maximum
 }
 
 size_t attn_smem_bytes(int nq, int nkv, int block) {
@@ -344,6 +418,15 @@ cudaError_t attn_combine_launch(const AttnParams& p, int batch, __half* out, cud
   const int rows = p.nq * p.block;
   DFL_TRY(max_smem_carveout(attn_combine_kernel));
   return launch_pdl(attn_combine_kernel, dim3((rows + 7) / 8, batch), dim3(256), 0, st, p, out);
+}
+
+cudaError_t attn_combine_limbs_launch(const AttnParams& p, int batch, const AttnLimbOut& lo, cudaStream_t st) {
+  const int C = (p.nq + 7) / 8;
+  if (C > 8 || lo.M != batch * p.block || lo.M < 1 || lo.M > 64 || !lo.xl || !lo.xscale)
+    return cudaErrorInvalidValue;
+  const int mp = (lo.M + 15) / 16 * 16;
+  return launch_pdl_cluster(attn_combine_limbs_kernel, dim3(C, mp), dim3(256), (unsigned)C, st, p, lo.M, mp,
+                            lo.xl, lo.xscale);
 }
 
 }  // namespace dfl

@@ -595,7 +595,7 @@ static cudaError_t attn_tc_launch_t(const AttnParams& p, int batch, cudaStream_t
   return launch_pdl(kern, dim3(p.splits, p.nkv, batch), dim3(C::THREADS), C::SMEM, st, mk, mv, p);
 }
 
-cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st) {
+cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st, AttnLimbOut* limbs) {
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
   if (p.nq % p.nkv || R < 1 || R > 256 || p.kv_len < 1 || p.chunk % TA_TK || p.normrope)
@@ -615,7 +615,13 @@ cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStre
   else
     e = many ? attn_tc_launch_t<1, 2, 1>(q, batch, st) : attn_tc_launch_t<1, 0, 1>(q, batch, st);
   DFL_TRY(e);
-  return q.out ? cudaSuccess : attn_combine_launch(p, batch, out, st);
+  if (q.out) return cudaSuccess;
+  if (limbs && p.nq <= 64) {  // the merge writes the o-projection's limbs
+    DFL_TRY(attn_combine_limbs_launch(p, batch, *limbs, st));
+    limbs->done = true;
+    return cudaSuccess;
+  }
+  return attn_combine_launch(p, batch, out, st);
 }
 
 }  // namespace dfl

@@ -307,6 +307,56 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
 }
 
+// The same with thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x,
+                                      cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
+// thread-block cluster barrier (every thread of every CTA of the cluster) and
+// loads from a peer CTA's shared memory
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// W8A16 activation limbs of one value: q = rint(x * up) (|q| < 2^20, up a
+// power of two) written as l0 + 128 l1 + 16384 l2, l0 and l1 in [-64, 63],
+// l2 in [-64, 64]
+__device__ __forceinline__ void limbs_of(float x, float up, int8_t& l0, int8_t& l1, int8_t& l2) {
+  const int qv = __float2int_rn(x * up);   // exact scaling by a power of two
+  const int x0 = ((qv + 64) & 127) - 64;
+  const int r1 = (qv - x0) / 128;          // exact
+  const int x1 = ((r1 + 64) & 127) - 64;
+  l0 = (int8_t)x0;
+  l1 = (int8_t)x1;
+  l2 = (int8_t)((r1 - x1) / 128);
+}
+
 #define DFL_TRY(call)                      \
   do {                                     \
     const cudaError_t e_ = (call);         \

@@ -703,10 +703,12 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     ap.kv = m; ap.kv_seqs = cc ? cc->max_batch : b;
     ap.omax = hd->amax;
     ap.err = hd->dev_err;
-    CK(attn_tc_launch(ap, b, hd->attn_out, st));
+    // with several KV splits the merge writes the o-projection's limbs itself
+    AttnLimbOut lo{hd->xl, hd->xs, M, false};
+    CK(attn_tc_launch(ap, b, hd->attn_out, st, &lo));
     // o_proj + residual
     W8Params o{};
-    CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->amax, NQ, hd->xl, hd->xs, st));
+    if (!lo.done) CK(w8_limbs_launch(hd->attn_out, M, NQ * 128, hd->amax, NQ, hd->xl, hd->xs, st));
     o.scale = ly.s_o; o.N = H; o.K = NQ * 128; o.M = M; o.xl = hd->xl; o.xscale = hd->xs;
     o.h_out = hd->h; o.hstat_out = hd->hstat; o.hmax_out = hd->hmax; o.next_norm = ly.post_norm;
     CK(w8tc_launch(ly.w_o, o, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
@@ -728,7 +730,9 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
       dn.next_norm = hd->layers[l + 1].in_norm;
     }
     CK(w8tc_launch(ly.w_d, dn, kResid, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
-    launches += 9 + (splits > 1);  // 2 norms + 2 limb splits, qkv, attention (+ combine), o, gate|up, down
+    // 2 norms + limbs of the SiLU output, qkv, attention, merge and/or limbs of its output,
+    // o, gate|up, down
+    launches += 8 + (splits > 1) + (lo.done ? 0 : 1);
   }
   CK(mark(5));
   // dense path: the lm_head reads only rows 1..B-1 of every block, packed

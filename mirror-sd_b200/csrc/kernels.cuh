@@ -224,9 +224,21 @@ size_t attn_smem_bytes(int nq, int nkv, int block);
 void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits);
 // mma.sync split kernel (also the fused QK-norm + RoPE variant) + combine
 cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
+// The o-projection's input as W8A16 limbs ([3][MP][NQ*128] limb-major, MP =
+// M padded to 16, rows >= M zero; power-of-two row scales), written by the
+// split merge when it can (more than one KV split, at most 64 query heads):
+// attn_tc_launch then sets `done` and writes no f16 rows.
+struct AttnLimbOut {
+  int8_t* xl;
+  float* xscale;
+  int M;       // activation rows (batch * block)
+  bool done;
+};
 // tcgen05 split kernel (S and O in TMEM; no normrope) + combine
-cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
+cudaError_t attn_tc_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st,
+                           AttnLimbOut* limbs = nullptr);
 cudaError_t attn_combine_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
+cudaError_t attn_combine_limbs_launch(const AttnParams& p, int batch, const AttnLimbOut& lo, cudaStream_t st);
 
 // A given as column blocks held in separate arrays: A[:, f*cols:(f+1)*cols] is
 // ptr[f] (rows ld[f] elements apart), f < n; n * cols == K

@@ -489,16 +489,7 @@ __global__ void w8_tilepack_kernel(const int8_t* __restrict__ src, int n_src, in
 
 // ------------------------------------------------------------------ activation limbs
 // Limb layout of one launch: int8 [3][MP][K] (limb-major), rows M..MP-1 zero,
-// plus the fp32 row scale 2^(e_m - 20) with max|x_m| < 2^e_m.
-__device__ __forceinline__ void limbs_of(float x, float up, int8_t& l0, int8_t& l1, int8_t& l2) {
-  const int qv = __float2int_rn(x * up);   // exact scaling by a power of two, |qv| < 2^20
-  const int x0 = ((qv + 64) & 127) - 64;
-  const int r1 = (qv - x0) / 128;          // exact
-  const int x1 = ((r1 + 64) & 127) - 64;
-  l0 = (int8_t)x0;
-  l1 = (int8_t)x1;
-  l2 = (int8_t)((r1 - x1) / 128);
-}
+// plus the fp32 row scale 2^(e_m - 20) with max|x_m| < 2^e_m (limbs_of).
 
 __device__ __forceinline__ float block_max(float v, float* sh) {
   v = warp_max(v);
