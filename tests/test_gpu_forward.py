@@ -51,6 +51,14 @@ def test_forward_mid_ragged_tiles(pkg):
     _run_case(pkg, ocfg, 2, 300, seed=5)
 
 
+def test_forward_heads_not_multiple_of_8(pkg):
+    # 12 query heads: the split merge that writes the o-projection's limbs runs
+    # as clusters of two CTAs per row, the second holding 4 heads; 3 sequences
+    # of block 8 leave 8 padding rows in the 32-row limb tile
+    ocfg = tiny_cfg(num_attention_heads=12, num_key_value_heads=4)
+    _run_case(pkg, ocfg, 3, 150, seed=12)
+
+
 def test_forward_num_draft_layers(pkg):
     _run_case(pkg, tiny_cfg(num_hidden_layers=3), 1, 40, seed=9, num_layers=2)
 
