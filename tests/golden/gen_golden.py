@@ -213,7 +213,9 @@ def soft_anchor_fixture(ref_root):
 
 
 if __name__ == "__main__":
-    ref = next((a for a in sys.argv[1:] if not a.startswith("--")), "/root/reference")
+    ref = next((a for a in sys.argv[1:] if not a.startswith("--")), None)
+    if ref is None:
+        sys.exit("usage: python tests/golden/gen_golden.py /path/to/reference [--only-soft-anchor]")
     if "--only-soft-anchor" in sys.argv:
         soft_anchor_fixture(ref)
     else:
