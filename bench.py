@@ -155,54 +155,59 @@ def cpu_oracle_weights(w, lm):
                            lm.float().cpu(), layers)
 
 
-def cpu_step_time(cfgd, dense, noise, th, max_steps, budget_s):
-    """Time full fp32 draft steps of the CPU oracle (forward + lm_head + argmax)."""
+def cpu_step_time(cfgd, dense, noise, th, steps, warmup=0, budget_s=None):
+    """Time full fp32 draft steps of the CPU oracle (forward + lm_head +
+    argmax): `warmup` untimed steps, then `steps` timed ones (or fewer when
+    `budget_s` seconds of timed steps run out).  Returns the timed durations."""
     import torch
     from oracle import dflash_oracle as O
     torch.set_num_threads(os.cpu_count())
     ocfg = O.OracleConfig(**cfgd)
     nz, tt = noise.float().cpu(), th.float().cpu()
     times = []
-    t_start = time.perf_counter()
     with torch.no_grad():
-        while len(times) < max_steps:
+        for i in range(warmup + steps):
             t0 = time.perf_counter()
             hid = O.draft_forward(ocfg, dense, nz, tt)
             O.greedy(O.draft_logits(dense, hid, cfgd["block_size"]))
-            times.append(time.perf_counter() - t0)
-            if time.perf_counter() - t_start > budget_s:
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+            if budget_s is not None and sum(times) > budget_s:
                 break
     return times
 
 
 def run_reference_arm(args, cfgd, rank, world):
+    """The reference algorithm on the host CPU: the fp32 oracle restatement of
+    mirror_sd/dflash.py (MLX cannot run here), on weights and inputs built on
+    the CPU by the oracle itself (nothing of the CUDA library is loaded), with
+    exactly --warmup untimed and --steps timed draft steps."""
     import torch
-    pkg = _pkg()
+    from oracle import dflash_oracle as O
     if rank != 0:
         return
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
-    torch.cuda.set_device(dev)
-    cfg = pkg.DFlashConfig(**cfgd)
-    cfg.target_layer_ids = list(range(F))
-    w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
-    noise, th = synth_inputs(cfgd, args.ctx, args.batch, dev, 0)
-    dense = cpu_oracle_weights(w, lm)
-    del w, lm
-    times = cpu_step_time(cfgd, dense, noise, th, max_steps=max(1, min(args.steps, 3)), budget_s=90)
-    if args.warmup > 0 and len(times) > 1:
-        times = times[1:]  # first call warms the allocator / threads
+    torch.set_num_threads(os.cpu_count())
+    ocfg = O.OracleConfig(**cfgd)
+    ocfg.num_target_features = F
+    t0 = time.perf_counter()
+    _, dense = O.synth_weights(ocfg, seed=0, random_norms=False)
+    noise, th = O.synth_inputs(ocfg, args.batch, args.ctx, cfgd["block_size"], seed=1)
+    build_s = time.perf_counter() - t0
+    times = cpu_step_time(cfgd, dense, noise, th, steps=args.steps, warmup=args.warmup)
     t = statistics.mean(times)
     toks = args.batch * (cfgd["block_size"] - 1)
     val = toks / t
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "draft tok/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+            "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup, "ms_per_step": t * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic",
             "config": workload_config(args, cfgd),
             "cpu_baseline": {"value": val, "unit": "draft tok/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{len(times)} full draft step(s) of the fp32 CPU restatement "
-                                       f"(oracle/dflash_oracle.py; MLX unavailable) on the same config, "
-                                       f"torch CPU with {os.cpu_count()} threads"},
+                             "sample": f"{len(times)} timed full draft steps (after {args.warmup} untimed) "
+                                       f"of the fp32 CPU restatement (oracle/dflash_oracle.py; MLX "
+                                       f"unavailable) on the same config, weights built on the CPU by the "
+                                       f"oracle ({build_s:.0f} s, untimed), torch CPU with "
+                                       f"{os.cpu_count()} threads"},
             "e2e": {"value": val, "unit": "draft tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -228,7 +233,8 @@ def run_serving(args, pkg, rank, world, dev):
     next step brings accept + 1 context rows per request.  One step = the
     draft forward of every request (dense tcgen05 projections and lm_head at
     these row counts), the verifier emulation (two small torch ops), device
-    acceptance, the accepted lengths read back, and the block-row trim."""
+    acceptance, the accepted lengths read back, and the block-row trim.
+    Returns the JSON line on rank 0 (None elsewhere)."""
     import torch
     shard = importlib.import_module("mirror-sd_b200.shard")
     serving = importlib.import_module("mirror-sd_b200.serving")
@@ -306,8 +312,12 @@ def run_serving(args, pkg, rank, world, dev):
                                       "prefill_ms": prefill_ms, "prefill_rows": sum(ctx)})
     if sampler:
         sampler.stop()
+    line = None
     if rank == 0:
         hbm, tf_burst, tf_sust, src = peaks()
+        # burst peak for a sub-second timed region, the sustained one beyond
+        tf_peak, peak_name = (tf_burst, "bf16_tflops") if ms * args.steps < 1e3 else \
+            (tf_sust, "bf16_tflops_sustained")
         n_all = sum(r["n"] for r in per_rank)
         acc_all = sum(r["accepted"] for r in per_rank)
         M = n * B
@@ -328,17 +338,196 @@ def run_serving(args, pkg, rank, world, dev):
                        "block": B, "ctx": "U[512, 8192] prefilled", "cache": "sink 64 / window 1024",
                        "accept": "geometric p=0.85", "parallelism": f"requests sharded over {world} GPU(s)"},
             "tensor_roofline": {"flops_per_step_rank0": flops, "achieved_tflops": flops / (ms / 1e3) / 1e12,
-                                "peak": tf_sust, "frac": flops / (ms / 1e3) / 1e12 / tf_sust,
-                                "peak_source": f"{src} bf16_tflops_sustained"},
+                                "peak": tf_peak, "frac": flops / (ms / 1e3) / 1e12 / tf_peak,
+                                "frac_of_sustained": flops / (ms / 1e3) / 1e12 / tf_sust,
+                                "peak_source": f"{src} {peak_name} (timed region {ms * args.steps:.0f} ms)"},
             "prefill": {"rows": sum(r["prefill_rows"] for r in per_rank),
                         "ms_max": max(r["prefill_ms"] for r in per_rank)},
             "mean_accept": acc_all / (args.steps * n_all),
             "gpu_launches_per_step": launches + 2,
             "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         }
-        print(json.dumps(line), flush=True)
     server.close()
     model.close()
+    return line
+
+
+# ---------------------------------------------------------------- kernel cases
+KERNEL_CASES = """\
+Kernel cases (--kernel CASE), each one hot-path kernel through its C entry
+point on the 27B-class dims (32 block rows), small enough for an ncu capture
+(< 2 GB on the device, more than the 126 MB L2 streamed per launch):
+  w8_gu    gate|up W8A16 projection   N=34816 K=5120   (178 MB int8)
+  w8_down  down W8A16 projection      N=5120  K=17408  (89 MB)
+  w8_qkv   fused q|k|v projection     N=7168  K=5120   (37 MB)
+  w8_o     o projection               N=5120  K=5120   (26 MB)
+  w8:N:K   any W8A16 shape (N, K multiples of 128)
+  lm_head  tied lm_head + argmax      V=151936 H=5120  (1.56 GB bf16)
+  attn     block attention            40/8 heads, 32 queries, kv 4128
+  attn16   the same at batch 16, kv 32800 (2.1 GB of K/V)
+  attn_c5  the batched serving shape: 256 sequences, 32 q / 8 kv heads, 16
+           queries, kv 1104 (a sink 64 / window 1024 cache plus the block)
+  fc       context fc GEMM            4096 x 25600 x 5120 (bf16)
+  step1    one draft step at the bench's 27B dims (block 32, ctx 4096, batch 1)
+           with one decoder layer: the fc and context K|V GEMMs exactly as in
+           the bench with about 4 GB on the device
+  serve    one stateless draft step of --seqs sequences (64 by default) of
+           block 16, ctx 64 each, 8B-class dims: the dense block path
+"""
+
+
+def run_kernel_case(case, iters, warmup, seqs):
+    """Time one kernel case with CUDA events (mean of `iters` launches after
+    `warmup`) and print one JSON line: time, algorithmic bytes and flops."""
+    import torch
+    pkg = _pkg()
+    K = importlib.import_module("mirror-sd_b200.kernels")
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    M = 32
+    if case.startswith("w8_") or case.startswith("w8:"):
+        if case.startswith("w8:"):
+            N, Kd = (int(v) for v in case.split(":")[1:3])
+        else:
+            N, Kd = {"w8_gu": (34816, 5120), "w8_down": (5120, 17408), "w8_qkv": (7168, 5120),
+                     "w8_o": (5120, 5120)}[case]
+        q = torch.randint(-127, 128, (N, Kd), generator=g, device=dev, dtype=torch.int8)
+        s = (torch.rand(N, generator=g, device=dev) * 1e-3).to(torch.float16)
+        x = torch.randn(M, Kd, generator=g, device=dev).to(torch.float16)
+        fn = lambda: K.w8_linear(q, s, x)
+        nbytes, flops = N * Kd, 2 * M * N * Kd
+    elif case == "lm_head":
+        V, H = 151936, 5120
+        E = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        hn = torch.randn(1, M, H, generator=g, device=dev).to(torch.bfloat16)
+        ws = torch.empty(pkg._native.load().dflash_lm_head_workspace_size(1, M, V, H), dtype=torch.uint8,
+                         device=dev)
+        fn = lambda: K.lm_head_argmax(hn, E, workspace=ws)
+        nbytes, flops = V * H * 2, 2 * (M - 1) * V * H
+    elif case in ("attn", "attn16", "attn_c5"):
+        bsz, L, nq, Mq = {"attn": (1, 4128, 40, M), "attn16": (16, 32800, 40, M),
+                          "attn_c5": (256, 1104, 32, 16)}[case]
+        qq = torch.randn(bsz, nq, Mq, 128, generator=g, device=dev).to(torch.float16)
+        kk = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
+        vv = torch.randn(bsz, 8, L, 128, generator=g, device=dev).to(torch.float16)
+        ws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        fn = lambda: K.attention(qq, kk, vv, workspace=ws)
+        nbytes, flops = bsz * 2 * 8 * L * 128 * 2, bsz * 4 * nq * Mq * L * 128
+    elif case == "step1":
+        cfg = pkg.DFlashConfig(**dict(CFG_27B, num_hidden_layers=1))
+        cfg.target_layer_ids = list(range(F))
+        w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+        C, B, H = 4096, 32, 5120
+        model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=1, max_ctx=C, max_block=B, device=dev)
+        noise = (torch.randn(1, B, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        th = torch.randn(1, C, F * H, generator=g, device=dev).to(torch.bfloat16)
+        toks = torch.empty((1, B - 1), dtype=torch.int32, device=dev)
+        fn = lambda: model.draft_step(noise, th, want_hidden=False, out_tokens=toks)
+        nbytes = C * F * H * 2 + H * F * H * 2
+        flops = 2 * C * F * H * H + 2 * C * H * 2 * 8 * 128
+    elif case == "serve":
+        cfg = pkg.DFlashConfig(**CFG_8B)
+        cfg.target_layer_ids = list(range(F))
+        w, lm = pkg.synth_weights_q8(cfg, seed=0, device=dev)
+        n, C, B, H = seqs, 64, 16, 4096
+        model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=n, max_ctx=C, max_block=B, device=dev)
+        noise = (torch.randn(n, B, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        th = torch.randn(n, C, F * H, generator=g, device=dev).to(torch.bfloat16)
+        toks = torch.empty((n, B - 1), dtype=torch.int32, device=dev)
+        fn = lambda: model.draft_step(noise, th, want_hidden=False, out_tokens=toks)
+        params = 5 * ((32 + 16) * 128 * H + H * 32 * 128 + 3 * 12288 * H)
+        nbytes = params * 2 + 151936 * H * 2
+        flops = 2 * n * B * (params + 151936 * H) + 2 * n * C * (F * H * H + H * 5 * 2 * 8 * 128)
+    elif case == "fc":
+        Mr, Kd, N = 4096, 25600, 5120
+        A = torch.randn(Mr, Kd, generator=g, device=dev).to(torch.bfloat16)
+        Bm = (torch.randn(N, Kd, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        fn = lambda: K.tc_gemm(A, Bm)
+        nbytes, flops = (Mr + N) * Kd * 2, 2 * Mr * N * Kd
+    else:
+        raise SystemExit(f"unknown kernel case {case}\n{KERNEL_CASES}")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / iters
+    print(json.dumps({"kernel_case": case, "us_per_call": ms * 1e3, "bytes": nbytes, "flops": flops,
+                      "gb_s": nbytes / ms / 1e6, "tflop_s": flops / ms / 1e9, "iters": iters,
+                      "warmup": warmup}), flush=True)
+
+
+def run_attention_sweep(iters):
+    """c4: block attention (40 query / 8 kv heads, 32 queries, head 128) over
+    ctx 1K..32K at batch 1 and 16, one JSON line per point; algorithmic bytes =
+    Q + O + K + V (f16), fraction of the measured HBM copy peak."""
+    import torch
+    _pkg()
+    K = importlib.import_module("mirror-sd_b200.kernels")
+    lib = importlib.import_module("mirror-sd_b200._native").load()
+    hbm = peaks()[0]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = None
+    for b in (1, 16):
+        for C in (1024, 4096, 8192, 16384, 32768):
+            L = C + 32
+            q = torch.randn(b, 40, 32, 128, generator=g, device=dev).to(torch.float16)
+            k = torch.randn(b, 8, L, 128, generator=g, device=dev).to(torch.float16)
+            v = torch.randn(b, 8, L, 128, generator=g, device=dev).to(torch.float16)
+            need = lib.dflash_attention_workspace_size(b, 40, 8, 32, L)
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(need, dtype=torch.uint8, device=dev)
+            for _ in range(3):
+                K.attention(q, k, v, workspace=ws)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                K.attention(q, k, v, workspace=ws)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            us = e0.elapsed_time(e1) / iters * 1e3
+            nbytes = 2 * b * 40 * 32 * 128 * 2 + 2 * b * 8 * L * 128 * 2
+            flops = 4.0 * b * 40 * 32 * L * 128
+            print(json.dumps({"config": "c4 attention sweep", "batch": b, "ctx": C, "kv_rows": L,
+                              "bytes": nbytes, "us": us, "gb_s": nbytes / us / 1e3,
+                              "hbm_frac": nbytes / us / 1e3 / hbm, "tflop_s": flops / us / 1e6}), flush=True)
+            del q, k, v
+
+
+def _cpulist(txt):
+    cpus = set()
+    for part in txt.split(","):
+        part = part.strip()
+        if not part:
+            continue
+        if "-" in part:
+            a, b = part.split("-")
+            cpus.update(range(int(a), int(b) + 1))
+        else:
+            cpus.add(int(part))
+    return cpus
+
+
+def gpu_numa(dev):
+    """(NUMA node, set of local CPUs) of the GPU's PCI device from sysfs,
+    restricted to the CPUs this process may use; (None, None) when unknown."""
+    import torch
+    p = torch.cuda.get_device_properties(dev)
+    path = f"/sys/bus/pci/devices/{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    try:
+        with open(os.path.join(path, "numa_node")) as f:
+            node = int(f.read().strip())
+        with open(os.path.join(path, "local_cpulist")) as f:
+            cpus = _cpulist(f.read()) & os.sched_getaffinity(0)
+    except (OSError, ValueError):
+        return None, None
+    return node, (cpus or None)
 
 
 def local_gpu_id(dev):
@@ -361,13 +550,28 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c3", "c2", "c5"], default="c3")
+    ap.add_argument("--config", choices=["c3", "c2", "c5", "c4"], default="c3",
+                    help="c3 headline; c2 8B step; c5 batched serving; c4 attention sweep")
+    ap.add_argument("--kernel", default=None, help="time one kernel case instead (list: --kernel help)")
+    ap.add_argument("--iters", type=int, default=20, help="--kernel / c4: timed launches")
     ap.add_argument("--seqs", type=int, default=256, help="c5: requests over all GPUs")
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-serving", action="store_true",
+                    help="skip the batched c5 serving run that the c3 line carries under 'serving'")
+    ap.add_argument("--serving-steps", type=int, default=10)
     args = ap.parse_args()
+    if args.kernel is not None:
+        if args.kernel == "help":
+            print(KERNEL_CASES)
+            return
+        run_kernel_case(args.kernel, args.iters, args.warmup, args.seqs)
+        return
+    if args.config == "c4":
+        run_attention_sweep(args.iters)
+        return
     cfgd = dict(CFG_27B if args.config == "c3" else CFG_8B)
     if args.ctx is None:
         args.ctx = 4096 if args.config == "c3" else 2048
@@ -379,16 +583,16 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        # CPU only: rank 0 runs it, the other ranks exit at once (no process
+        # group, no CUDA context)
+        run_reference_arm(args, cfgd, rank, world)
+        return
     if world > 1:
         import datetime
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
-    if args.impl == "reference":
-        run_reference_arm(args, cfgd, rank, world)
-        if world > 1:
-            dist.destroy_process_group()
-        return
 
     pkg = _pkg()
     shard = importlib.import_module("mirror-sd_b200.shard")
@@ -397,7 +601,9 @@ def main():
     if args.config == "c5":
         if args.steps == 200:
             args.steps = 20
-        run_serving(args, pkg, rank, world, dev)
+        line = run_serving(args, pkg, rank, world, dev)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         if world > 1:
             dist.destroy_process_group()
         return
@@ -486,12 +692,29 @@ def main():
     # end-to-end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        # pinned host buffers on the GPU's own NUMA node: allocate them from
+        # the CPUs local to the GPU's PCI device, then restore the affinity
+        node, local_cpus = gpu_numa(dev)
+        saved_aff = os.sched_getaffinity(0)
+        if local_cpus:
+            os.sched_setaffinity(0, local_cpus)
         noise_h = noise.cpu().pin_memory()
         th_h = th.cpu().pin_memory()
         tgt_h = target.cpu().pin_memory()
         tok_h = torch.empty((args.batch, B - 1), dtype=torch.int32).pin_memory()
         acc_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
         cor_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
+        os.sched_setaffinity(0, saved_aff)
+        # this rank's host->device rate alone (one copy of target_hidden)
+        th_probe = torch.empty_like(th)
+        torch.cuda.synchronize(dev)
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record()
+        th_probe.copy_(th_h, non_blocking=True)
+        h1.record()
+        torch.cuda.synchronize(dev)
+        h2d_alone = th.numel() * 2 / (h0.elapsed_time(h1) / 1e3) / 1e9
+        del th_probe
         # two input buffer sets: step i+1's host->device copies run on a copy
         # stream while step i computes; every step's copies are in the timed region
         bufs = [(torch.empty_like(noise), torch.empty_like(th), torch.empty_like(target)) for _ in range(2)]
@@ -539,13 +762,38 @@ def main():
         ms_e2e = shard.max_over_ranks(s2.elapsed_time(e2) / k2)
         h2d = noise.numel() * 2 + th.numel() * 2 + target.numel() * 4
         d2h = out_t.numel() * 4 + acc.numel() * 4 + cor.numel() * 4
+        ranks_h2d = shard.gather_to_rank0({"gpu_numa_node": node, "local_cpus": len(local_cpus or []),
+                                           "h2d_gbs_alone": h2d_alone,
+                                           "h2d_gbs_in_e2e": h2d / (ms_e2e / 1e3) / 1e9})
         e2e = {"value": shard.job_throughput([args.batch * (B - 1)] * world, ms_e2e), "unit": "draft tok/s",
                "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "steps": k2, "api": "DFlashDraftModel.draft_step on pinned host tensors; the next step's "
-               "host->device copies overlap the current step (copy stream, two buffer sets)"}
+               "host->device copies overlap the current step (copy stream, two buffer sets)",
+               "host_buffers": "pinned, allocated from the CPUs local to the GPU's PCI device (NUMA node "
+                               "of the GPU) when sysfs names them",
+               "per_rank": ranks_h2d}
 
     if sampler:
         sampler.stop()
+    cpu_base = None
+    if rank == 0 and not args.no_cpu_baseline and world == 1:
+        dense = cpu_oracle_weights(w, lm)
+        times = cpu_step_time(cfgd, dense, noise, th, steps=2, warmup=0, budget_s=30)
+        t = min(times)
+        cpu_base = {"value": args.batch * (B - 1) / t, "unit": "draft tok/s",
+                    "cores": os.cpu_count(), "kind": "port",
+                    "sample": f"{len(times)} full fp32 draft step(s) (oracle/dflash_oracle.py, "
+                              f"the reference's MLX being unavailable), best of them"}
+        del dense
+    model.close()
+    del model, w, lm
+    torch.cuda.empty_cache()
+    # the batched config (c5) on the same GPUs, reported under "serving"
+    serving = None
+    if not args.no_serving:
+        sargs = argparse.Namespace(**vars(args))
+        sargs.steps, sargs.warmup = args.serving_steps, 3
+        serving = run_serving(sargs, pkg, rank, world, dev)
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -563,6 +811,17 @@ def main():
         with open(tp) as f:
             traffic = json.load(f).get(f"fc_gemm_{args.config}_ctx{args.ctx}")
     t_step = ms_max / 1e3
+    # The timed region of the headline is K graph replays of a ~2 ms step: a
+    # burst, well under the seconds-long loop (at ~1350 MHz under the power
+    # cap) the sustained peak was measured over, so the burst peak is the
+    # denominator; the sustained fraction is reported beside it.
+    timed_s = ms * args.steps / 1e3
+    if timed_s < 1.0:
+        tf_peak, peak_name = tf_burst, "bf16_tflops"
+        peak_why = f"burst peak, the timed region is {timed_s * 1e3:.0f} ms"
+    else:
+        tf_peak, peak_name = tf_sust, "bf16_tflops_sustained"
+        peak_why = f"sustained peak, the timed region is {timed_s:.1f} s"
     line = {
         "metric": METRIC, "value": shard.job_throughput([args.batch * (B - 1)] * world, ms_max),
         "unit": "draft tok/s",
@@ -573,29 +832,27 @@ def main():
         "dtype": "w8a16: int8 weights, bf16/f16 activations, fp32 accumulate", "data": "synthetic",
         "config": workload_config(args, cfgd),
         "roofline": {"bound": "tensor", "kernel": "fc GEMM (tcgen05, bf16)", "achieved": fc_tfs,
-                     "peak": tf_sust, "unit": "TFLOP/s", "frac": (fc_tfs / tf_sust) if fc_tfs else None,
-                     "peak_source": f"{src} bf16_tflops_sustained", "traffic": traffic,
+                     "peak": tf_peak, "unit": "TFLOP/s", "frac": (fc_tfs / tf_peak) if fc_tfs else None,
+                     "frac_of_sustained": (fc_tfs / tf_sust) if fc_tfs else None,
+                     "peak_source": f"{src} {peak_name}: {peak_why}", "traffic": traffic,
                      "flops_per_launch": fc_flops, "launch_ms": phases["fc_gemm"]},
         "step_roofline": {"bytes": nbytes, "flops": nflops,
                           "hbm_floor_ms": nbytes / (hbm * 1e9) * 1e3,
-                          "tensor_floor_ms": nflops / (tf_sust * 1e12) * 1e3,
-                          "frac_of_max_floor": max(nbytes / (hbm * 1e9), nflops / (tf_sust * 1e12)) / t_step,
+                          "tensor_floor_ms": nflops / (tf_peak * 1e12) * 1e3,
+                          "frac_of_max_floor": max(nbytes / (hbm * 1e9), nflops / (tf_peak * 1e12)) / t_step,
+                          "frac_of_max_floor_sustained": max(nbytes / (hbm * 1e9),
+                                                             nflops / (tf_sust * 1e12)) / t_step,
                           "hbm_frac": nbytes / t_step / (hbm * 1e9)},
         "phases_ms": phases, "accept_len_mean": acc_mean,
         "gpu_launches": launches_per_step * args.steps, "launches_per_step": launches_per_step,
         "clocks": sampler.summary(t_wall0, t_wall1) if sampler else None,
         "e2e": e2e,
     }
-    if not args.no_cpu_baseline and world == 1:
-        dense = cpu_oracle_weights(w, lm)
-        times = cpu_step_time(cfgd, dense, noise, th, max_steps=2, budget_s=30)
-        t = min(times)
-        line["cpu_baseline"] = {"value": args.batch * (B - 1) / t, "unit": "draft tok/s",
-                                "cores": os.cpu_count(), "kind": "port",
-                                "sample": f"{len(times)} full fp32 draft step(s) (oracle/dflash_oracle.py, "
-                                          f"the reference's MLX being unavailable), best of them"}
+    if cpu_base is not None:
+        line["cpu_baseline"] = cpu_base
+    if serving is not None:
+        line["serving"] = serving
     print(json.dumps(line), flush=True)
-    model.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -163,6 +163,44 @@ typedef struct DFlashForwardArgs {
 
 #define DFLASH_PHASES 8
 
+/* ---- fp32-accumulate mode ------------------------------------------------
+ * A handle made by dflash_create_f32 runs the whole draft step in fp32 on the
+ * CUDA cores: fp32 weights (no quantisation), fp32 activations and fp32
+ * accumulation everywhere -- the arithmetic of mirror_sd/dflash.py on fp32
+ * weights (DFlashDraftModel.__call__, dflash.py:384-403) -- so its greedy draft
+ * ids and accepted lengths follow an fp32 evaluation of the reference.
+ * dflash_forward on such a handle reads `noise` as fp32 [batch, block, H] and
+ * `target_hidden` as fp32 [sum_s C_s, F*H] (same pointers, fp32 data), writes
+ * `out_hidden` as fp32 (out_hidden_fp32 is ignored), and takes the stateless
+ * arguments only: `cache`, `anchor_logits` and `target_layers` must be NULL.
+ * All weights are device pointers, row-major [out, in], copied by the call. */
+typedef struct DFlashLayerWeightsF32 {
+  const float* wq; /* [NQ*128, H] */
+  const float* wk; /* [NKV*128, H] */
+  const float* wv; /* [NKV*128, H] */
+  const float* wo; /* [H, NQ*128] */
+  const float* wg; /* [I, H] */
+  const float* wu; /* [I, H] */
+  const float* wd; /* [H, I] */
+  const float* input_layernorm;          /* [H] */
+  const float* post_attention_layernorm; /* [H] */
+  const float* q_norm;                   /* [128] */
+  const float* k_norm;                   /* [128] */
+} DFlashLayerWeightsF32;
+
+typedef struct DFlashWeightsViewF32 {
+  const float* fc;           /* [H, F*H] */
+  const float* hidden_norm;  /* [H] */
+  const float* norm;         /* [H] */
+  const float* lm_head;      /* [V, H]: the target's (tied) embedding */
+  const DFlashLayerWeightsF32* layers; /* HOST array of num_hidden_layers entries */
+} DFlashWeightsViewF32;
+
+/* DFlashDraftModel over fp32 weights (dflash.py:365-382 with an fp32
+ * checkpoint; the reference's MLX CPU path computes in the weights' dtype). */
+int dflash_create_f32(const DFlashDims* dims, const DFlashWeightsViewF32* weights, int device,
+                      void** handle);
+
 int dflash_create(const DFlashDims* dims, const DFlashWeightsView* weights, int device,
                   void** handle);
 int dflash_forward(void* handle, const DFlashForwardArgs* args, void* stream);
@@ -254,9 +292,10 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
  * dflash_attention_workspace_size() exceeds the array is rejected with
  * DFLASH_ERR_INVALID.
  *
- * First call per device: it looks up the array's device address, once per
- * device, while that device is current.  Make that first call outside any
- * stream capture.
+ * Device address: every call looks the array's address up on the caller's
+ * current device (cudaGetSymbolAddress; cheap once the library's device code
+ * is loaded there).  The first call on a device loads that code, so make the
+ * first call outside any stream capture.
  *
  * Sharing: all calls on a device share the one array, and it keeps whatever
  * the last call left in it.  Every byte a call reads is written earlier in
@@ -270,10 +309,7 @@ int dflash_attention_noalloc(const uint16_t* q, const uint16_t* k, const uint16_
                              const float* q_norm, const float* k_norm, float rope_theta,
                              int q_pos0, int k_pos0, float eps, uint16_t* out, void* stream);
 
-/* Tied lm_head + greedy argmax (+ acceptance when target != NULL) on
- * final-normed hidden rows: hn [batch, block, H] bf16, E [V, H] bf16; writes
- * tokens [batch, block-1] for rows 1..block-1 (generate.py:604-606, :722-728).
- * workspace: dflash_lm_head_workspace_size() bytes. */
+
 /* Soft anchor on its own (generate.py:1422-1436): for each of `batch` rows
  * of logits ([batch, ld], fp32 or bf16 when logits_bf16), the k largest
  * entries (larger first, lower index first on ties), their fp32 softmax, and
@@ -285,7 +321,13 @@ int dflash_soft_anchor(const void* logits, int logits_bf16, int batch, int V, in
                        const uint16_t* E, int H, uint16_t* out, void* workspace,
                        size_t workspace_bytes, void* stream);
 
-size_t dflash_lm_head_workspace_size(int batch, int block);
+/* Tied lm_head + greedy argmax (+ acceptance when target != NULL) on
+ * final-normed hidden rows: hn [batch, block, H] bf16, E [V, H] bf16; writes
+ * tokens [batch, block-1] for rows 1..block-1 (generate.py:604-606, :722-728).
+ * workspace: dflash_lm_head_workspace_size() bytes; it also holds the copy of
+ * E repacked into the kernel's vocabulary tiles, so the call allocates
+ * nothing. */
+size_t dflash_lm_head_workspace_size(int batch, int block, int V, int H);
 int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H,
                           int V, int32_t* tokens, const int32_t* target, int32_t* acc_len,
                           int32_t* correction, void* workspace, size_t workspace_bytes,

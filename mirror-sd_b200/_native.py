@@ -44,6 +44,17 @@ class DFlashWeightsView(ctypes.Structure):
                 ("lm_head", c_void_p), ("layers", ctypes.POINTER(DFlashLayerWeights))]
 
 
+class DFlashLayerWeightsF32(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in
+                ["wq", "wk", "wv", "wo", "wg", "wu", "wd",
+                 "input_layernorm", "post_attention_layernorm", "q_norm", "k_norm"]]
+
+
+class DFlashWeightsViewF32(ctypes.Structure):
+    _fields_ = [("fc", c_void_p), ("hidden_norm", c_void_p), ("norm", c_void_p),
+                ("lm_head", c_void_p), ("layers", ctypes.POINTER(DFlashLayerWeightsF32))]
+
+
 class DFlashForwardArgs(ctypes.Structure):
     _fields_ = [("batch", c_int32), ("block", c_int32), ("ctx_len", c_int32),
                 ("rope_offset", c_int32), ("num_layers", c_int32),
@@ -67,6 +78,8 @@ PHASE_NAMES = ["start", "rope+init", "fc_gemm", "hidden_norm", "ctx_kv_gemm", "l
 EXPORTS = {
     "dflash_create": (c_int32, [ctypes.POINTER(DFlashDims), ctypes.POINTER(DFlashWeightsView),
                                 ctypes.c_int, ctypes.POINTER(c_void_p)]),
+    "dflash_create_f32": (c_int32, [ctypes.POINTER(DFlashDims), ctypes.POINTER(DFlashWeightsViewF32),
+                                    ctypes.c_int, ctypes.POINTER(c_void_p)]),
     "dflash_forward": (c_int32, [c_void_p, ctypes.POINTER(DFlashForwardArgs), c_void_p]),
     "dflash_accept": (c_int32, [c_void_p, c_void_p, ctypes.c_int, ctypes.c_int, c_void_p, c_void_p,
                                 c_void_p]),
@@ -107,7 +120,7 @@ EXPORTS = {
                                            ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, c_void_p, c_void_p, c_float, ctypes.c_int,
                                            ctypes.c_int, c_float, c_void_p, c_void_p]),
-    "dflash_lm_head_workspace_size": (c_size_t, [ctypes.c_int, ctypes.c_int]),
+    "dflash_lm_head_workspace_size": (c_size_t, [ctypes.c_int] * 4),
     "dflash_lm_head_argmax": (c_int32, [c_void_p, c_void_p, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_size_t, c_void_p]),

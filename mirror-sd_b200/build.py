@@ -17,7 +17,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libdflash_b200.so")
-SOURCES = ["quant.cu", "w8_tc.cu", "attention.cu", "attention_tc.cu", "tc_gemm.cu", "lm_head.cu", "misc.cu", "anchor.cu", "dflash_api.cu"]
+SOURCES = ["quant.cu", "w8_tc.cu", "attention.cu", "attention_tc.cu", "tc_gemm.cu", "lm_head.cu", "misc.cu", "anchor.cu",
+           "f32_path.cu", "dflash_api.cu"]
 HEADERS = ["common.cuh", "kernels.cuh"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]

@@ -83,14 +83,15 @@ struct Handle {
   uint8_t* lm_tiles = nullptr;      // lm_head packed by lm_pack_launch (128-row swizzled tiles)
   float *hidden_norm = nullptr, *norm = nullptr, *inv_freq = nullptr;
   float* k_norm_all = nullptr;     // [L, 128]
-  __nv_bfloat16* w_kv_ctx = nullptr;  // [L*2*NKV*128, H] exact bf16 of the int8 K|V weights
+  __half* w_kv_ctx = nullptr;       // [L*2*NKV*128, H] exact f16 of the int8 K|V weights
   float* s_kv_ctx = nullptr;       // [L*2*NKV*128]
   std::vector<Layer> layers;
   // workspace
   float2* rope = nullptr;
   float *h = nullptr, *hstat = nullptr;
-  float* ctx_part = nullptr;
-  __nv_bfloat16* ctx_n = nullptr;   // bf16(fc * hidden_norm weight): the context K|V GEMM's A
+  float* ctx_part = nullptr;        // per-256-column sums of squares of the fc rows [H/256, Cx]
+  float* ctx_raw = nullptr;         // fc output [Cx, H] fp32
+  __half* ctx_n = nullptr;          // hidden_norm(fc rows) in f16: the context K|V GEMM's A
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
   int8_t* xl = nullptr;             // projection input limbs [3][64][max(H, NQ*128, I)]
   float* xs = nullptr;              // their row scales [64]
@@ -117,6 +118,29 @@ struct Handle {
   size_t stateless_rows = 0;         // K/V rows per layer and kv head of the stateless store
   __half* xa = nullptr;              // dense path: normalised projection input [Mx, H] f16
   int last_launches = 0;
+  // fp32-accumulate mode (dflash_create_f32): fp32 weights, activations and sums
+  bool f32 = false;
+  struct LayerF32 {
+    float* w_qkv = nullptr;          // [(NQ + 2 NKV) * 128, H]: q rows, k rows, v rows
+    float* w_o = nullptr;            // [H, NQ * 128]
+    float* w_gu = nullptr;           // [2 I, H]: gate rows, then up rows
+    float* w_d = nullptr;            // [H, I]
+  };
+  std::vector<LayerF32> flayers;
+  float* f_fc = nullptr;             // [H, F * H]
+  float* f_lm = nullptr;             // [V, H]
+  float* f_wkv = nullptr;            // [L][2 * NKV * 128][H]: every layer's k rows then v rows
+  float *f_ctx = nullptr, *f_ctxn = nullptr;   // fc output and its hidden_norm [Cx, H]
+  float* f_kvc = nullptr;            // context K | V of the step's layers [Cx, nl * 2 * NKV * 128]
+  float *f_h = nullptr, *f_xn = nullptr;        // residual stream, normed rows [Mx, H]
+  float* f_qkv = nullptr;            // block q | k | v [Mx, (NQ + 2 NKV) * 128]
+  float* f_attn = nullptr;           // [Mx, NQ * 128]
+  float* f_act = nullptr;            // [Mx, I]
+  float* f_hn = nullptr;             // final-normed rows j >= 1 of every block [Mx, H]
+  float* f_part = nullptr;           // GEMM split partials
+  size_t f_part_floats = 0;
+  float *f_opart = nullptr, *f_mpart = nullptr, *f_lpart = nullptr;   // attention split partials
+  size_t f_attn_rows = 0;
 };
 
 // Draft KV cache (dflash.py:139-212).  Per layer and sequence the host keeps
@@ -208,6 +232,139 @@ size_t attn_rows_capacity(int max_batch, int nkv, int R, int kv_len_max, int num
     // also cover every shorter length that yields more splits (never: splits <= kv tiles)
   }
   return best;
+}
+
+constexpr int kF32MaxAttnSplits = 16;
+
+// attention split partial rows an fp32 handle needs: only steps with more
+// than one split use them
+size_t f32_attn_rows_capacity(int max_batch, int nq, int block, int num_sms) {
+  size_t best = 0;
+  for (int b = 1; b <= max_batch; ++b) {
+    int chunk, splits;
+    f32_attn_pick_split(b, nq, 1 << 28, num_sms, kF32MaxAttnSplits, &chunk, &splits);
+    if (splits > 1) best = std::max(best, (size_t)b * nq * splits * block);
+  }
+  return best;
+}
+
+// The fp32-accumulate draft step (DFlashDraftModel.__call__, dflash.py:384-403,
+// then lm_head + greedy argmax + acceptance, generate.py:604-606, :722-728),
+// stateless: sequence s attends to its C_s context rows and its block rows.
+int forward_f32(Handle* hd, const DFlashForwardArgs* a, std::vector<KvSeq>& sq, cudaStream_t st) {
+  const DFlashDims& d = hd->d;
+  const int H = d.hidden_size, I = d.intermediate_size, NQ = d.num_attention_heads,
+            NKV = d.num_key_value_heads, F = d.num_target_features;
+  const int b = a->batch, B = a->block, nl = a->num_layers;
+  const int M = b * B;
+  const int Ctot = sq[b].ctx_start;
+  if (a->cache || a->anchor_logits || a->target_layers)
+    return fail(DFLASH_ERR_INVALID, "cache, anchor_logits and target_layers are not available on an fp32 handle");
+  if (M > kMaxBlockRows) return fail(DFLASH_ERR_INVALID, "%d block rows above %d", M, kMaxBlockRows);
+  if ((reinterpret_cast<uintptr_t>(a->noise) | reinterpret_cast<uintptr_t>(a->target_hidden) |
+       reinterpret_cast<uintptr_t>(a->out_hidden)) & 15)
+    return fail(DFLASH_ERR_INVALID, "noise, target_hidden and out_hidden must be 16-byte aligned");
+  KvMap m{};
+  m.nseq = b;
+  m.seq = hd->kv_seq;
+  m.sink = 0;
+  int kvmax = 0;
+  for (int s = 0; s < b; ++s) {
+    const int off = a->rope_offsets ? a->rope_offsets[s] : a->rope_offset;
+    if (off < 0) return fail(DFLASH_ERR_INVALID, "rope offsets must be >= 0");
+    sq[s].n0 = 0; sq[s].rs_pre = 0; sq[s].rs_post = 0;
+    sq[s].n_att = sq[s + 1].ctx_start - sq[s].ctx_start + B;
+    sq[s].pos0 = off;
+    sq[s].cseq = s;
+    kvmax = std::max(kvmax, sq[s].n_att);
+  }
+  m.ring = m.slots = kvmax;
+  std::lock_guard<std::mutex> lock(hd->mu);
+  CK(cudaSetDevice(hd->device));
+  const bool timing = a->phase_events && a->n_phase_events >= DFLASH_PHASES;
+  auto mark = [&](int k) -> cudaError_t {
+    return timing ? cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[k]), st) : cudaSuccess;
+  };
+  const int sms = hd->num_sms;
+  const float eps = d.rms_norm_eps;
+  int launches = 0;
+  F32GemmParams gp{};
+  gp.part = hd->f_part; gp.part_floats = hd->f_part_floats; gp.err = hd->dev_err;
+  auto gemm = [&](const float* A, int Mr, const float* Bw, int N, int K, int mode, float* out, int ldo) {
+    F32GemmParams p = gp;
+    p.M = Mr; p.N = N; p.K = K;
+    launches += 2;
+    return f32_gemm_launch(A, Bw, mode, p, out, ldo, sms, st);
+  };
+  CK(mark(0));
+  CK(rope_table_map_launch(m, sq.data(), B, hd->inv_freq, hd->rope, st));
+  if (b + 1 > kKvChunk) launches += (b + kKvChunk) / kKvChunk;
+  CK(cudaMemcpyAsync(hd->f_h, a->noise, (size_t)M * H * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  launches += 1;
+  CK(mark(1));
+  const int nkv2 = 2 * NKV * 128;
+  const int ld_kvc = nl * nkv2;
+  if (Ctot > 0) {
+    CK(gemm(reinterpret_cast<const float*>(a->target_hidden), Ctot, hd->f_fc, H, F * H, kF32Store, hd->f_ctx, H));
+    CK(mark(2));
+    CK(f32_rmsnorm_launch(hd->f_ctx, Ctot, H, hd->hidden_norm, eps, hd->f_ctxn, nullptr, 1, st));
+    CK(mark(3));
+    CK(gemm(hd->f_ctxn, Ctot, hd->f_wkv, ld_kvc, H, kF32Store, hd->f_kvc, ld_kvc));
+    CK(f32_headnorm_launch(hd->f_kvc, Ctot, ld_kvc, 0, NKV, nl, nkv2, nullptr, hd->k_norm_all, hd->rope, 0, eps,
+                           sms, st));
+    launches += 2;
+  } else {
+    CK(mark(2));
+    CK(mark(3));
+  }
+  CK(mark(4));
+  const int nqkv = (NQ + 2 * NKV) * 128;
+  F32AttnParams ap{};
+  ap.q = hd->f_qkv; ap.q_ld = nqkv;
+  ap.c_ld = ld_kvc;
+  ap.kb = hd->f_qkv + NQ * 128; ap.vb = hd->f_qkv + (NQ + NKV) * 128; ap.b_ld = nqkv;
+  ap.seq = hd->kv_seq; ap.nseq = b; ap.block = B; ap.nq = NQ; ap.nkv = NKV;
+  f32_attn_pick_split(b, NQ, kvmax, sms, kF32MaxAttnSplits, &ap.chunk, &ap.splits);
+  if (ap.splits > 1 && (size_t)b * NQ * ap.splits * B > hd->f_attn_rows)
+    return fail(DFLASH_ERR_INVALID, "attention workspace too small");
+  ap.scale = (float)(1.0 / std::sqrt(128.0));
+  ap.opart = hd->f_opart; ap.mpart = hd->f_mpart; ap.lpart = hd->f_lpart;
+  ap.out = hd->f_attn; ap.out_ld = NQ * 128;
+  for (int l = 0; l < nl; ++l) {
+    const Layer& ly = hd->layers[l];
+    const Handle::LayerF32& fl = hd->flayers[l];
+    CK(f32_rmsnorm_launch(hd->f_h, M, H, ly.in_norm, eps, hd->f_xn, nullptr, 1, st));
+    CK(gemm(hd->f_xn, M, fl.w_qkv, nqkv, H, kF32Store, hd->f_qkv, nqkv));
+    CK(f32_headnorm_launch(hd->f_qkv, M, nqkv, NQ, NKV, 1, 0, ly.q_norm, hd->k_norm_all + l * 128, hd->rope, Ctot,
+                           eps, sms, st));
+    ap.kc = hd->f_kvc + (size_t)l * nkv2;
+    ap.vc = ap.kc + NKV * 128;
+    CK(f32_attn_launch(ap, sms, st));
+    CK(gemm(hd->f_attn, M, fl.w_o, H, NQ * 128, kF32Add, hd->f_h, H));
+    CK(f32_rmsnorm_launch(hd->f_h, M, H, ly.post_norm, eps, hd->f_xn, nullptr, 1, st));
+    CK(gemm(hd->f_xn, M, fl.w_gu, 2 * I, H, kF32Silu, hd->f_act, I));
+    CK(gemm(hd->f_act, M, fl.w_d, H, I, kF32Add, hd->f_h, H));
+    launches += 4 + (ap.splits > 1);
+  }
+  CK(mark(5));
+  const bool lm = a->out_tokens || a->target_tokens;
+  CK(f32_rmsnorm_launch(hd->f_h, M, H, hd->norm, eps, static_cast<float*>(a->out_hidden), lm ? hd->f_hn : nullptr,
+                        B, st));
+  launches += 1;
+  CK(mark(6));
+  if (lm) {
+    F32GemmParams p = gp;
+    p.M = b * (B - 1); p.N = d.vocab_size; p.K = H;
+    p.best_val = hd->lm_val; p.best_idx = hd->lm_idx;
+    CK(f32_gemm_launch(hd->f_hn, hd->f_lm, kF32Argmax, p, nullptr, 0, sms, st));
+    const int parts = (d.vocab_size + 127) / 128;
+    CK(argmax_accept_launch(hd->lm_val, hd->lm_idx, parts, b * (B - 1), B, b, a->out_tokens, a->target_tokens,
+                            a->acc_len, a->correction, st, 1));
+    launches += 2;
+  }
+  CK(mark(7));
+  hd->last_launches = launches;
+  return DFLASH_OK;
 }
 
 }  // namespace
@@ -314,10 +471,10 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(cudaMemcpyAsync(ly.post_norm, lw.post_attention_layernorm, H * 4, cudaMemcpyDeviceToDevice, st));
     CKC(cudaMemcpyAsync(ly.q_norm, lw.q_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
     CKC(cudaMemcpyAsync(hd->k_norm_all + l * 128, lw.k_norm, 128 * 4, cudaMemcpyDeviceToDevice, st));
-    // context K|V operand: exact bf16 of the int8 values, scales applied in the epilogue
-    __nv_bfloat16* kv = hd->w_kv_ctx + (size_t)l * nkvc * H;
-    CKC(i8_to_bf16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
-    CKC(i8_to_bf16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
+    // context K|V operand: exact f16 of the int8 values, scales applied in the epilogue
+    __half* kv = hd->w_kv_ctx + (size_t)l * nkvc * H;
+    CKC(i8_to_f16_launch(lw.wk, (size_t)NKV * 128 * H, kv, st));
+    CKC(i8_to_f16_launch(lw.wv, (size_t)NKV * 128 * H, kv + (size_t)NKV * 128 * H, st));
     CKC(w8_scale_launch((const __half*)lw.sk, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, 0, st));
     CKC(w8_scale_launch((const __half*)lw.sv, NKV * 128, hd->s_kv_ctx + (size_t)l * nkvc, big, 0, NKV * 128, st));
     if ((long long)d.max_batch * d.max_block > kW8Rows) {
@@ -348,6 +505,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->hstat, (size_t)(H / 128) * Mx));
   if (Cx > 0) {
     CKC(A.alloc(&hd->ctx_part, (size_t)(H / 256) * Cx));
+    CKC(A.alloc(&hd->ctx_raw, (size_t)Cx * H));
     CKC(A.alloc(&hd->ctx_n, (size_t)Cx * H));
   }
   const size_t kv_elems = (size_t)L * NKV * hd->stateless_rows * 128;
@@ -400,6 +558,131 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
     CKC(cudaMemset(hd->tc_cnt, 0, (size_t)hd->num_sms * sizeof(int)));
     CKC(cudaMemset(hd->sa_cnt, 0, (size_t)d.max_batch * sizeof(int)));
   }
+  CKC(cudaDeviceSynchronize());
+#undef CKC
+  *out = hd;
+  return DFLASH_OK;
+}
+
+int dflash_create_f32(const DFlashDims* dims, const DFlashWeightsViewF32* w, int device, void** out) {
+  if (int r = check_dims(dims)) return r;
+  if (!w || !out || !w->fc || !w->hidden_norm || !w->norm || !w->lm_head || !w->layers)
+    return fail(DFLASH_ERR_INVALID, "weights view has NULL members");
+  const DFlashDims d = *dims;
+  const int H = d.hidden_size, I = d.intermediate_size, NQ = d.num_attention_heads,
+            NKV = d.num_key_value_heads, L = d.num_hidden_layers, F = d.num_target_features, V = d.vocab_size;
+  for (int l = 0; l < L; ++l) {
+    const DFlashLayerWeightsF32& lw = w->layers[l];
+    if (!lw.wq || !lw.wk || !lw.wv || !lw.wo || !lw.wg || !lw.wu || !lw.wd || !lw.input_layernorm ||
+        !lw.post_attention_layernorm || !lw.q_norm || !lw.k_norm)
+      return fail(DFLASH_ERR_INVALID, "layer %d has NULL weight pointers", l);
+  }
+  CK(cudaSetDevice(device));
+  Handle* hd = new Handle();
+  hd->device = device;
+  hd->d = d;
+  hd->f32 = true;
+  int rc = DFLASH_OK;
+  auto cleanup = [&]() {
+    cudaDeviceSynchronize();
+    hd->arena.release();
+    delete hd;
+  };
+#define CKC(call)                                                                                    \
+  do {                                                                                               \
+    cudaError_t e_ = (call);                                                                         \
+    if (e_ != cudaSuccess) {                                                                         \
+      rc = fail(e_ == cudaErrorMemoryAllocation ? DFLASH_ERR_OOM : DFLASH_ERR_CUDA, "%s: %s", #call, \
+                cudaGetErrorString(e_));                                                             \
+      cleanup();                                                                                     \
+      return rc;                                                                                     \
+    }                                                                                                \
+  } while (0)
+  CKC(cudaDeviceGetAttribute(&hd->num_sms, cudaDevAttrMultiProcessorCount, device));
+  Arena& A = hd->arena;
+  cudaStream_t st = 0;
+  auto copy = [&](float* dst, const float* src, size_t n) {
+    return cudaMemcpyAsync(dst, src, n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+  };
+  const size_t nqkv = (size_t)(NQ + 2 * NKV) * 128, nkv1 = (size_t)NKV * 128;
+  CKC(A.alloc(&hd->f_fc, (size_t)H * F * H));
+  CKC(copy(hd->f_fc, w->fc, (size_t)H * F * H));
+  CKC(A.alloc(&hd->f_lm, (size_t)V * H));
+  CKC(copy(hd->f_lm, w->lm_head, (size_t)V * H));
+  CKC(A.alloc(&hd->hidden_norm, H));
+  CKC(A.alloc(&hd->norm, H));
+  CKC(copy(hd->hidden_norm, w->hidden_norm, H));
+  CKC(copy(hd->norm, w->norm, H));
+  {
+    std::vector<float> inv(64);
+    for (int i = 0; i < 64; ++i) inv[i] = (float)std::pow((double)d.rope_theta, -2.0 * i / 128.0);
+    CKC(A.alloc(&hd->inv_freq, 64));
+    CKC(cudaMemcpy(hd->inv_freq, inv.data(), 64 * 4, cudaMemcpyHostToDevice));
+  }
+  CKC(A.alloc(&hd->k_norm_all, (size_t)L * 128));
+  CKC(A.alloc(&hd->f_wkv, (size_t)L * 2 * nkv1 * H));
+  for (int l = 0; l < L; ++l) {
+    const DFlashLayerWeightsF32& lw = w->layers[l];
+    Handle::LayerF32 fl;
+    CKC(A.alloc(&fl.w_qkv, nqkv * H));
+    CKC(copy(fl.w_qkv, lw.wq, (size_t)NQ * 128 * H));
+    CKC(copy(fl.w_qkv + (size_t)NQ * 128 * H, lw.wk, nkv1 * H));
+    CKC(copy(fl.w_qkv + (size_t)(NQ + NKV) * 128 * H, lw.wv, nkv1 * H));
+    CKC(A.alloc(&fl.w_o, (size_t)H * NQ * 128));
+    CKC(copy(fl.w_o, lw.wo, (size_t)H * NQ * 128));
+    CKC(A.alloc(&fl.w_gu, (size_t)2 * I * H));
+    CKC(copy(fl.w_gu, lw.wg, (size_t)I * H));
+    CKC(copy(fl.w_gu + (size_t)I * H, lw.wu, (size_t)I * H));
+    CKC(A.alloc(&fl.w_d, (size_t)H * I));
+    CKC(copy(fl.w_d, lw.wd, (size_t)H * I));
+    float* kv = hd->f_wkv + (size_t)l * 2 * nkv1 * H;
+    CKC(copy(kv, lw.wk, nkv1 * H));
+    CKC(copy(kv + nkv1 * H, lw.wv, nkv1 * H));
+    Layer ly{};
+    CKC(A.alloc(&ly.in_norm, H));
+    CKC(A.alloc(&ly.post_norm, H));
+    CKC(A.alloc(&ly.q_norm, 128));
+    CKC(copy(ly.in_norm, lw.input_layernorm, H));
+    CKC(copy(ly.post_norm, lw.post_attention_layernorm, H));
+    CKC(copy(ly.q_norm, lw.q_norm, 128));
+    CKC(copy(hd->k_norm_all + l * 128, lw.k_norm, 128));
+    hd->layers.push_back(ly);
+    hd->flayers.push_back(fl);
+  }
+  // ---- workspace
+  const int Mx = d.max_batch * d.max_block;
+  const int Cx = ctx_rows_capacity(d);
+  CKC(A.alloc(&hd->rope, (size_t)(Cx + Mx) * 64));
+  if (Cx > 0) {
+    CKC(A.alloc(&hd->f_ctx, (size_t)Cx * H));
+    CKC(A.alloc(&hd->f_ctxn, (size_t)Cx * H));
+    CKC(A.alloc(&hd->f_kvc, (size_t)Cx * L * 2 * nkv1));
+  }
+  CKC(A.alloc(&hd->f_h, (size_t)Mx * H));
+  CKC(A.alloc(&hd->f_xn, (size_t)Mx * H));
+  CKC(A.alloc(&hd->f_qkv, (size_t)Mx * nqkv));
+  CKC(A.alloc(&hd->f_attn, (size_t)Mx * NQ * 128));
+  CKC(A.alloc(&hd->f_act, (size_t)Mx * I));
+  CKC(A.alloc(&hd->f_hn, (size_t)Mx * H));
+  {
+    // split partials: every GEMM of a step fits unsplit, and small ones may split
+    size_t need = std::max({(size_t)Cx * H, (size_t)Cx * L * 2 * nkv1, (size_t)Mx * nqkv, (size_t)Mx * 2 * I,
+                            (size_t)Mx * H});
+    hd->f_part_floats = std::max(need, (size_t)8 << 20);
+    CKC(A.alloc(&hd->f_part, hd->f_part_floats));
+  }
+  hd->f_attn_rows = f32_attn_rows_capacity(d.max_batch, NQ, d.max_block, hd->num_sms);
+  if (hd->f_attn_rows > 0) {
+    CKC(A.alloc(&hd->f_opart, hd->f_attn_rows * 128));
+    CKC(A.alloc(&hd->f_mpart, hd->f_attn_rows));
+    CKC(A.alloc(&hd->f_lpart, hd->f_attn_rows));
+  }
+  const size_t lm_parts = (size_t)(V + 127) / 128;
+  CKC(A.alloc(&hd->lm_val, lm_parts * Mx));
+  CKC(A.alloc(&hd->lm_idx, lm_parts * Mx));
+  CKC(A.alloc(&hd->kv_seq, (size_t)d.max_batch + 1));
+  CKC(A.alloc(&hd->dev_err, 1));
+  CKC(cudaMemset(hd->dev_err, 0, sizeof(int)));
   CKC(cudaDeviceSynchronize());
 #undef CKC
   *out = hd;
@@ -491,6 +774,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   }
   if (a->target_tokens && (!a->acc_len || !a->correction))
     return fail(DFLASH_ERR_INVALID, "acc_len and correction are required with target_tokens");
+  if (hd->f32) return forward_f32(hd, a, sq, static_cast<cudaStream_t>(stream));
   const int top_k = a->anchor_top_k ? a->anchor_top_k : 8;
   const long long anchor_ld = a->anchor_logits_ld ? a->anchor_logits_ld : d.vocab_size;
   if (a->anchor_logits && (top_k < 1 || top_k > kSaMaxK || top_k > d.vocab_size))
@@ -611,12 +895,15 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     TcParams fp{};
     fp.tail_part = hd->tc_part; fp.tail_cnt = hd->tc_cnt; fp.tail_cap = hd->tc_cap;
     fp.M = Ctot; fp.N = H; fp.K = F * H; fp.err = hd->dev_err;
-    // hidden_norm (dflash.py:392) is split over the two GEMMs: the fc epilogue
-    // stores f16(fc * w) with per-row sums of squares, and the context K|V
-    // GEMM scales each row by its 1/rms
-    fp.out_b16 = hd->ctx_n; fp.colw = hd->hidden_norm; fp.sumsq_part = hd->ctx_part;
+    // hidden_norm (dflash.py:392): the fc epilogue stores the fp32 rows with
+    // per-256-column sums of squares; ctx_norm rounds the normalised rows to
+    // f16 (11 mantissa bits, and no overflow once normalised), the context
+    // K|V GEMM's A operand
+    fp.out_f32 = hd->ctx_raw; fp.sumsq_part = hd->ctx_part;
     CK(tc_gemm_launch_src(fc_src, hd->fc, true, kTcFc, fp, st));
     CK(mark(2));
+    CK(ctx_norm_launch(hd->ctx_raw, hd->ctx_part, H / 256, Ctot, H, hd->hidden_norm, d.rms_norm_eps, hd->ctx_n,
+                       st));
     CK(mark(3));
     TcParams kp{};
     kp.tail_part = hd->tc_part; kp.tail_cnt = hd->tc_cnt; kp.tail_cap = hd->tc_cap;
@@ -624,10 +911,9 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
     kp.scale = hd->s_kv_ctx; kp.k_norm = hd->k_norm_all; kp.rope = hd->rope;
     kp.k_out = Kbase; kp.v_out = Vbase; kp.layer_stride = layer_stride;
     kp.nkv = NKV; kp.eps = d.rms_norm_eps; kp.kv = m;
-    kp.row_sumsq = hd->ctx_part; kp.row_parts = H / 256; kp.row_dim = H;
-    CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, true, kTcCtxKV, kp, st));
+    CK(tc_gemm_launch(hd->ctx_n, hd->w_kv_ctx, false, kTcCtxKV, kp, st));
     CK(mark(4));
-    launches += 2;   // fc (+ hidden_norm's f16 half), context K|V (+ its 1/rms)
+    launches += 3;   // fc, hidden_norm, context K|V
   } else {
     CK(mark(2));
     CK(mark(3));
@@ -1056,7 +1342,6 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
   p.mpart = p.opart + rows * 128;
   p.lpart = p.mpart + rows;
   float2* rope = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(p.lpart + rows) + 15) & ~uintptr_t(15));
-  float* inv = reinterpret_cast<float*>(rope + (size_t)(kv_len + block) * 64);
   p.q = reinterpret_cast<const __half*>(q);
   p.k = reinterpret_cast<const __half*>(k);
   p.v = reinterpret_cast<const __half*>(v);
@@ -1069,10 +1354,7 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
     const int maxpos = std::max(q_pos0 + block, k_pos0 + kv_len);
     if ((size_t)maxpos > (size_t)(kv_len + block))
       return fail(DFLASH_ERR_INVALID, "positions must lie below kv_len + block");
-    std::vector<float> invh(64);
-    for (int i = 0; i < 64; ++i) invh[i] = (float)std::pow((double)rope_theta, -2.0 * i / 128.0);
-    CK(cudaMemcpyAsync(inv, invh.data(), 64 * 4, cudaMemcpyHostToDevice, st));
-    CK(rope_table_launch(0, kv_len + block, inv, rope, st));
+    CK(rope_table_launch(0, kv_len + block, rope_theta, rope, st));
     p.q_norm = q_norm; p.k_norm = k_norm; p.rope = rope; p.eps = eps;
     p.q_row0 = q_pos0; p.k_row0 = k_pos0;
   }
@@ -1117,11 +1399,14 @@ int dflash_soft_anchor(const void* logits, int logits_bf16, int batch, int V, in
   return DFLASH_OK;
 }
 
-size_t dflash_lm_head_workspace_size(int batch, int block) {
+// workspace: per-CTA (max, index) partials, the error word, then E repacked
+// into the lm_head's 128-row swizzled tiles (1024-byte aligned)
+size_t dflash_lm_head_workspace_size(int batch, int block, int V, int H) {
+  if (batch < 1 || block < 1 || V < 1 || H < 1) return 0;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return (size_t)sms * batch * block * 8 + 256;
+  return (size_t)sms * batch * block * 8 + 256 + 1024 + lm_pack_bytes(V, H);
 }
 
 int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int block, int H, int V,
@@ -1131,32 +1416,27 @@ int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int 
   if (batch < 1 || block < 2 || batch * block > 64 || H % 64 || V < 1)
     return fail(DFLASH_ERR_INVALID, "bad lm_head shape");
   if (target && (!acc_len || !correction)) return fail(DFLASH_ERR_INVALID, "acc_len/correction required");
-  if (ws_bytes < dflash_lm_head_workspace_size(batch, block))
-    return fail(DFLASH_ERR_INVALID, "workspace too small");
+  if (ws_bytes < dflash_lm_head_workspace_size(batch, block, V, H))
+    return fail(DFLASH_ERR_INVALID, "workspace too small (%zu < %zu)", ws_bytes,
+                dflash_lm_head_workspace_size(batch, block, V, H));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int M = batch * block;
-  uint8_t* et = nullptr;
-  int* err = nullptr;
-  CK(cudaMallocAsync(&et, lm_pack_bytes(V, H), st));
-  CK(cudaMallocAsync(&err, sizeof(int), st));
-  CK(cudaMemsetAsync(err, 0, sizeof(int), st));
-  CK(lm_pack_launch(reinterpret_cast<const __nv_bfloat16*>(E), V, H, et, st));
   LmParams p{};
   p.hn = reinterpret_cast<const __nv_bfloat16*>(hn);
   p.V = V; p.H = H; p.M = M;
   p.best_val = static_cast<float*>(workspace);
   p.best_idx = reinterpret_cast<int*>(p.best_val + (size_t)sms * M);
+  int* err = p.best_idx + (size_t)sms * M;
+  uint8_t* et = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(err + 1) + 1023) & ~uintptr_t(1023));
+  CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+  CK(lm_pack_launch(reinterpret_cast<const __nv_bfloat16*>(E), V, H, et, st));
   int grid = 0;
-  cudaError_t e = lm_argmax_launch(p, et, sms, err, &grid, st);
-  if (e == cudaSuccess)
-    e = argmax_accept_launch(p.best_val, p.best_idx, grid, M, block, batch, tokens, target, acc_len,
-                             correction, st);
-  cudaFreeAsync(et, st);
-  cudaFreeAsync(err, st);
-  CK(e);
+  CK(lm_argmax_launch(p, et, sms, err, &grid, st));
+  CK(argmax_accept_launch(p.best_val, p.best_idx, grid, M, block, batch, tokens, target, acc_len, correction,
+                          st));
   return DFLASH_OK;
 }
 
@@ -1171,33 +1451,24 @@ int dflash_lm_head_argmax(const uint16_t* hn, const uint16_t* E, int batch, int 
 // device that loads the library, held until the process exits.
 //
 // `g_attn_scratch` is a host-side stand-in for the array.  The device address
-// comes from cudaGetSymbolAddress, looked up on a device's first call while
-// that device is current.  Calls on a device share the array, so calls that
-// overlap on the GPU race.  The array keeps the last call's contents.  The
-// partial kernel writes every (split, row) partial and the table rows it reads
-// before anything reads them, so nothing needs clearing between calls.
+// comes from cudaGetSymbolAddress, looked up on every call with the caller's
+// device current: after a cudaDeviceReset the library's device code is loaded
+// again, possibly at another address, so a cached address could go stale.  The
+// lookup is cheap once the code is loaded on the device; the first call on a
+// device loads it, so make that first call outside any stream capture.  Calls
+// on a device share the array, so calls that overlap on the GPU race.  The
+// array keeps the last call's contents.  The partial kernel writes every
+// (split, row) partial and the table rows it reads before anything reads them,
+// so nothing needs clearing between calls.
 
 static __device__ __align__(256) unsigned char g_attn_scratch[DFLASH_ATTN_STATIC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kScratchMaxDevices = 64;
-std::mutex g_scratch_mu;
-void* g_scratch_dev[kScratchMaxDevices] = {};
-
-// device address of g_attn_scratch on the current device, looked up once
+// device address of g_attn_scratch on the current device
 int attn_scratch_ptr(void** out) {
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= kScratchMaxDevices)
-    return fail(DFLASH_ERR_INVALID, "device ordinal %d beyond the %d supported", dev,
-                kScratchMaxDevices);
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_dev[dev]) {
-    void* p = nullptr;
-    CK(cudaGetSymbolAddress(&p, g_attn_scratch));
-    g_scratch_dev[dev] = p;
-  }
-  *out = g_scratch_dev[dev];
+  void* p = nullptr;
+  CK(cudaGetSymbolAddress(&p, g_attn_scratch));
+  *out = p;
   return DFLASH_OK;
 }
 }  // namespace

@@ -287,7 +287,8 @@ struct SaParams {
 };
 int soft_anchor_ctas(int V, int rows, int num_sms);
 cudaError_t soft_anchor_launch(const SaParams& p, int rows, bool e_tiled, int num_sms, cudaStream_t st);
-cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st);
+// (cos, sin) rows for positions pos0 .. pos0 + rows - 1, inv_freq from theta on the device
+cudaError_t rope_table_launch(int pos0, int rows, float theta, float2* out, cudaStream_t st);
 // table rows of one forward: packed context rows, then nseq * block block rows.
 // Also stores the map's records (host array `seq`, nseq + 1 entries) at m.seq.
 cudaError_t rope_table_map_launch(const KvMap& m, const KvSeq* seq, int block, const float* inv_freq,
@@ -308,4 +309,49 @@ cudaError_t i8_to_f16_rows_launch(const int8_t* src, int rows, int K, __half* ds
 cudaError_t bounded_wait_probe_launch(uint32_t polls, int* err, cudaStream_t st);
 cudaError_t i8_to_bf16_launch(const int8_t* src, size_t n, __nv_bfloat16* dst, cudaStream_t st);
 cudaError_t i8_to_f16_launch(const int8_t* src, size_t n, __half* dst, cudaStream_t st);
+
+// ---- fp32-accumulate path (f32_path.cu): fp32 weights and activations on the
+// CUDA cores.  GEMM epilogues (after the ordered split-K sum):
+//   kF32Store  : out = A . B^T
+//   kF32Add    : out += A . B^T (the residual stream)
+//   kF32Silu   : B holds the gate rows then the up rows; out = silu(g) * u
+//   kF32Argmax : per-row (max, first index) over each 128-column tile into
+//                best_val / best_idx [N tiles][M] (no split, no partials)
+enum F32Mode : int { kF32Store = 0, kF32Add = 1, kF32Silu = 2, kF32Argmax = 3 };
+
+struct F32GemmParams {
+  int M, N, K;          // A [M, K], B [N, K] fp32 row-major; K % 64 == 0
+  float* part;          // split-K partials [S][M][N]
+  size_t part_floats;
+  float* best_val;      // kF32Argmax
+  int* best_idx;
+  int* err;             // device error word for bounded waits
+};
+
+struct F32AttnParams {
+  const float* q; int q_ld;               // block row m, head h at q + m * q_ld + h * 128
+  const float* kc; const float* vc; int c_ld;   // context rows (packed), kv head hk at + hk * 128
+  const float* kb; const float* vb; int b_ld;   // block rows
+  const KvSeq* seq;                       // device records: ctx_start of each sequence (+ total)
+  int nseq, block, nq, nkv;
+  int chunk, splits;                      // keys per split (a multiple of 32), splits
+  float scale;                            // head_dim^-0.5
+  float *opart, *mpart, *lpart;           // [nseq][nq][splits][block] (x 128 for opart)
+  float* out; int out_ld;                 // [M, NQ * 128]
+};
+
+int f32_gemm_splits(int M, int N, int K, int num_sms, size_t part_floats);
+// the GEMM (+ the split reduction and epilogue into out[M, ldo], except kF32Argmax)
+cudaError_t f32_gemm_launch(const float* A, const float* B, int mode, F32GemmParams p, float* out, int ldo,
+                            int num_sms, cudaStream_t st);
+// y = rms_norm(x) (if y); y2 = its rows j >= 1 of every block, packed (if y2)
+cudaError_t f32_rmsnorm_launch(const float* x, int rows, int H, const float* w, float eps, float* y, float* y2,
+                               int block, cudaStream_t st);
+// per-head RMSNorm + neox RoPE in place: heads [0, nq) with wq, [nq, nq + nk) with
+// wk (+ plane * 128), in `planes` column planes plane_cols apart; table row rope_row0 + row
+cudaError_t f32_headnorm_launch(float* x, int rows, int ld, int nq, int nk, int planes, int plane_cols,
+                                const float* wq, const float* wk, const float2* rope, int rope_row0, float eps,
+                                int num_sms, cudaStream_t st);
+void f32_attn_pick_split(int nseq, int nq, int kv_len_max, int num_sms, int max_splits, int* chunk, int* splits);
+cudaError_t f32_attn_launch(const F32AttnParams& p, int num_sms, cudaStream_t st);
 }  // namespace dfl

@@ -13,12 +13,15 @@
 
 namespace dfl {
 
-__global__ void rope_table_kernel(int pos0, int rows, const float* __restrict__ inv_freq,
-                                  float2* __restrict__ out) {
+// inv_freq_i = theta^(-2i/128) is evaluated here in fp64 and rounded to fp32
+// (the same rounding as the handle's table, which the host computes once), so
+// the launch reads nothing from the host and can be captured in a graph
+__global__ void rope_table_kernel(int pos0, int rows, float theta, float2* __restrict__ out) {
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * 64) return;
   const int r = idx >> 6, i = idx & 63;
-  const float ang = static_cast<float>(pos0 + r) * inv_freq[i];
+  const float inv = static_cast<float>(pow(static_cast<double>(theta), -2.0 * i / 128.0));
+  const float ang = static_cast<float>(pos0 + r) * inv;
   float s, c;
   sincosf(ang, &s, &c);
   out[idx] = make_float2(c, s);
@@ -235,10 +238,10 @@ __global__ void i8_to_f16_rows_kernel(const int8_t* __restrict__ src, int rows, 
   }
 }
 
-cudaError_t rope_table_launch(int pos0, int rows, const float* inv_freq, float2* out, cudaStream_t st) {
+cudaError_t rope_table_launch(int pos0, int rows, float theta, float2* out, cudaStream_t st) {
   if (rows < 1) return cudaSuccess;
   DFL_TRY(max_smem_carveout(rope_table_kernel));
-  rope_table_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(pos0, rows, inv_freq, out);
+  rope_table_kernel<<<(rows * 64 + 255) / 256, 256, 0, st>>>(pos0, rows, theta, out);
   return cudaGetLastError();
 }
 

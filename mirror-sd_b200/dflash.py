@@ -163,6 +163,38 @@ class DFlashWeightsQ8:
     layers: List[Q8Layer]
 
 
+@dataclass
+class F32Layer:
+    """One decoder layer in fp32: name -> [out, in] fp32 tensor for each of
+    PROJ, plus the four norm weights."""
+    w: dict
+    input_layernorm: torch.Tensor
+    post_attention_layernorm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+@dataclass
+class DFlashWeightsF32:
+    """fp32 weights for the fp32-accumulate mode (a checkpoint stored in fp32,
+    or a W8A16 one dequantised exactly with ``from_q8``)."""
+    fc: torch.Tensor             # fp32 [H, F*H]
+    hidden_norm: torch.Tensor    # fp32 [H]
+    norm: torch.Tensor           # fp32 [H]
+    layers: List[F32Layer]
+
+    @staticmethod
+    def from_q8(w: "DFlashWeightsQ8") -> "DFlashWeightsF32":
+        """Exact fp32 copies of W8A16 weights: q * fp16(s) per output channel
+        (both factors are exact in fp32, and so is their product)."""
+        layers = [F32Layer(w={k: l.q[k].float() * l.s[k].float()[:, None] for k in PROJ},
+                           input_layernorm=l.input_layernorm.float(),
+                           post_attention_layernorm=l.post_attention_layernorm.float(),
+                           q_norm=l.q_norm.float(), k_norm=l.k_norm.float()) for l in w.layers]
+        return DFlashWeightsF32(fc=w.fc.float(), hidden_norm=w.hidden_norm.float(), norm=w.norm.float(),
+                                layers=layers)
+
+
 def quantize_q8(w: torch.Tensor):
     """Symmetric per-output-channel int8 with fp16 scales on the GPU, bit-exact
     with ``ANEDraftModel._quantize_weight_q8`` (ane_model.py:265-279).
@@ -327,9 +359,14 @@ class DFlashDraftModel:
     context rows of one step over all sequences (0: max_batch * max_ctx).
     Above 64 block rows per step the projections run as dense tensor-core
     GEMMs over f16 copies of the int8 weights (twice their memory).
+
+    With ``DFlashWeightsF32`` weights (and an fp32 ``lm_head``) the model runs
+    in fp32-accumulate mode: fp32 weights, activations and sums on the CUDA
+    cores, inputs taken as fp32, hidden states returned in fp32.  That mode
+    is stateless (no cache, soft anchor or in-place target layers).
     """
 
-    def __init__(self, config: DFlashConfig, weights: DFlashWeightsQ8, lm_head: torch.Tensor,
+    def __init__(self, config: DFlashConfig, weights, lm_head: torch.Tensor,
                  max_batch: int = 1, max_ctx: int = 4096, max_block: Optional[int] = None,
                  device=None, max_ctx_rows: int = 0):
         self.config = config
@@ -340,7 +377,9 @@ class DFlashDraftModel:
         if self.device.type != "cuda":
             raise ValueError("DFlashDraftModel runs on a CUDA device only")
         self._lib = N.load()
-        self._lm_head = lm_head.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        self.fp32 = isinstance(weights, DFlashWeightsF32)
+        self._act_dtype = torch.float32 if self.fp32 else torch.bfloat16
+        self._lm_head = lm_head.to(device=self.device, dtype=self._act_dtype).contiguous()
         self._weights = weights
         H, F = config.hidden_size, len(config.target_layer_ids)
         if tuple(weights.fc.shape) != (H, F * H):
@@ -366,25 +405,46 @@ class DFlashDraftModel:
             keep.append(t)
             return t.data_ptr()
 
-        layers = (N.DFlashLayerWeights * config.num_hidden_layers)()
-        for i, lw in enumerate(weights.layers):
-            L = layers[i]
-            for name in PROJ:
-                setattr(L, name, dev(lw.q[name], torch.int8))
-                setattr(L, "s" + name[1], dev(lw.s[name], torch.float16))
-            L.input_layernorm = dev(lw.input_layernorm, torch.float32)
-            L.post_attention_layernorm = dev(lw.post_attention_layernorm, torch.float32)
-            L.q_norm = dev(lw.q_norm, torch.float32)
-            L.k_norm = dev(lw.k_norm, torch.float32)
-        view = N.DFlashWeightsView(fc=dev(weights.fc, torch.bfloat16),
-                                   hidden_norm=dev(weights.hidden_norm, torch.float32),
-                                   norm=dev(weights.norm, torch.float32),
-                                   lm_head=self._lm_head.data_ptr(), layers=layers)
+        if len(weights.layers) != config.num_hidden_layers:
+            raise ValueError(f"{len(weights.layers)} layers of weights for {config.num_hidden_layers} layers")
         handle = ctypes.c_void_p()
-        torch.cuda.synchronize(self.device)
-        N.check(self._lib.dflash_create(ctypes.byref(dims), ctypes.byref(view),
-                                        self.device.index or 0, ctypes.byref(handle)),
-                "dflash_create")
+        if self.fp32:
+            layers = (N.DFlashLayerWeightsF32 * config.num_hidden_layers)()
+            for i, lw in enumerate(weights.layers):
+                L = layers[i]
+                for name in PROJ:
+                    setattr(L, name, dev(lw.w[name], torch.float32))
+                L.input_layernorm = dev(lw.input_layernorm, torch.float32)
+                L.post_attention_layernorm = dev(lw.post_attention_layernorm, torch.float32)
+                L.q_norm = dev(lw.q_norm, torch.float32)
+                L.k_norm = dev(lw.k_norm, torch.float32)
+            view = N.DFlashWeightsViewF32(fc=dev(weights.fc, torch.float32),
+                                          hidden_norm=dev(weights.hidden_norm, torch.float32),
+                                          norm=dev(weights.norm, torch.float32),
+                                          lm_head=self._lm_head.data_ptr(), layers=layers)
+            torch.cuda.synchronize(self.device)
+            N.check(self._lib.dflash_create_f32(ctypes.byref(dims), ctypes.byref(view),
+                                                self.device.index or 0, ctypes.byref(handle)),
+                    "dflash_create_f32")
+        else:
+            layers = (N.DFlashLayerWeights * config.num_hidden_layers)()
+            for i, lw in enumerate(weights.layers):
+                L = layers[i]
+                for name in PROJ:
+                    setattr(L, name, dev(lw.q[name], torch.int8))
+                    setattr(L, "s" + name[1], dev(lw.s[name], torch.float16))
+                L.input_layernorm = dev(lw.input_layernorm, torch.float32)
+                L.post_attention_layernorm = dev(lw.post_attention_layernorm, torch.float32)
+                L.q_norm = dev(lw.q_norm, torch.float32)
+                L.k_norm = dev(lw.k_norm, torch.float32)
+            view = N.DFlashWeightsView(fc=dev(weights.fc, torch.bfloat16),
+                                       hidden_norm=dev(weights.hidden_norm, torch.float32),
+                                       norm=dev(weights.norm, torch.float32),
+                                       lm_head=self._lm_head.data_ptr(), layers=layers)
+            torch.cuda.synchronize(self.device)
+            N.check(self._lib.dflash_create(ctypes.byref(dims), ctypes.byref(view),
+                                            self.device.index or 0, ctypes.byref(handle)),
+                    "dflash_create")
         self._handle = handle
         # ANE-style split API state
         self._pending = None
@@ -486,12 +546,16 @@ class DFlashDraftModel:
         sequences of this step reads and extends (distinct indices below the
         cache's max_batch), so a step may cover any subset of the cache's
         sequences; default 0..b-1."""
-        noise = self._as_dev(noise_embedding, torch.bfloat16)
+        noise = self._as_dev(noise_embedding, self._act_dtype)
         if noise.dim() != 3:
             raise ValueError("noise_embedding [b, q, H] expected")
         b, q, H = noise.shape
         F = len(self.config.target_layer_ids)
         layers = None
+        if self.fp32 and (isinstance(target_hidden, (list, tuple)) or cache is not None
+                          or anchor_logits is not None):
+            raise ValueError("the fp32-accumulate mode is stateless: no cache, anchor_logits or "
+                             "in-place target layers")
         if isinstance(target_hidden, (list, tuple)):
             # the F selected target layers, each [b, ctx, H] (or packed rows
             # with ctx_lens): the fc GEMM reads them in place
@@ -506,7 +570,7 @@ class DFlashDraftModel:
             rows = layers[0].shape[0]
             src_shape = tuple(target_hidden[0].shape)
         else:
-            th = self._as_dev(target_hidden, torch.bfloat16)
+            th = self._as_dev(target_hidden, self._act_dtype)
             if th.shape[-1] != F * H:
                 raise ValueError("hidden size mismatch")
             rows = th.reshape(-1, th.shape[-1]).shape[0]
@@ -538,11 +602,15 @@ class DFlashDraftModel:
             store = getattr(cache, "store", None)
             if not isinstance(store, _CacheStore):
                 raise ValueError("cache must come from this model's make_cache()")
+        if self.fp32:
+            hidden_fp32 = True
         if want_hidden and out_hidden is None:
             out_hidden = torch.empty((b, q, H), dtype=torch.float32 if hidden_fp32 else torch.bfloat16,
                                      device=self.device)
         if out_hidden is not None:
             hidden_fp32 = out_hidden.dtype == torch.float32
+            if self.fp32 and not hidden_fp32:
+                raise ValueError("an fp32-accumulate model writes fp32 hidden states")
         if (want_tokens or target_tokens is not None) and out_tokens is None:
             out_tokens = torch.empty((b, q - 1), dtype=torch.int32, device=self.device)
         al = None
@@ -603,7 +671,7 @@ class DFlashDraftModel:
 
     def __call__(self, noise_embedding, target_hidden, mask=None, cache=None, **kwargs):
         """``DFlashDraftModel.__call__`` (dflash.py:384-403): returns the
-        final-normed hidden states [b, q, H] (bf16)."""
+        final-normed hidden states [b, q, H] (bf16; fp32 in fp32-accumulate mode)."""
         if mask is not None:
             raise ValueError("the DFlash draft attention is non-causal; mask must be None")
         hidden, _, _, _ = self.draft_step(noise_embedding, target_hidden, cache=cache,

@@ -66,7 +66,7 @@ def lm_head_argmax(hn, E, target=None, workspace=None):
     V = E.shape[0]
     hn, E = hn.to(torch.bfloat16).contiguous(), E.to(torch.bfloat16).contiguous()
     toks = torch.empty((b, blk - 1), dtype=torch.int32, device=hn.device)
-    need = lib.dflash_lm_head_workspace_size(b, blk)
+    need = lib.dflash_lm_head_workspace_size(b, blk, V, H)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty((need,), dtype=torch.uint8, device=hn.device)
     acc = cor = tt = None

@@ -6,7 +6,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .dflash import PROJ, DFlashConfig, DFlashWeightsQ8, Q8Layer, quantize_q8
+from .dflash import PROJ, DFlashConfig, DFlashWeightsF32, DFlashWeightsQ8, F32Layer, Q8Layer, quantize_q8
 
 
 def weights_from_q8_numpy(q8: dict, device) -> DFlashWeightsQ8:
@@ -65,3 +65,34 @@ def synth_weights_q8(cfg: DFlashConfig, seed: int = 0, device="cuda", std: float
         lm[i:j] = randn(j - i, H).to(torch.bfloat16)
     w = DFlashWeightsQ8(fc=fc, hidden_norm=norm_w(H), norm=norm_w(H), layers=layers)
     return w, lm
+
+
+@torch.no_grad()
+def synth_weights_f32(cfg: DFlashConfig, seed: int = 0, device="cuda", std: float = 0.02,
+                      random_norms: bool = False, num_target_features: int = 5):
+    """Seeded fp32 N(0, std) weights of the given dims for the fp32-accumulate
+    mode (the CPU plumbing config: every weight fp32 N(0, 0.02), norm weights
+    ones or 1 + N(0, 0.1) with random_norms), generated on the GPU.
+    Returns ``(DFlashWeightsF32, lm_head [V, H] fp32)``; the lm_head is the
+    tied embedding, so it also embeds the block ids."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    H, I, hd = cfg.hidden_size, cfg.intermediate_size, cfg.head_dim
+    nh, nkv, F = cfg.num_attention_heads, cfg.num_key_value_heads, num_target_features
+    shapes = {"wq": (nh * hd, H), "wk": (nkv * hd, H), "wv": (nkv * hd, H), "wo": (H, nh * hd),
+              "wg": (I, H), "wu": (I, H), "wd": (H, I)}
+
+    def randn(*shape):
+        return torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std
+
+    def norm_w(n):
+        if random_norms:
+            return 1.0 + 0.1 * torch.randn((n,), generator=g, device=dev)
+        return torch.ones((n,), device=dev)
+
+    layers = [F32Layer(w={k: randn(*shp) for k, shp in shapes.items()}, input_layernorm=norm_w(H),
+                       post_attention_layernorm=norm_w(H), q_norm=norm_w(hd), k_norm=norm_w(hd))
+              for _ in range(cfg.num_hidden_layers)]
+    fc = randn(H, F * H)
+    lm = randn(cfg.vocab_size, H)
+    return DFlashWeightsF32(fc=fc, hidden_norm=norm_w(H), norm=norm_w(H), layers=layers), lm

@@ -55,6 +55,29 @@ def test_noalloc_matches_workspace_entry_on_consecutive_calls(pkg):
         assert torch.isfinite(out.float()).all()
         err = (out.float() - ref.float()).abs().max().item()
         assert err < 2e-2, err
+    # both calls also against an fp32 restatement on the CPU (per-head RMSNorm
+    # and neox RoPE for the first, GQA attention for both), so a fault shared
+    # by the two entry points' kernels cannot pass unseen
+    from oracle import dflash_oracle as O
+    qr = O.rope_neox(O.rms_norm(q1.float().cpu(), qn1.cpu(), 1e-6), torch.arange(32) + 4096, 1e6)
+    kr = O.rope_neox(O.rms_norm(k1.float().cpu(), kn1.cpu(), 1e-6), torch.arange(4096 + 32), 1e6)
+    want1 = _attn_fp32(qr, kr, v1.float().cpu())
+    want2 = _attn_fp32(q2.float().cpu(), k2.float().cpu(), v2.float().cpu())
+    for out, want in ((out1, want1), (out2, want2)):
+        err = (out.float().cpu() - want).abs().max().item()
+        assert err < 2e-2, err
+
+
+def _attn_fp32(q, k, v):
+    """fp32 non-causal GQA attention: q [b, NQ, B, 128], k/v [b, NKV, L, 128]
+    -> [b, B, NQ*128] (the reference's mx.repeat + SDPA, dflash.py:310-317)."""
+    G = q.shape[1] // k.shape[1]
+    kk = torch.repeat_interleave(k, G, dim=1)
+    vv = torch.repeat_interleave(v, G, dim=1)
+    p = torch.softmax(torch.matmul(q, kk.transpose(-1, -2)) * 128 ** -0.5, dim=-1)
+    o = torch.matmul(p, vv)
+    b, nq, B, D = q.shape
+    return o.transpose(1, 2).reshape(b, B, nq * D)
 
 
 def test_noalloc_rejects_shapes_beyond_the_static_array(pkg):
