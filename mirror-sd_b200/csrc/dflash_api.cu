@@ -93,6 +93,7 @@ struct Handle {
   float* ctx_raw = nullptr;         // fc output [Cx, H] fp32
   __half* ctx_n = nullptr;          // hidden_norm(fc rows) in f16: the context K|V GEMM's A
   __half *K = nullptr, *V = nullptr, *Q = nullptr, *attn_out = nullptr, *act = nullptr;
+  float* act_w8 = nullptr;          // W8A16 path: silu(g) * u rows in fp32 [min(Mx, 64), I]
   int8_t* xl = nullptr;             // projection input limbs [3][64][max(H, NQ*128, I)]
   float* xs = nullptr;              // their row scales [64]
   float* hmax = nullptr;            // [H/128, Mx] partial max |h * next norm weight|
@@ -514,6 +515,7 @@ int dflash_create(const DFlashDims* dims, const DFlashWeightsView* w, int device
   CKC(A.alloc(&hd->Q, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->attn_out, (size_t)Mx * NQ * 128));
   CKC(A.alloc(&hd->act, (size_t)Mx * I));
+  CKC(A.alloc(&hd->act_w8, (size_t)std::min(Mx, kW8Rows) * I));
   CKC(A.alloc(&hd->xl, (size_t)3 * 64 * std::max(std::max(H, NQ * 128), I)));
   CKC(A.alloc(&hd->xs, 64));
   CKC(A.alloc(&hd->hmax, (size_t)(H / 128) * Mx));
@@ -1004,11 +1006,11 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
                             hd->xl, hd->xs, st));
     W8Params gu{};
     gu.scale = ly.s_gu; gu.N = 2 * I; gu.K = H; gu.M = M;
-    gu.xl = hd->xl; gu.xscale = hd->xs; gu.act = hd->act; gu.amax_out = hd->amax;
+    gu.xl = hd->xl; gu.xscale = hd->xs; gu.act = hd->act_w8; gu.amax_out = hd->amax;
     CK(w8tc_launch(ly.w_gu, gu, kSiluMul, hd->dev_err, hd->w8_part, hd->w8_part_floats, hd->w8_cnt, hd->num_sms, st));
     // down + residual
     W8Params dn{};
-    CK(w8_limbs_launch(hd->act, M, I, hd->amax, 2 * I / 128, hd->xl, hd->xs, st));
+    CK(w8_limbs_launch(hd->act_w8, M, I, hd->amax, 2 * I / 128, hd->xl, hd->xs, st));
     dn.scale = ly.s_d; dn.N = H; dn.K = I; dn.M = M; dn.xl = hd->xl; dn.xscale = hd->xs;
     dn.h_out = hd->h; dn.hstat_out = hd->hstat;
     if (l + 1 < nl) {  // the next layer's input RMSNorm reads h

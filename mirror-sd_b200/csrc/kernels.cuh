@@ -87,7 +87,7 @@ struct W8Params {
   float* hstat_out;       // kResid: [N/128, M] partial sums of h^2
   float* hmax_out;        // kResid: [N/128, M] partial max |h * next_norm| (or NULL)
   const float* next_norm; // kResid: weight of the RMSNorm that reads h next
-  __half* act;            // kSiluMul: [M, N/2]
+  float* act;             // kSiluMul: [M, N/2] fp32 (no f16 range limit before the limb split)
   float* amax_out;        // kSiluMul: [N/128, M] partial max |act| (or NULL)
   // kQKV
   __half* q_out;          // [b, NQ, B, 128]
@@ -205,7 +205,9 @@ struct LmParams {
 // the kernel finds the maxima itself, one CTA per row)
 cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart, int nparts,
                             int8_t* xl, float* xscale, cudaStream_t st);
-// x = f16(h * rsqrt(mean h^2 + eps) * w) -> limbs; hstat / hmax: [hparts, M]
+cudaError_t w8_limbs_launch(const float* x, int M, int K, const float* maxpart, int nparts,
+                            int8_t* xl, float* xscale, cudaStream_t st);
+// x = h * rsqrt(mean h^2 + eps) * w (fp32) -> limbs; hstat / hmax: [hparts, M]
 // partial sums of h^2 and partial maxima of |h * w|
 cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float* hmax, int hparts,
                                  int M, int K, const float* w, float eps, int8_t* xl, float* xscale,

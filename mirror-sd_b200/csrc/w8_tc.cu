@@ -3,14 +3,16 @@
 //
 //   Y[m, n] = scale[n] * sum_k X[m, k] * Wq[n, k]      m < M <= 64, Wq int8
 //
-// The f16 activations run on the int8 tensor pipe (tcgen05.mma kind::i8) as
+// The activations run on the int8 tensor pipe (tcgen05.mma kind::i8) as
 // three int8 limbs.  Each row m gets a power-of-two scale 2^(e_m - 20),
 // where 2^e_m bounds max|x|.  Then x * 2^(20 - e_m) rounds to an integer
 // q, |q| < 2^20, written as q = l0 + 128 l1 + 16384 l2 with
 // l0, l1 in [-64, 63] and l2 in [-64, 64].
-// For every element within 2^10 of the row maximum this is exact: an f16 has
-// 11 significant bits.  Smaller elements lose at most 2^(e_m - 21), below the
-// f16 rounding of the larger ones.  The weight-limb products accumulate
+// The rows come as fp32 (the normed residual rows and silu(g) * u) or as f16
+// (the attention output of a single-split step, a convex combination of f16 V
+// rows): no f16 range limit applies before the split.  Every element keeps an
+// absolute error of at most 2^(e_m - 21): 20 significant bits at the row
+// maximum, and an f16 input within 2^10 of it is exact.  The weight-limb products accumulate
 // exactly in int32 (|sum| < 127 * 64 * K < 2^31 for K <= 2^18).  Hence the
 // integer sums, recombined in fp32 and scaled, are the W8A16 product with no
 // rounding inside the dot product.
@@ -209,11 +211,9 @@ __device__ __forceinline__ void w8_epilogue_row(const W8Params& p, int tile, int
       const float uv = u[e] * (__ldg(p.scale + gch + 64 + e) * rs);
       o[e] = (gv / (1.0f + expf(-gv))) * uv;
     }
-    const uint32_t pk = pack_f16x2(o[0], o[1]);
-    *reinterpret_cast<uint32_t*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) = pk;
+    *reinterpret_cast<float2*>(p.act + (size_t)m * (p.N / 2) + tile * 64 + lane * 2) = make_float2(o[0], o[1]);
     if (p.amax_out) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk));
-      const float mx = warp_max(fmaxf(fabsf(f.x), fabsf(f.y)));
+      const float mx = warp_max(fmaxf(fabsf(o[0]), fabsf(o[1])));
       if (lane == 0) p.amax_out[(size_t)tile * p.M + m] = mx;
     }
   } else {  // kQKV: the tile is one head
@@ -504,7 +504,7 @@ __device__ __forceinline__ float block_max(float v, float* sh) {
   return sh[32];
 }
 
-// f16 rows -> limbs.  With producer maxima (maxpart [nparts, M]) every CTA
+// f16 or fp32 rows -> limbs.  With producer maxima (maxpart [nparts, M]) every CTA
 // converts one 1024-element chunk of one row in a single pass; without them a
 // CTA owns a whole row and finds its maximum first.
 constexpr int LB_CHUNK = 1024;
@@ -525,6 +525,10 @@ __device__ __forceinline__ void load_h4(const __half* row, int k, float (&v)[4])
   const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
+__device__ __forceinline__ void load_h4(const float* row, int k, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(row + k);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
 
 // max over the producer's partials of row m (every thread of the CTA gets it)
 __device__ __forceinline__ float part_max(const float* part, int nparts, int M, int m, float* sh) {
@@ -533,7 +537,8 @@ __device__ __forceinline__ float part_max(const float* part, int nparts, int M, 
   return block_max(mx, sh);
 }
 
-__global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int K,
+template <class T>
+__global__ void w8_limbs_kernel(const T* __restrict__ x, int M, int MP, int K,
                                 const float* __restrict__ maxpart, int nparts,
                                 int8_t* __restrict__ xl, float* __restrict__ xscale) {
   griddep_wait();
@@ -554,7 +559,7 @@ __global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int
     if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = 1.f;
     return;
   }
-  const __half* row = x + (size_t)m * K;
+  const T* row = x + (size_t)m * K;
   float mx;
   if (maxpart) {
     mx = part_max(maxpart, nparts, M, m, sh);
@@ -579,8 +584,9 @@ __global__ void w8_limbs_kernel(const __half* __restrict__ x, int M, int MP, int
 }
 
 // RMSNorm of the residual rows (h fp32; sums of h^2 and maxima of |h * w| from
-// the producer's partials) rounded to f16 like the reference's activations,
-// then split into limbs; one 1024-element chunk of one row per CTA
+// the producer's partials) split into limbs straight from fp32 -- no f16
+// rounding, so no f16 range limit and 21 significant bits near the row
+// maximum; one 1024-element chunk of one row per CTA
 __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* __restrict__ hstat,
                                      const float* __restrict__ hmax, int hparts, int M, int MP, int K,
                                      const float* __restrict__ w, float eps, int8_t* __restrict__ xl,
@@ -615,8 +621,8 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
   __syncthreads();
   const float rstd = sh[32];
   __syncthreads();
-  // bound on max |f16(h * rstd * w)|: the fp32 products and the f16 rounding
-  // stay within 2^-9 of rstd * max |h * w|
+  // bound on max |h * rstd * w|: the fp32 products stay within 2^-9 of
+  // rstd * max |h * w|
   const float bound = part_max(hmax, hparts, M, m, sh) * rstd * (1.f + 1.f / 512.f);
   int e;
   frexpf(bound, &e);
@@ -626,10 +632,7 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
   for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
     const float4 hv = *reinterpret_cast<const float4*>(row + k);
     const float4 wv = __ldg(reinterpret_cast<const float4*>(w + k));
-    const float v[4] = {__half2float(__float2half_rn(hv.x * rstd * wv.x)),
-                        __half2float(__float2half_rn(hv.y * rstd * wv.y)),
-                        __half2float(__float2half_rn(hv.z * rstd * wv.z)),
-                        __half2float(__float2half_rn(hv.w * rstd * wv.w))};
+    const float v[4] = {hv.x * rstd * wv.x, hv.y * rstd * wv.y, hv.z * rstd * wv.z, hv.w * rstd * wv.w};
     limbs_store4(o0, o1, o2, k, v, up);
   }
 }
@@ -772,13 +775,22 @@ cudaError_t w8_tilepack_launch(const int8_t* src, int n_src, int K, int8_t* dst,
   return cudaGetLastError();
 }
 
-cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart, int nparts,
-                            int8_t* xl, float* xscale, cudaStream_t st) {
+template <class T>
+static cudaError_t w8_limbs_go(const T* x, int M, int K, const float* maxpart, int nparts, int8_t* xl,
+                               float* xscale, cudaStream_t st) {
   if (M < 1 || M > 64 || K % 128) return cudaErrorInvalidValue;
   const int mp = (M + 15) / 16 * 16;
   const dim3 grid(maxpart ? (K + LB_CHUNK - 1) / LB_CHUNK : 1, mp);
-  DFL_TRY(max_smem_carveout(w8_limbs_kernel));
-  return launch_pdl(w8_limbs_kernel, grid, dim3(256), 0, st, x, M, mp, K, maxpart, nparts, xl, xscale);
+  DFL_TRY(max_smem_carveout(w8_limbs_kernel<T>));
+  return launch_pdl(w8_limbs_kernel<T>, grid, dim3(256), 0, st, x, M, mp, K, maxpart, nparts, xl, xscale);
+}
+cudaError_t w8_limbs_launch(const __half* x, int M, int K, const float* maxpart, int nparts,
+                            int8_t* xl, float* xscale, cudaStream_t st) {
+  return w8_limbs_go(x, M, K, maxpart, nparts, xl, xscale, st);
+}
+cudaError_t w8_limbs_launch(const float* x, int M, int K, const float* maxpart, int nparts,
+                            int8_t* xl, float* xscale, cudaStream_t st) {
+  return w8_limbs_go(x, M, K, maxpart, nparts, xl, xscale, st);
 }
 
 cudaError_t rmsnorm_limbs_launch(const float* h, const float* hstat, const float* hmax, int hparts,

@@ -262,3 +262,34 @@ def test_bounded_wait_expiry_is_reported_and_the_context_survives(pkg):
     check_tokens(toks, O.draft_logits(dense, ref, ocfg.block_size), MARGIN)
     model.device_status()
     model.close()
+
+
+def test_forward_activations_beyond_f16_range(pkg):
+    """Projection inputs of about 1e5 and SiLU * up products of about 1e8 (a
+    post-attention norm weight of 3e4): the W8A16 path splits its fp32 rows
+    into limbs directly, so nothing overflows where f16 (max 65504) would,
+    and the hidden states stay within the north-star tolerance of the fp32
+    oracle (the reference's MLP intermediates are bf16, dflash.py:322-330)."""
+    ocfg = tiny_cfg(hidden_size=1024, intermediate_size=2816, num_attention_heads=8, num_key_value_heads=2,
+                    vocab_size=5003, block_size=16, num_hidden_layers=2)
+    q8, dense = O.synth_weights(ocfg, seed=31)
+    big = (3e4 * (1.0 + 0.1 * np.random.default_rng(32).standard_normal(ocfg.hidden_size))).astype(np.float32)
+    q8["layers"][0]["post_norm"] = big
+    dense.layers[0].post_norm = torch.from_numpy(big)
+    model = gpu_model(pkg, ocfg, q8, max_batch=1, max_ctx=64)
+    noise, th = O.synth_inputs(ocfg, 1, 64, ocfg.block_size, seed=33)
+    hid, toks, _, _ = model.draft_step(noise.cuda(), th.cuda(), hidden_fp32=True)
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        ref = O.draft_forward(ocfg, dense, noise, th)
+        # the magnitudes this case drives through layer 0's MLP
+        lw = dense.layers[0]
+        h = noise + O.attention(ocfg, lw, O.rms_norm(noise, lw.in_norm, 1e-6),
+                                O.context_projection(ocfg, dense, th))
+        x2 = O.rms_norm(h, lw.post_norm, 1e-6)
+        act = O.silu(x2 @ lw.wg.T) * (x2 @ lw.wu.T)
+    assert float(x2.abs().max()) > 1e5 and float(act.abs().max()) > 1e7
+    assert torch.isfinite(hid).all()
+    check_hidden(hid, ref, label="W8A16, activations beyond the f16 range")
+    check_tokens(toks, O.draft_logits(dense, ref, ocfg.block_size), MARGIN)
+    model.close()
