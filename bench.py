@@ -223,6 +223,92 @@ def workload_config(args, cfgd):
             "parallelism": f"batch-sharded x{args.gpus}, no collectives"}
 
 
+CFG_4B = dict(hidden_size=2560, num_hidden_layers=5, intermediate_size=9728, num_attention_heads=32,
+              num_key_value_heads=8, head_dim=128, vocab_size=151936, block_size=16)
+
+
+def run_fp32(args, pkg, rank, world, dev):
+    """--config c1: the CPU plumbing config in fp32-accumulate mode on the GPU:
+    4B-class dims, every weight fp32 N(0, 0.02), block 16, ctx 64, batch 1
+    per GPU, block ids uniform with position 0 the mask id (embedded by the
+    tied lm_head), target_hidden N(0, 1).  A step is the fp32 draft forward
+    + lm_head argmax + acceptance on the CUDA cores, replayed from a CUDA
+    graph.  Returns the JSON line on rank 0."""
+    import torch
+    shard = importlib.import_module("mirror-sd_b200.shard")
+    cfgd = dict(CFG_4B)
+    cfg = pkg.DFlashConfig(**cfgd)
+    cfg.target_layer_ids = list(range(F))
+    w, lm = pkg.synth_weights_f32(cfg, seed=0, device=dev)
+    B, H, V, C = cfgd["block_size"], cfgd["hidden_size"], cfgd["vocab_size"], args.ctx
+    model = pkg.DFlashDraftModel(cfg, w, lm, max_batch=args.batch, max_ctx=C, max_block=B, device=dev)
+    g = torch.Generator(device=dev).manual_seed(rank)
+    ids = torch.randint(0, V, (args.batch, B), generator=g, device=dev)
+    ids[:, 0] = cfg.mask_token_id
+    noise = lm[ids]
+    th = torch.randn(args.batch, C, F * H, generator=g, device=dev)
+    out_t = torch.empty((args.batch, B - 1), dtype=torch.int32, device=dev)
+    _, toks, _, _ = model.draft_step(noise, th, want_hidden=False)
+    target = synth_targets(toks, V, 0.9, rank)
+    acc = torch.empty((args.batch,), dtype=torch.int32, device=dev)
+    cor = torch.empty((args.batch,), dtype=torch.int32, device=dev)
+
+    def step():
+        model.draft_step(noise, th, target_tokens=target, want_hidden=False, out_tokens=out_t, acc_len=acc,
+                         correction=cor)
+
+    for _ in range(args.warmup):
+        step()
+    launches = model._lib.dflash_last_launch_count(model._handle)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        step()
+    for _ in range(3):
+        graph.replay()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local_gpu_id(dev)) if rank == 0 else None
+    time.sleep(0.6 if sampler else 0)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    s0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    s1.record()
+    torch.cuda.synchronize(dev)
+    t1 = time.time()
+    if sampler:
+        sampler.stop()
+    ms = shard.max_over_ranks(s0.elapsed_time(s1) / args.steps)
+    del graph
+    model.close()
+    if rank != 0:
+        return None
+    hbm = peaks()[0]
+    I, NQ, NKV, L = cfgd["intermediate_size"], cfgd["num_attention_heads"], cfgd["num_key_value_heads"], \
+        cfgd["num_hidden_layers"]
+    params = L * ((NQ + 2 * NKV) * 128 * H + H * NQ * 128 + 3 * I * H) + F * H * H + V * H
+    nbytes = 4 * (params + args.batch * (C * F * H + B * H))
+    return {"metric": "draft tok/s, fp32-accumulate mode (c1: 4B-class, fp32 weights, block 16, ctx 64)",
+            "value": shard.job_throughput([args.batch * (B - 1)] * world, ms), "unit": "draft tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32: fp32 weights, activations and accumulation (CUDA cores)", "data": "synthetic",
+            "config": {"workload": f"c1: 4B-class fp32 draft, block {B}, ctx {C}, batch {args.batch} per GPU",
+                       "parallelism": f"batch-sharded x{world}, no collectives"},
+            "roofline": {"bound": "hbm", "bytes_per_step": nbytes, "achieved": nbytes / (ms / 1e3) / 1e9,
+                         "peak": hbm, "unit": "GB/s", "frac": nbytes / (ms / 1e3) / 1e9 / hbm},
+            "launches_per_step": launches,
+            "clocks": sampler.summary(t0, t1) if sampler else None}
+
+
 def run_serving(args, pkg, rank, world, dev):
     """--config c5: batched serving on the 8B-class draft.  256 requests with
     contexts uniform in [512, 8192] and block 16 are sharded over the ranks
@@ -550,8 +636,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=["c3", "c2", "c5", "c4"], default="c3",
-                    help="c3 headline; c2 8B step; c5 batched serving; c4 attention sweep")
+    ap.add_argument("--config", choices=["c3", "c2", "c5", "c4", "c1"], default="c3",
+                    help="c3 headline; c2 8B step; c5 batched serving; c4 attention sweep; "
+                         "c1 fp32-accumulate mode")
     ap.add_argument("--kernel", default=None, help="time one kernel case instead (list: --kernel help)")
     ap.add_argument("--iters", type=int, default=20, help="--kernel / c4: timed launches")
     ap.add_argument("--seqs", type=int, default=256, help="c5: requests over all GPUs")
@@ -574,7 +661,7 @@ def main():
         return
     cfgd = dict(CFG_27B if args.config == "c3" else CFG_8B)
     if args.ctx is None:
-        args.ctx = 4096 if args.config == "c3" else 2048
+        args.ctx = {"c3": 4096, "c1": 64}.get(args.config, 2048)
     if args.warmup < 3:
         args.warmup = 3
 
@@ -598,10 +685,10 @@ def main():
     shard = importlib.import_module("mirror-sd_b200.shard")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if args.config == "c5":
+    if args.config in ("c5", "c1"):
         if args.steps == 200:
             args.steps = 20
-        line = run_serving(args, pkg, rank, world, dev)
+        line = (run_serving if args.config == "c5" else run_fp32)(args, pkg, rank, world, dev)
         if line is not None:
             print(json.dumps(line), flush=True)
         if world > 1:
