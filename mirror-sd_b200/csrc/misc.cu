@@ -122,33 +122,56 @@ __global__ void init_h_kernel(const __nv_bfloat16* __restrict__ noise, int M, in
   }
 }
 
-// ctx_out[r, k] = f16(raw[r, k] * rsqrt(sum_p part[p, r] / H + eps) * w[k]); one CTA per row
-__global__ void ctx_norm_kernel(const float* __restrict__ raw, const float* __restrict__ part,
-                                int nparts, int rows, int H, const float* __restrict__ w, float eps,
-                                __half* __restrict__ out) {
+// ctx_out[r, k] = f16(raw[r, k] * rsqrt(sum_p part[p, r] / H + eps) * w[k]);
+// one CTA of CN_THREADS per row.  The row's loads are issued first (up to
+// CN_HELD groups of 8 values per thread stay in registers) while warp 0 sums
+// the partials, so the reduction's latency hides under the row's reads.
+constexpr int CN_THREADS = 128, CN_HELD = 6;
+__global__ void __launch_bounds__(CN_THREADS) ctx_norm_kernel(const float* __restrict__ raw,
+                                                              const float* __restrict__ part, int nparts,
+                                                              int rows, int H, const float* __restrict__ w,
+                                                              float eps, __half* __restrict__ out) {
   griddep_wait();
   griddep_launch_dependents();
   const int r = blockIdx.x;
   __shared__ float rs;
-  if (threadIdx.x == 0) {
+  const float* src = raw + (size_t)r * H;
+  __half* dst = out + (size_t)r * H;
+  const int ng = H / 8;
+  float4 v[CN_HELD][2];
+#pragma unroll
+  for (int i = 0; i < CN_HELD; ++i) {
+    const int g = threadIdx.x + i * CN_THREADS;
+    if (g < ng) {
+      v[i][0] = *reinterpret_cast<const float4*>(src + 8 * g);
+      v[i][1] = *reinterpret_cast<const float4*>(src + 8 * g + 4);
+    }
+  }
+  if (threadIdx.x < 32) {
     float ss = 0.f;
-    for (int q = 0; q < nparts; ++q) ss += part[(size_t)q * rows + r];
-    rs = rsqrtf(ss / static_cast<float>(H) + eps);
+    for (int q = threadIdx.x; q < nparts; q += 32) ss += part[(size_t)q * rows + r];
+    ss = warp_sum(ss);
+    if (threadIdx.x == 0) rs = rsqrtf(ss / static_cast<float>(H) + eps);
   }
   __syncthreads();
   const float rstd = rs;
-  for (int k = threadIdx.x * 8; k < H; k += blockDim.x * 8) {
-    const float4 a = *reinterpret_cast<const float4*>(raw + (size_t)r * H + k);
-    const float4 c = *reinterpret_cast<const float4*>(raw + (size_t)r * H + k + 4);
-    const float4 w0 = *reinterpret_cast<const float4*>(w + k);
-    const float4 w1 = *reinterpret_cast<const float4*>(w + k + 4);
+  auto put = [&](int g, const float4& a, const float4& c) {
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 8 * g));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + 8 * g + 4));
     uint4 o;
     o.x = pack_f16x2(a.x * rstd * w0.x, a.y * rstd * w0.y);
     o.y = pack_f16x2(a.z * rstd * w0.z, a.w * rstd * w0.w);
     o.z = pack_f16x2(c.x * rstd * w1.x, c.y * rstd * w1.y);
     o.w = pack_f16x2(c.z * rstd * w1.z, c.w * rstd * w1.w);
-    *reinterpret_cast<uint4*>(out + (size_t)r * H + k) = o;
+    *reinterpret_cast<uint4*>(dst + 8 * g) = o;
+  };
+#pragma unroll
+  for (int i = 0; i < CN_HELD; ++i) {
+    const int g = threadIdx.x + i * CN_THREADS;
+    if (g < ng) put(g, v[i][0], v[i][1]);
   }
+  for (int g = threadIdx.x + CN_HELD * CN_THREADS; g < ng; g += CN_THREADS)   // rows wider than held
+    put(g, *reinterpret_cast<const float4*>(src + 8 * g), *reinterpret_cast<const float4*>(src + 8 * g + 4));
 }
 
 // hn = bf16(h * rstd * w) for every row; also the caller's hidden output
@@ -282,7 +305,7 @@ cudaError_t ctx_norm_launch(const float* raw, const float* part, int nparts, int
                             const float* w, float eps, __half* out, cudaStream_t st) {
   if (H % 8 || rows < 1) return cudaErrorInvalidValue;
   DFL_TRY(max_smem_carveout(ctx_norm_kernel));
-  return launch_pdl(ctx_norm_kernel, dim3(rows), dim3(256), 0, st, raw, part, nparts, rows, H, w, eps, out);
+  return launch_pdl(ctx_norm_kernel, dim3(rows), dim3(CN_THREADS), 0, st, raw, part, nparts, rows, H, w, eps, out);
 }
 cudaError_t final_norm_launch(const float* h, const float* hstat, int hparts, int M, int H,
                               const float* w, float eps, __nv_bfloat16* hn, void* out, bool out_f32,

@@ -16,7 +16,9 @@
 // Persistent: one CTA per SM walks output tiles 128 x 256 (blockIdx.x, +grid,
 // ...) in a rasterised order (groups of 8 n-blocks, n fastest), so the tiles
 // in flight at once share A and B rows in L2.  K step 64 (one 128-byte
-// swizzle atom), 4-stage TMA ring across tile boundaries.
+// swizzle atom), 4-stage TMA ring across tile boundaries.  With more than
+// 128 rows, clusters of two CTAs share 256 x 256 tiles instead
+// (tcgen05.mma.cta_group::2, 6-stage rings of 32 KB: TcCfg below).
 // Warp 0: TMA producer.  Warp 1: TMEM allocator + single-thread UMMA issuer
 // (tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16) into one of two fp32
 // accumulators (2 x 256 TMEM columns), so the epilogue of a tile overlaps the
@@ -24,6 +26,9 @@
 // accumulator row, so per-row and per-head reductions are thread-local).
 // Every mbarrier wait is bounded; a timeout sets the device error word and the
 // CTA unwinds (TMEM is released on every path).
+#include <algorithm>
+#include <cstdlib>
+
 #include "kernels.cuh"
 
 namespace dfl {
@@ -31,10 +36,21 @@ namespace dfl {
 constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;   // 16 KB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;   // 32 KB
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_THREADS = 192;
-constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 constexpr int TC_GROUP_N = 8;  // rasterisation: n-blocks per tile group
+
+// PAIR: a cluster of two CTAs computes one 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256): each CTA stages its own 128 A rows and
+// half of the 256 B rows, so a CTA's shared memory carries 32 KB per k-block
+// instead of 48 KB, the ring gets 6 stages, and B crosses L2 once per pair.
+template <bool PAIR>
+struct TcCfg {
+  static constexpr int NR = PAIR ? 2 : 1;                      // CTAs per tile
+  static constexpr int STAGES = PAIR ? 6 : TC_STAGES;
+  static constexpr int B_BYTES = TC_B_BYTES / NR;              // this CTA's B rows
+  static constexpr int STAGE_BYTES = TC_A_BYTES + B_BYTES;
+  static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+};
 
 // tile t -> (m-block, n-block): groups of TC_GROUP_N n-blocks; inside a group
 // the n-block runs fastest
@@ -59,8 +75,7 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 struct TcItem {
   int tile, kb0, kb1, part;   // part < 0: a whole tile
 };
-__device__ __forceinline__ TcItem tc_item(int ti, int T, int nk, int split) {
-  const int G = gridDim.x, c = blockIdx.x;
+__device__ __forceinline__ TcItem tc_item(int ti, int T, int nk, int split, int G, int c) {
   const int R = T / G;
   if (split > 0 && ti >= R) {
     const int q = c + (ti - R) * G;
@@ -69,8 +84,7 @@ __device__ __forceinline__ TcItem tc_item(int ti, int T, int nk, int split) {
   }
   return {c + ti * G, 0, nk, -1};
 }
-__device__ __forceinline__ int tc_items(int T, int split) {
-  const int G = gridDim.x, c = blockIdx.x;
+__device__ __forceinline__ int tc_items(int T, int split, int G, int c) {
   if (split > 0) {
     const int R = T / G;
     const int P = (T - R * G) * split;
@@ -150,17 +164,18 @@ struct TcAMaps {
   CUtensorMap m[NSRC];
 };
 
-template <int AB_FMT, int MODE, int NSRC>
+template <int AB_FMT, int MODE, int NSRC, bool PAIR>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ TcAMaps<NSRC> maps_a, const __grid_constant__ CUtensorMap map_b,
                    const TcParams p) {
+  using CF = TcCfg<PAIR>;
   griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * TC_STAGE_BYTES);
-  uint64_t* empty = full + TC_STAGES;
-  uint64_t* accf = empty + TC_STAGES;  // [2] accumulator ready
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CF::STAGES * CF::STAGE_BYTES);
+  uint64_t* empty = full + CF::STAGES;
+  uint64_t* accf = empty + CF::STAGES;  // [2] accumulator ready
   uint64_t* acce = accf + 2;           // [2] accumulator drained by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -168,27 +183,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = p.K / TC_BK;
-  const int nmb = (p.M + TC_BM - 1) / TC_BM, nnb = p.N / TC_BN;
+  // pair mode: tiles of 256 rows, CTA `rank` of the cluster owns rows rank*128.. of each
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+  const int G = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  const int cidx = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+  const int nmb = (p.M + TC_BM * CF::NR - 1) / (TC_BM * CF::NR), nnb = p.N / TC_BN;
   const int ntiles = nmb * nnb;
-  const int my_tiles = tc_items(ntiles, p.split);
+  const int my_tiles = tc_items(ntiles, p.split, G, cidx);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; ++s) {
+    for (int s = 0; s < CF::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&accf[b], 1);
-      mbar_init(&acce[b], 4);
+      mbar_init(&acce[b], 4 * CF::NR);   // the epilogue warps of every CTA of the tile
     }
     *abort_flag = 0;
     fence_mbar_init();
     for (int f = 0; f < NSRC && f * p.a_cols < p.K; ++f) prefetch_tmap(&maps_a.m[f]);
     prefetch_tmap(&map_b);
   }
+  if (PAIR) {
+    // both CTAs' barriers exist before any CTA signals its peer's
+    __syncthreads();
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * TC_BN);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, 2 * TC_BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, 2 * TC_BN);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -200,20 +230,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < my_tiles && ok; ++ti) {
-        const TcItem w = tc_item(ti, ntiles, nk, p.split);
+        const TcItem w = tc_item(ti, ntiles, nk, p.split, G, cidx);
         int mb, nb;
         tc_tile(w.tile, nmb, nnb, mb, nb);
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
-          const int s = it % TC_STAGES;
-          const uint32_t ph = (it / TC_STAGES) & 1;
+          const int s = it % CF::STAGES;
+          const uint32_t ph = (it / CF::STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.err, abort_flag)) { ok = false; break; }
-          uint8_t* sa = smem + s * TC_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[s], TC_STAGE_BYTES);
+          uint8_t* sa = smem + s * CF::STAGE_BYTES;
           int col = kb * TC_BK, f = 0;
           if (NSRC > 1) {
             f = col / p.a_cols;
             col -= f * p.a_cols;
           }
+          if (PAIR) {
+            // both CTAs' copies complete on rank 0's full barrier, which
+            // expects the bytes of the pair (an odd CTA's copy may land before
+            // rank 0 arms the barrier: the transaction count is signed)
+            const uint32_t fb = mapa_shared(&full[s], 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * CF::STAGE_BYTES);
+            tma_load_2d_pair(sa, &maps_a.m[f], fb, col, (mb * 2 + (int)rank) * TC_BM);
+            if (MODE == kTcArgmax)
+              tma_load_2d_pair(sa + TC_A_BYTES, &map_b, fb, 0, ((2 * nb + (int)rank) * nk + kb) * 128);
+            else
+              tma_load_2d_pair(sa + TC_A_BYTES, &map_b, fb, kb * TC_BK, nb * TC_BN + (int)rank * 128);
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[s], CF::STAGE_BYTES);
           tma_load_2d(sa, &maps_a.m[f], &full[s], col, mb * TC_BM);
           if (MODE == kTcArgmax) {
             // B = the lm_head's pre-swizzled vocabulary tiles: 16 KB blocks
@@ -229,8 +272,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(TC_BM, TC_BN, AB_FMT);
+    if (lane == 0 && rank == 0) {   // in a pair, the even CTA issues for both
+      constexpr uint32_t idesc = umma_idesc_f16(TC_BM * CF::NR, TC_BN, AB_FMT);
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < my_tiles && ok; ++ti) {
@@ -238,23 +281,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!mbar_wait(&acce[b], ((ti >> 1) & 1) ^ 1, p.err, abort_flag)) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * TC_BN;
-        const TcItem w = tc_item(ti, ntiles, nk, p.split);
+        const TcItem w = tc_item(ti, ntiles, nk, p.split, G, cidx);
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
-          const int s = it % TC_STAGES;
-          const uint32_t ph = (it / TC_STAGES) & 1;
+          const int s = it % CF::STAGES;
+          const uint32_t ph = (it / CF::STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * TC_STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + s * CF::STAGE_BYTES);
           const uint64_t adesc = umma_desc_sw128(sa);
           const uint64_t bdesc = umma_desc_sw128(sa + TC_A_BYTES);
 #pragma unroll
           for (int k = 0; k < TC_BK / 16; ++k) {
             // advance 16 elements (32 bytes) inside the swizzle atom: +2 in 16-byte units
-            umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != w.kb0 || k != 0));
+            if (PAIR)
+              umma_f16_pair(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != w.kb0 || k != 0));
+            else
+              umma_f16(acc, adesc + 2 * k, bdesc + 2 * k, idesc, (kb != w.kb0 || k != 0));
           }
-          umma_commit(&empty[s]);
+          if (PAIR)
+            umma_commit_pair(&empty[s]);   // frees the stage in both CTAs
+          else
+            umma_commit(&empty[s]);
         }
-        umma_commit(&accf[b]);  // fires once every MMA of the tile has retired
+        if (PAIR)
+          umma_commit_pair(&accf[b]);  // both halves of the tile are ready
+        else
+          umma_commit(&accf[b]);  // fires once every MMA of the tile has retired
       }
     }
   } else {
@@ -263,11 +315,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row_local = q * 32 + lane;
     for (int ti = 0; ti < my_tiles; ++ti) {
       const int buf = ti & 1;
-      const TcItem w = tc_item(ti, ntiles, nk, p.split);
+      const TcItem w = tc_item(ti, ntiles, nk, p.split, G, cidx);
       int mb, nb;
       tc_tile(w.tile, nmb, nnb, mb, nb);
       const int n0 = nb * TC_BN;
-      const int row = mb * TC_BM + row_local;
+      const int row = (mb * CF::NR + (int)rank) * TC_BM + row_local;
       const bool row_ok = row < p.M;
       // No epilogue warp leaves the loop early: after a timeout (the abort
       // flag) the items are walked without work, so every named barrier of
@@ -277,8 +329,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t tbase = tmem + buf * TC_BN + ((uint32_t)(q * 32) << 16);
       bool run = live;
       if (w.part >= 0) {
-        const int slot = w.tile - (ntiles / gridDim.x) * gridDim.x;
-        float* mine = p.tail_part + ((size_t)slot * p.split + w.part) * (TC_BM * TC_BN);
+        const int slot = w.tile - (ntiles / G) * G;
+        // partial of (slot, part, rank): every CTA half of a pair keeps its own rows
+        float* mine = p.tail_part + (((size_t)slot * p.split + w.part) * CF::NR + rank) * (TC_BM * TC_BN);
         if (live) {
 #pragma unroll 1
           for (int ch = 0; ch < TC_BN / 32; ++ch) {
@@ -294,8 +347,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (threadIdx.x == 64) {
           // every part counts, after an abort too, so the counter always
           // returns to zero for the next launch
-          const bool last = atomicAdd(p.tail_cnt + slot, 1) == p.split - 1;
-          if (last) p.tail_cnt[slot] = 0;
+          const int ci = slot * CF::NR + (int)rank;
+          const bool last = atomicAdd(p.tail_cnt + ci, 1) == p.split - 1;
+          if (last) p.tail_cnt[ci] = 0;
           *tail_flag = last;
         }
         named_bar_sync(2, 128);
@@ -303,7 +357,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (run) {
           // the last part: sum the parts in fixed order into the accumulator
           __threadfence();
-          const float* base = p.tail_part + (size_t)slot * p.split * (TC_BM * TC_BN);
+          const float* base = p.tail_part + ((size_t)slot * p.split * CF::NR + rank) * (TC_BM * TC_BN);
 #pragma unroll 1
           for (int ch = 0; ch < TC_BN / 32; ++ch) {
             // 32 independent loads per part, so they are all in flight at once
@@ -312,7 +366,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e) a[e] = __ldcg(col + (size_t)e * TC_BM);
             for (int q2 = 1; q2 < p.split; ++q2) {
-              const float* cq = col + (size_t)q2 * (TC_BM * TC_BN);
+              const float* cq = col + (size_t)q2 * CF::NR * (TC_BM * TC_BN);
               float v[32];
 #pragma unroll
               for (int e = 0; e < 32; ++e) v[e] = __ldcg(cq + (size_t)e * TC_BM);
@@ -496,14 +550,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acce[buf]);  // accumulator free for tile ti + 2
+      if (lane == 0) {  // accumulator free for tile ti + 2 (rank 0 issues the MMAs of a pair)
+        if (PAIR)
+          mbar_arrive_cluster(mapa_shared(&acce[buf], 0));
+        else
+          mbar_arrive(&acce[buf]);
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) {
+    // no CTA of the pair leaves while its peer may still signal its barriers
+    // or the tensor core may still read its shared memory
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * TC_BN);
+    if (PAIR)
+      tmem_dealloc_pair(tmem, 2 * TC_BN);
+    else
+      tmem_dealloc(tmem, 2 * TC_BN);
   }
 }
 
@@ -544,6 +612,17 @@ static bool make_map(CUtensorMap* map, const void* base, bool bf16, uint64_t inn
   return r == CUDA_SUCCESS;
 }
 
+// CTA pairs are on unless DFLASH_TC_PAIRS=0 (read once), which keeps the
+// single-CTA kernel for comparison runs
+static bool tc_pairs_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("DFLASH_TC_PAIRS");
+    on = (e && e[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 // Tail split: the tiles of the partial last round (all tiles when there are
 // fewer than SMs) are cut along K into S parts spread over the grid.  S
 // minimises the makespan in tile units, R + ceil(tail * S / G) * (1 / S + c),
@@ -573,40 +652,77 @@ int tc_tail_split(int tiles, int sms, int nk, int cap_parts, int* grid_out) {
   return bs;
 }
 
-template <int FMT, int MODE, int NSRC>
+// clusters of two CTAs of `kern` that fit on the device at once (an SM without
+// a partner in its GPC cannot host half a pair); cached per instantiation
+template <class Kern>
+static int tc_max_pairs(Kern kern, size_t smem, int* cache) {
+  if (*cache >= 0) return *cache;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  *cache = n;
+  return n;
+}
+
+template <int FMT, int MODE, int NSRC, bool PAIR>
 static cudaError_t tc_launch_t(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, TcParams p, cudaStream_t st) {
-  auto kern = tc_gemm_kernel<FMT, MODE, NSRC>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)TC_SMEM);
+  using CF = TcCfg<PAIR>;
+  auto kern = tc_gemm_kernel<FMT, MODE, NSRC, PAIR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)CF::SMEM);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   DFL_TRY(cudaGetDevice(&dev));
   DFL_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int tiles = (p.N / TC_BN) * ((p.M + TC_BM - 1) / TC_BM);
+  DFL_TRY(max_smem_carveout(kern));
+  int units = sms;   // CTAs, or CTA pairs, resident at once
+  if (PAIR) {
+    static int cache = -1;
+    units = std::min(sms / 2, tc_max_pairs(kern, CF::SMEM, &cache));
+    if (units < 1) return cudaErrorInvalidConfiguration;
+  }
+  const int tiles = (p.N / TC_BN) * ((p.M + TC_BM * CF::NR - 1) / (TC_BM * CF::NR));
   const bool ws = p.tail_part != nullptr && p.tail_cnt != nullptr;
   int grid = 0;
-  p.split = tc_tail_split(tiles, sms, p.K / TC_BK, ws ? p.tail_cap : 0, &grid);
-  DFL_TRY(max_smem_carveout(kern));
-  return launch_pdl(kern, dim3(grid), dim3(TC_THREADS), TC_SMEM, st, ma, mb, p);
+  p.split = tc_tail_split(tiles, units, p.K / TC_BK, ws ? p.tail_cap / CF::NR : 0, &grid);
+  if (PAIR)
+    return launch_pdl_cluster_smem(kern, dim3(2 * grid), dim3(TC_THREADS), 2, CF::SMEM, st, ma, mb, p);
+  return launch_pdl(kern, dim3(grid), dim3(TC_THREADS), CF::SMEM, st, ma, mb, p);
+}
+
+template <int FMT, int MODE, int NSRC>
+static cudaError_t tc_launch_pick(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, const TcParams& p, bool pair,
+                                  cudaStream_t st) {
+  return pair ? tc_launch_t<FMT, MODE, NSRC, true>(ma, mb, p, st) : tc_launch_t<FMT, MODE, NSRC, false>(ma, mb, p, st);
 }
 
 template <int NSRC>
 static cudaError_t tc_dispatch(const TcAMaps<NSRC>& ma, const CUtensorMap& mb, bool bf16, int mode,
-                               const TcParams& p, cudaStream_t st) {
+                               const TcParams& p, bool pair, cudaStream_t st) {
   if (bf16) {
-    if (mode == kTcFc) return tc_launch_t<1, kTcFc, NSRC>(ma, mb, p, st);
-    if (mode == kTcStoreF32) return tc_launch_t<1, kTcStoreF32, NSRC>(ma, mb, p, st);
+    if (mode == kTcFc) return tc_launch_pick<1, kTcFc, NSRC>(ma, mb, p, pair, st);
+    if (mode == kTcStoreF32) return tc_launch_pick<1, kTcStoreF32, NSRC>(ma, mb, p, pair, st);
     if constexpr (NSRC == 1) {
-      if (mode == kTcArgmax) return tc_launch_t<1, kTcArgmax, 1>(ma, mb, p, st);
-      if (mode == kTcCtxKV) return tc_launch_t<1, kTcCtxKV, 1>(ma, mb, p, st);
+      if (mode == kTcArgmax) return tc_launch_pick<1, kTcArgmax, 1>(ma, mb, p, pair, st);
+      if (mode == kTcCtxKV) return tc_launch_pick<1, kTcCtxKV, 1>(ma, mb, p, pair, st);
     }
   } else {
     if constexpr (NSRC == 1) {
-      if (mode == kTcCtxKV) return tc_launch_t<0, kTcCtxKV, 1>(ma, mb, p, st);
-      if (mode == kTcBlkQKV) return tc_launch_t<0, kTcBlkQKV, 1>(ma, mb, p, st);
-      if (mode == kTcResid) return tc_launch_t<0, kTcResid, 1>(ma, mb, p, st);
-      if (mode == kTcSilu) return tc_launch_t<0, kTcSilu, 1>(ma, mb, p, st);
+      if (mode == kTcCtxKV) return tc_launch_pick<0, kTcCtxKV, 1>(ma, mb, p, pair, st);
+      if (mode == kTcBlkQKV) return tc_launch_pick<0, kTcBlkQKV, 1>(ma, mb, p, pair, st);
+      if (mode == kTcResid) return tc_launch_pick<0, kTcResid, 1>(ma, mb, p, pair, st);
+      if (mode == kTcSilu) return tc_launch_pick<0, kTcSilu, 1>(ma, mb, p, pair, st);
     }
-    if (mode == kTcStoreF32) return tc_launch_t<0, kTcStoreF32, NSRC>(ma, mb, p, st);
+    if (mode == kTcStoreF32) return tc_launch_pick<0, kTcStoreF32, NSRC>(ma, mb, p, pair, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -620,25 +736,27 @@ cudaError_t tc_gemm_launch_src(const TcSources& a, const void* B, bool bf16, int
   if (a.n < 1 || a.n > kTcMaxSrc || a.cols < TC_BK || a.cols % TC_BK || (long long)a.n * a.cols != p.K)
     return cudaErrorInvalidValue;
   p.a_cols = a.cols;
+  // CTA pairs (M = 256 tiles) once there are two 128-row blocks to share B
+  const bool pair = p.M > TC_BM && tc_pairs_enabled();
   CUtensorMap mb;
   if (mode == kTcArgmax) {
     const uint64_t vt = ((uint64_t)p.V + 127) / 128;
     if (!bf16 || p.V < 1 || (uint64_t)p.N < vt * 128 || (uint64_t)p.N > vt * 128 + 128) return cudaErrorInvalidValue;
     if (!make_map(&mb, B, true, TC_BK, vt * (p.K / TC_BK) * 128, 128, TC_BK, false)) return cudaErrorInvalidValue;
-  } else if (!make_map(&mb, B, bf16, p.K, p.N, TC_BN, p.K)) {
+  } else if (!make_map(&mb, B, bf16, p.K, p.N, pair ? TC_BN / 2 : TC_BN, p.K)) {
     return cudaErrorInvalidValue;
   }
   if (a.n == 1) {
     TcAMaps<1> ma;
     if (!make_map(&ma.m[0], a.ptr[0], bf16, a.cols, p.M, TC_BM, a.ld[0])) return cudaErrorInvalidValue;
-    return tc_dispatch<1>(ma, mb, bf16, mode, p, st);
+    return tc_dispatch<1>(ma, mb, bf16, mode, p, pair, st);
   }
   if (mode != kTcFc && mode != kTcStoreF32) return cudaErrorInvalidValue;
   TcAMaps<kTcMaxSrc> ma;
   for (int f = 0; f < a.n; ++f)
     if (!make_map(&ma.m[f], a.ptr[f], bf16, a.cols, p.M, TC_BM, a.ld[f])) return cudaErrorInvalidValue;
   for (int f = a.n; f < kTcMaxSrc; ++f) ma.m[f] = ma.m[0];
-  return tc_dispatch<kTcMaxSrc>(ma, mb, bf16, mode, p, st);
+  return tc_dispatch<kTcMaxSrc>(ma, mb, bf16, mode, p, pair, st);
 }
 
 cudaError_t tc_gemm_launch(const void* A, const void* B, bool bf16, int mode, const TcParams& p,
