@@ -242,15 +242,32 @@ __global__ void __launch_bounds__(384) attn_partial_kernel(const AttnParams p) {
 
 // Merge of the split partials of one (sequence bi, head, block row j): one
 // warp, lanes split the splits for the max / denominator and the head dims
-// for the weighted sum.  Returns lane's 4 output dims as f16.
+// for the weighted sum.  Returns lane's 4 output dims as f16.  The maxima,
+// the denominators and the first ROWS partial rows are all loaded before any
+// is used, so up to ROWS splits cost one L2 round trip; the sums run in split
+// order.  The fused limb merge takes ROWS = 20 (17 splits at the 27B draft's
+// ctx 4096 step); the plain merge, launched with many CTAs per SM at large
+// batch, keeps its registers low with 8.
+template <int AT_MERGE_ROWS>
 __device__ __forceinline__ uint2 attn_merge_row(const AttnParams& p, int bi, int head, int j, int lane) {
   const int G = p.nq / p.nkv;
   const int R = G * p.block;
   const int kvh = head / G;
   const int r = (head - kvh * G) * p.block + j;
   const size_t base = (((size_t)bi * p.nkv + kvh) * p.splits) * (size_t)R + r;
-  float M = -INFINITY;
-  for (int s = lane; s < p.splits; s += 32) M = fmaxf(M, p.mpart[base + (size_t)s * R]);
+  auto orow = [&](int s) {
+    return __ldcg(reinterpret_cast<const float4*>(p.opart + (base + (size_t)s * R) * 128 + lane * 4));
+  };
+  float mv0 = -INFINITY, lv0 = 0.f;
+  if (lane < p.splits) {
+    mv0 = p.mpart[base + (size_t)lane * R];
+    lv0 = p.lpart[base + (size_t)lane * R];
+  }
+  float4 ov[AT_MERGE_ROWS];
+#pragma unroll
+  for (int t = 0; t < AT_MERGE_ROWS; ++t) ov[t] = t < p.splits ? orow(t) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float M = mv0;
+  for (int s = lane + 32; s < p.splits; s += 32) M = fmaxf(M, p.mpart[base + (size_t)s * R]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float Ms = (M == -INFINITY) ? 0.f : M;
@@ -261,21 +278,18 @@ __device__ __forceinline__ uint2 attn_merge_row(const AttnParams& p, int bi, int
     float w = 0.f;
     if (s < p.splits) {
       const size_t idx = base + (size_t)s * R;
-      w = exp2f(p.mpart[idx] - Ms);
-      L += p.lpart[idx] * w;
+      w = exp2f((s0 == 0 ? mv0 : p.mpart[idx]) - Ms);
+      L += (s0 == 0 ? lv0 : p.lpart[idx]) * w;
     }
     const int n = min(32, p.splits - s0);
-    // the partial rows of up to 16 splits are loaded before any is used, so
-    // their L2 round trips overlap (splits run to ~20 at one sequence)
-    for (int t0 = 0; t0 < n; t0 += 16) {
-      float4 ov[16];
+    for (int t0 = 0; t0 < n; t0 += AT_MERGE_ROWS) {
+      if (s0 + t0 > 0) {
 #pragma unroll
-      for (int t = 0; t < 16; ++t)
-        ov[t] = t0 + t < n ? __ldcg(reinterpret_cast<const float4*>(
-                                  p.opart + (base + (size_t)(s0 + t0 + t) * R) * 128 + lane * 4))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < AT_MERGE_ROWS; ++t)
+          ov[t] = t0 + t < n ? orow(s0 + t0 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
+      for (int t = 0; t < AT_MERGE_ROWS; ++t) {
         const float wt = __shfl_sync(0xffffffffu, w, (t0 + t) & 31);
         if (t0 + t < n) {
           acc[0] += ov[t].x * wt; acc[1] += ov[t].y * wt; acc[2] += ov[t].z * wt; acc[3] += ov[t].w * wt;
@@ -301,7 +315,7 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
   const int bi = blockIdx.y;
   if (row >= p.nq * p.block) return;
   const int head = row / p.block, j = row % p.block;
-  const uint2 pk = attn_merge_row(p, bi, head, j, lane);
+  const uint2 pk = attn_merge_row<8>(p, bi, head, j, lane);
   *reinterpret_cast<uint2*>(out + ((size_t)bi * p.block + j) * ((size_t)p.nq * 128) +
                             (size_t)head * 128 + lane * 4) = pk;
   if (p.omax) {  // per (head, row) max |out| for the o-projection's limb split
@@ -318,7 +332,7 @@ __global__ void attn_combine_kernel(const AttnParams p, __half* __restrict__ out
 // rows through distributed shared memory, so every CTA splits its own
 // columns with the row's power-of-two scale.  The limbs and scales are those
 // that attn_combine_kernel followed by the standalone limb split produce.
-__global__ void __launch_bounds__(256) attn_combine_limbs_kernel(const AttnParams p, int M, int MP,
+__global__ void __launch_bounds__(256, 2) attn_combine_limbs_kernel(const AttnParams p, int M, int MP,
                                                                  int8_t* __restrict__ xl,
                                                                  float* __restrict__ xscale) {
   griddep_wait();
@@ -345,7 +359,7 @@ __global__ void __launch_bounds__(256) attn_combine_limbs_kernel(const AttnParam
   const int bi = m / p.block, j = m - bi * p.block;
   float v[4] = {0.f, 0.f, 0.f, 0.f};
   if (head < p.nq) {
-    const uint2 pk = attn_merge_row(p, bi, head, j, lane);
+    const uint2 pk = attn_merge_row<20>(p, bi, head, j, lane);
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&pk.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&pk.y));
     v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
