@@ -560,6 +560,11 @@ __global__ void w8_limbs_kernel(const T* __restrict__ x, int M, int MP, int K,
     return;
   }
   const T* row = x + (size_t)m * K;
+  // with producer maxima, this thread's first four elements are loaded before
+  // the maximum's reduction waits
+  const int kf = k0 + threadIdx.x * 4;
+  float v0[4] = {0.f, 0.f, 0.f, 0.f};
+  if (maxpart && kf < k1) load_h4(row, kf, v0);
   float mx;
   if (maxpart) {
     mx = part_max(maxpart, nparts, M, m, sh);
@@ -576,9 +581,9 @@ __global__ void w8_limbs_kernel(const T* __restrict__ x, int M, int MP, int K,
   frexpf(mx, &e);  // every |x| <= mx < 2^e
   const float up = ldexpf(1.f, 20 - e);
   if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
-  for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
-    float v[4];
-    load_h4(row, k, v);
+  for (int k = kf; k < k1; k += blockDim.x * 4) {
+    float v[4] = {v0[0], v0[1], v0[2], v0[3]};
+    if (!maxpart || k != kf) load_h4(row, k, v);
     limbs_store4(o0, o1, o2, k, v, up);
   }
 }
@@ -593,7 +598,7 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
                                      float* __restrict__ xscale) {
   griddep_wait();
   griddep_launch_dependents();
-  __shared__ float sh[33];
+  __shared__ float sh[33], shm[33];
   const int m = blockIdx.y;
   const int k0 = blockIdx.x * LB_CHUNK, k1 = min(K, k0 + LB_CHUNK);
   int8_t* o0 = xl + (size_t)m * K;
@@ -608,30 +613,52 @@ __global__ void rmsnorm_limbs_kernel(const float* __restrict__ h, const float* _
     if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = 1.f;
     return;
   }
-  float ss = 0.f;
-  for (int q = threadIdx.x; q < hparts; q += blockDim.x) ss += hstat[(size_t)q * M + m];
+  // Every load of the CTA is issued before any reduction waits: the producer's
+  // partial sums and maxima of row m, and this thread's first four elements of
+  // the row and of the norm weight (one pass covers the chunk when
+  // LB_CHUNK = 4 * blockDim.x).
+  const float* row = h + (size_t)m * K;
+  const int kf = k0 + threadIdx.x * 4;
+  float4 hv0 = make_float4(0.f, 0.f, 0.f, 0.f), wv0 = hv0;
+  if (kf < k1) {
+    hv0 = *reinterpret_cast<const float4*>(row + kf);
+    wv0 = __ldg(reinterpret_cast<const float4*>(w + kf));
+  }
+  float ss = 0.f, mx = 0.f;
+  for (int q = threadIdx.x; q < hparts; q += blockDim.x) {
+    ss += hstat[(size_t)q * M + m];
+    mx = fmaxf(mx, hmax[(size_t)q * M + m]);
+  }
   ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) {
+    sh[threadIdx.x >> 5] = ss;
+    shm[threadIdx.x >> 5] = mx;
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+    const bool in = threadIdx.x < (blockDim.x >> 5);
+    float t = in ? sh[threadIdx.x] : 0.f;
+    float u = in ? shm[threadIdx.x] : 0.f;
     t = warp_sum(t);
-    if (threadIdx.x == 0) sh[32] = rsqrtf(t / static_cast<float>(K) + eps);
+    u = warp_max(u);
+    if (threadIdx.x == 0) {
+      sh[32] = rsqrtf(t / static_cast<float>(K) + eps);
+      shm[32] = u;
+    }
   }
   __syncthreads();
   const float rstd = sh[32];
-  __syncthreads();
   // bound on max |h * rstd * w|: the fp32 products stay within 2^-9 of
   // rstd * max |h * w|
-  const float bound = part_max(hmax, hparts, M, m, sh) * rstd * (1.f + 1.f / 512.f);
+  const float bound = shm[32] * rstd * (1.f + 1.f / 512.f);
   int e;
   frexpf(bound, &e);
   const float up = ldexpf(1.f, 20 - e);
   if (threadIdx.x == 0 && blockIdx.x == 0) xscale[m] = ldexpf(1.f, e - 20);
-  const float* row = h + (size_t)m * K;
-  for (int k = k0 + threadIdx.x * 4; k < k1; k += blockDim.x * 4) {
-    const float4 hv = *reinterpret_cast<const float4*>(row + k);
-    const float4 wv = __ldg(reinterpret_cast<const float4*>(w + k));
+  for (int k = kf; k < k1; k += blockDim.x * 4) {
+    const float4 hv = k == kf ? hv0 : *reinterpret_cast<const float4*>(row + k);
+    const float4 wv = k == kf ? wv0 : __ldg(reinterpret_cast<const float4*>(w + k));
     const float v[4] = {hv.x * rstd * wv.x, hv.y * rstd * wv.y, hv.z * rstd * wv.z, hv.w * rstd * wv.w};
     limbs_store4(o0, o1, o2, k, v, up);
   }
