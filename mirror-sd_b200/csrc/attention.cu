@@ -16,6 +16,8 @@
 // In the draft forward K/V rows are read through the KvMap of kernels.cuh:
 // each sequence attends to its own logical rows [0, n_att), wherever the
 // cache ring holds them.
+#include <algorithm>
+
 #include "kernels.cuh"
 
 namespace dfl {
@@ -23,6 +25,8 @@ namespace dfl {
 
 constexpr int AT_TK = 64;          // kv rows per shared tile
 constexpr int AT_LD = 128 + 8;     // halves per shared row (+16 B pad)
+constexpr int kAttnCtaCost = 4;    // per-CTA cost of a split in kv tiles (setup, partial write)
+constexpr int kAttnMaxWaveSplits = 8;  // largest split the wave model may pick
 
 __device__ __forceinline__ void normrope_row(__half* row, const float* w, const float2* cs_row,
                                              float eps, int lane) {
@@ -399,12 +403,42 @@ size_t attn_smem_bytes(int nq, int nkv, int block) {
   return ((size_t)RP * AT_LD + (size_t)4 * AT_TK * AT_LD) * 2;
 }
 
-// choose the KV split so that b * NKV * splits covers the SMs about once
-void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits) {
+// Upper bound of attn_pick_split's count for any kv length (workspace sizing)
+int attn_max_splits(int batch, int nkv, int num_sms, int rows) {
   const int per = batch * nkv;
+  const int s = (num_sms + per - 1) / per;
+  return rows > 128 ? std::max(s, kAttnMaxWaveSplits) : s;
+}
+
+// Choose the KV split.  With at most 128 query rows per kv head the split
+// covers the SMs about once (b * NKV * splits >= SMs; grids of two CTAs per SM
+// take the two-stage ring).  With more rows (two query groups) the tcgen05
+// kernel runs one CTA per SM, and the split minimises
+//   waves * (kv tiles per CTA + kAttnCtaCost),   waves = ceil(b * NKV * splits / SMs),
+// so that no partial second wave doubles the time: at ctx 32768 and batch 1,
+// 18 splits (144 CTAs) take 69 us where 19 (152 CTAs, 4 in a second wave) took
+// 117 us; at batch 16, 8 splits (1024 CTAs, 6.9 waves) take 886 us against 964
+// for 2.  kAttnCtaCost, the per-CTA setup and partial write in tile units,
+// fits the c4 sweep (1, 2, 8, 15, 18, 37 and 55 splits at ctx 8K-32K).
+void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int rows, int* chunk, int* splits) {
+  const int per = batch * nkv;
+  const int tiles = (kv_len + AT_TK - 1) / AT_TK;
   int s = (num_sms + per - 1) / per;
-  const int max_s = (kv_len + AT_TK - 1) / AT_TK;
-  if (s > max_s) s = max_s;
+  if (rows > 128) {
+    const int cap = attn_max_splits(batch, nkv, num_sms, rows);
+    long long best = -1;
+    for (int c = 1; c <= cap && c <= tiles; ++c) {
+      const int per_cta = (tiles + c - 1) / c;
+      const int se = (tiles + per_cta - 1) / per_cta;
+      const long long waves = ((long long)per * se + num_sms - 1) / num_sms;
+      const long long cost = waves * (per_cta + kAttnCtaCost);
+      if (best < 0 || cost < best) {
+        best = cost;
+        s = se;
+      }
+    }
+  }
+  if (s > tiles) s = tiles;
   if (s < 1) s = 1;
   int ch = (kv_len + s - 1) / s;
   ch = (ch + AT_TK - 1) / AT_TK * AT_TK;

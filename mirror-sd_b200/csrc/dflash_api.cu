@@ -225,12 +225,10 @@ int check_dims(const DFlashDims* d) {
 size_t attn_rows_capacity(int max_batch, int nkv, int R, int kv_len_max, int num_sms) {
   size_t best = 0;
   for (int b = 1; b <= max_batch; ++b) {
-    int chunk, splits;
-    attn_pick_split(b, nkv, kv_len_max, num_sms, &chunk, &splits);
-    // splits can only shrink for shorter kv_len, so the max-length case bounds it
-    size_t rows = (size_t)b * nkv * splits * R;
+    (void)kv_len_max;
+    // attn_max_splits bounds the split count at every kv length
+    const size_t rows = (size_t)b * nkv * attn_max_splits(b, nkv, num_sms, R) * R;
     if (rows > best) best = rows;
-    // also cover every shorter length that yields more splits (never: splits <= kv tiles)
   }
   return best;
 }
@@ -923,7 +921,7 @@ int dflash_forward(void* handle, const DFlashForwardArgs* a, void* stream) {
   }
 
   int chunk, splits;
-  attn_pick_split(b, NKV, kvmax, hd->num_sms, &chunk, &splits);
+  attn_pick_split(b, NKV, kvmax, hd->num_sms, G * B, &chunk, &splits);
   if ((size_t)b * NKV * splits * G * B > hd->attn_part_rows)
     return fail(DFLASH_ERR_INVALID, "attention workspace too small");
   int hparts = 1;
@@ -1313,7 +1311,7 @@ size_t dflash_attention_workspace_size(int batch, int nq, int nkv, int block, in
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   int chunk, splits;
-  attn_pick_split(batch, nkv, kv_len, sms, &chunk, &splits);
+  attn_pick_split(batch, nkv, kv_len, sms, (nq / nkv) * block, &chunk, &splits);
   const size_t rows = (size_t)batch * nkv * splits * (nq / nkv) * block;
   const size_t rope_rows = (size_t)kv_len + block;
   return rows * 130 * 4 + rope_rows * 64 * 8 + 64 * 4 + 256;
@@ -1336,7 +1334,7 @@ int dflash_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, in
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   int chunk, splits;
-  attn_pick_split(batch, nkv, kv_len, sms, &chunk, &splits);
+  attn_pick_split(batch, nkv, kv_len, sms, (nq / nkv) * block, &chunk, &splits);
   const size_t rows = (size_t)batch * nkv * splits * (nq / nkv) * block;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   AttnParams p{};

@@ -223,7 +223,9 @@ cudaError_t quantize_q8_launch(const float* w, int oc, int ic, int8_t* q, __half
                                cudaStream_t st);
 
 size_t attn_smem_bytes(int nq, int nkv, int block);
-void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int* chunk, int* splits);
+// rows: query rows per kv head (heads / kv heads * block)
+void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int rows, int* chunk, int* splits);
+int attn_max_splits(int batch, int nkv, int num_sms, int rows);
 // mma.sync split kernel (also the fused QK-norm + RoPE variant) + combine
 cudaError_t attn_launch(const AttnParams& p, int batch, __half* out, cudaStream_t st);
 // The o-projection's input as W8A16 limbs ([3][MP][NQ*128] limb-major, MP =
