@@ -79,3 +79,48 @@ def test_extract_context_feature_and_sample(pkg):
     out = pkg.extract_context_feature(hs[:3], [7, 8, 9])
     assert out.shape == (1, 3, 6)
     assert pkg.sample(torch.tensor([[1.0, 3.0, 3.0]])).tolist() == [1]
+
+
+def _attn_splits(batch, nkv, kv_len, sms, rows):
+    """Restatement of the library's KV split choice (attention.cu
+    attn_pick_split): with more than 128 query rows per kv head (one CTA per
+    SM) minimise waves * (kv tiles per CTA + 4); otherwise cover the SMs once."""
+    per = batch * nkv
+    tiles = -(-kv_len // 64)
+    s = -(-sms // per)
+    if rows > 128:
+        cap, best = max(s, 8), None
+        for c in range(1, min(cap, tiles) + 1):
+            per_cta = -(-tiles // c)
+            se = -(-tiles // per_cta)
+            cost = -(-(per * se) // sms) * (per_cta + 4)
+            if best is None or cost < best:
+                best, s = cost, se
+    s = max(1, min(s, tiles))
+    ch = -(-(-(-kv_len // s)) // 64) * 64
+    return -(-kv_len // ch)
+
+
+def test_attention_split_waves(pkg):
+    """The attention workspace (C entry dflash_attention_workspace_size) holds
+    batch * NKV * splits partial rows: the split count avoids a partial second
+    wave of one-CTA-per-SM grids (27B dims: 40 / 8 heads, block 32)."""
+    import torch
+    lib = pkg._native.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+
+    def ws(batch, nq, nkv, block, kv_len, splits):
+        rows = batch * nkv * splits * (nq // nkv) * block
+        return rows * 130 * 4 + (kv_len + block) * 64 * 8 + 64 * 4 + 256
+
+    for batch, nq, nkv, block, kv_len in [(1, 40, 8, 32, 32800), (16, 40, 8, 32, 32800), (1, 40, 8, 32, 4128),
+                                          (16, 40, 8, 32, 8224), (4, 40, 8, 32, 16416), (1, 32, 8, 16, 2064),
+                                          (256, 32, 8, 16, 1104)]:
+        s = _attn_splits(batch, nkv, kv_len, sms, (nq // nkv) * block)
+        assert lib.dflash_attention_workspace_size(batch, nq, nkv, block, kv_len) == ws(batch, nq, nkv, block,
+                                                                                       kv_len, s)
+    if sms == 148:
+        assert _attn_splits(1, 8, 32800, 148, 160) == 18      # 144 CTAs, one wave (19 left 4 in a second)
+        assert _attn_splits(16, 8, 32800, 148, 160) == 8      # 1024 CTAs, 6.9 waves
+        assert _attn_splits(16, 8, 8224, 148, 160) == 1
+        assert _attn_splits(1, 8, 4128, 148, 160) == 17       # the c3 step: 136 CTAs
