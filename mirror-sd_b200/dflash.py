@@ -144,6 +144,54 @@ def sample(logits: torch.Tensor, temperature: float = 0.0) -> torch.Tensor:
 PROJ = ["wq", "wk", "wv", "wo", "wg", "wu", "wd"]
 
 
+def key_padding_lengths(mask, batch: int, q_len: int, ctx_len: int) -> Optional[List[int]]:
+    """Map the ``mask`` that ``DFlashDraftModel.__call__`` passes to SDPA
+    (dflash.py:315, over the stateless step's keys ``[context ; block]``) to
+    left padding: ``None`` when every key is kept, else the number of context
+    rows each sequence keeps, its last ones (the block is always kept).
+
+    Additive masks may hold 0 (kept) and values <= -1e4 or -inf (masked: their
+    exponentials underflow to exactly 0 in fp32, as in the reference's ANE
+    padding masks, ane_model.py:529-536); boolean masks keep True entries.  The
+    mask broadcasts to [batch, heads, q_len, ctx_len + q_len] as SDPA
+    broadcasts it and must be the same for every head and query.  Other masks
+    (biases, right padding, masked block keys) raise NotImplementedError: left
+    padding keeps every kept key at its own RoPE position once the kept rows are
+    packed and each sequence's positions start at ``ctx_len - kept``."""
+    m = torch.as_tensor(mask).detach().cpu()
+    if m.dtype == torch.bool:
+        keep = m
+    else:
+        mf = m.to(torch.float64)
+        if not bool(((mf == 0) | (mf <= -1e4)).all()):
+            raise NotImplementedError("additive masks may hold only 0 (kept) and <= -1e4 / -inf (masked)")
+        keep = mf == 0
+    L = ctx_len + q_len
+    if keep.dim() > 4 or keep.shape[-1] != L:
+        raise ValueError(f"mask must broadcast to [batch, heads, {q_len}, {L}], got {tuple(keep.shape)}")
+    while keep.dim() < 4:
+        keep = keep.unsqueeze(0)
+    try:
+        keep = keep.expand(batch, keep.shape[1], q_len, L)
+    except RuntimeError as e:
+        raise ValueError(f"mask must broadcast to [batch, heads, {q_len}, {L}], got {tuple(m.shape)}") from e
+    rows = keep[:, :1, :1, :].expand_as(keep)
+    if not bool((keep == rows).all()):
+        raise NotImplementedError("the mask must be the same for every head and query row")
+    rows = keep[:, 0, 0, :]
+    if bool(rows.all()):
+        return None
+    if not bool(rows[:, ctx_len:].all()):
+        raise NotImplementedError("block keys cannot be masked (the draft block attends to itself)")
+    lens = []
+    for i in range(batch):
+        kept = int(rows[i, :ctx_len].sum())
+        if kept and not bool(rows[i, ctx_len - kept:ctx_len].all()):
+            raise NotImplementedError("only left padding of the context is supported (kept rows last)")
+        lens.append(kept)
+    return lens
+
+
 @dataclass
 class Q8Layer:
     """One decoder layer: int8 [out, in] + fp16 [out] per projection, fp32 norms."""
@@ -673,7 +721,23 @@ class DFlashDraftModel:
         """``DFlashDraftModel.__call__`` (dflash.py:384-403): returns the
         final-normed hidden states [b, q, H] (bf16; fp32 in fp32-accumulate mode)."""
         if mask is not None:
-            raise ValueError("the DFlash draft attention is non-causal; mask must be None")
+            b, q = int(noise_embedding.shape[0]), int(noise_embedding.shape[1])
+            if cache is not None or isinstance(target_hidden, (list, tuple)):
+                # with a cache (or target layers read in place) only masks that
+                # keep every key are taken
+                m = torch.as_tensor(mask)
+                if not bool((m if m.dtype == torch.bool else m == 0).all()):
+                    raise NotImplementedError("a masking mask needs cache=None and a [b, ctx, F*H] target_hidden")
+            else:
+                C = int(target_hidden.shape[1])
+                lens = key_padding_lengths(mask, b, q, C)
+                if lens is not None:
+                    th = target_hidden if isinstance(target_hidden, torch.Tensor) else torch.as_tensor(target_hidden)
+                    packed = torch.cat([th[i, C - c:] for i, c in enumerate(lens)], dim=0)
+                    hidden, _, _, _ = self.draft_step(noise_embedding, packed, ctx_lens=lens,
+                                                      rope_offsets=[C - c for c in lens],
+                                                      want_hidden=True, want_tokens=False)
+                    return hidden
         hidden, _, _, _ = self.draft_step(noise_embedding, target_hidden, cache=cache,
                                           want_hidden=True, want_tokens=False)
         return hidden

@@ -119,9 +119,14 @@ def rope_neox(x: torch.Tensor, positions: torch.Tensor, theta: float) -> torch.T
     return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
 
 
-def sdpa(q, k, v, scale):
-    """``mx.fast.scaled_dot_product_attention`` with mask None (full, non-causal)."""
+def sdpa(q, k, v, scale, mask=None):
+    """``mx.fast.scaled_dot_product_attention`` (dflash.py:315-317): full,
+    non-causal attention; an additive ``mask`` is added to the scores and a
+    boolean one keeps its True entries, broadcast to [b, heads, q, keys]."""
     s = torch.matmul(q, k.transpose(-1, -2)) * scale
+    if mask is not None:
+        m = torch.as_tensor(mask)
+        s = s.masked_fill(~m, float("-inf")) if m.dtype == torch.bool else s + m.to(s.dtype)
     p = torch.softmax(s, dim=-1)
     return torch.matmul(p, v)
 
@@ -209,7 +214,7 @@ class OracleWeights:
 # --------------------------------------------------------------------------
 # forward (mirror_sd/dflash.py:236-403)
 # --------------------------------------------------------------------------
-def attention(cfg: OracleConfig, lw: OracleLayer, h, ctx, cache=None):
+def attention(cfg: OracleConfig, lw: OracleLayer, h, ctx, cache=None, mask=None):
     """Qwen3DFlashAttention.__call__ (dflash.py:277-319)."""
     b, q_len, _ = h.shape
     c_len = ctx.shape[1]
@@ -231,7 +236,7 @@ def attention(cfg: OracleConfig, lw: OracleLayer, h, ctx, cache=None):
     if rep > 1:                                                # :310-313 (mx.repeat)
         k = torch.repeat_interleave(k, rep, dim=1)
         v = torch.repeat_interleave(v, rep, dim=1)
-    o = sdpa(q, k, v, hd ** -0.5)                              # :315-317
+    o = sdpa(q, k, v, hd ** -0.5, mask)                        # :315-317
     o = o.transpose(1, 2).reshape(b, q_len, nh * hd)
     return o @ lw.wo.T                                         # :319
 
@@ -241,9 +246,9 @@ def mlp(lw: OracleLayer, x):
     return (silu(x @ lw.wg.T) * (x @ lw.wu.T)) @ lw.wd.T
 
 
-def decoder_layer(cfg, lw, h, ctx, cache=None):
+def decoder_layer(cfg, lw, h, ctx, cache=None, mask=None):
     """Qwen3DFlashDecoderLayer.__call__ (dflash.py:341-362)."""
-    h = h + attention(cfg, lw, rms_norm(h, lw.in_norm, cfg.rms_norm_eps), ctx, cache)
+    h = h + attention(cfg, lw, rms_norm(h, lw.in_norm, cfg.rms_norm_eps), ctx, cache, mask)
     return h + mlp(lw, rms_norm(h, lw.post_norm, cfg.rms_norm_eps))
 
 
@@ -253,14 +258,14 @@ def context_projection(cfg, w: OracleWeights, target_hidden):
 
 
 def draft_forward(cfg: OracleConfig, w: OracleWeights, noise, target_hidden,
-                  cache: Optional[list] = None, num_layers: Optional[int] = None):
+                  cache: Optional[list] = None, num_layers: Optional[int] = None, mask=None):
     """DFlashDraftModel.__call__ (dflash.py:384-403): returns the final-normed
     hidden states [b, q_len, H]."""
     h = noise
     ctx = context_projection(cfg, w, target_hidden)
     n = len(w.layers) if num_layers is None else num_layers
     for i in range(n):
-        h = decoder_layer(cfg, w.layers[i], h, ctx, None if cache is None else cache[i])
+        h = decoder_layer(cfg, w.layers[i], h, ctx, None if cache is None else cache[i], mask)
     return rms_norm(h, w.norm, cfg.rms_norm_eps)
 
 

@@ -124,3 +124,51 @@ def test_attention_split_waves(pkg):
         assert _attn_splits(16, 8, 32800, 148, 160) == 8      # 1024 CTAs, 6.9 waves
         assert _attn_splits(16, 8, 8224, 148, 160) == 1
         assert _attn_splits(1, 8, 4128, 148, 160) == 17       # the c3 step: 136 CTAs
+
+
+def test_key_padding_lengths(pkg):
+    """The masks DFlashDraftModel.__call__ takes (dflash.py:315 passes them to
+    SDPA): all-kept -> None, left padding -> kept context counts, anything the
+    device path cannot express exactly -> NotImplementedError."""
+    import torch
+    f = pkg.key_padding_lengths
+    b, q, C = 3, 4, 6
+    L = C + q
+    assert f(torch.zeros(L), b, q, C) is None
+    assert f(torch.ones(1, 1, q, L, dtype=torch.bool), b, q, C) is None
+    keep = torch.ones(b, 1, 1, L, dtype=torch.bool)
+    keep[0, 0, 0, :2] = False          # sequence 0 keeps its last 4 context rows
+    keep[2, 0, 0, :C] = False          # sequence 2 keeps no context
+    assert f(keep, b, q, C) == [4, 6, 0]
+    add = torch.where(keep, torch.tensor(0.0), torch.tensor(-1e4))        # the ANE padding value
+    assert f(add, b, q, C) == [4, 6, 0]
+    assert f(torch.where(keep, 0.0, float("-inf")), b, q, C) == [4, 6, 0]
+    right = torch.ones(b, 1, 1, L, dtype=torch.bool)
+    right[1, 0, 0, C - 2:C] = False    # right padding: kept rows first
+    with pytest.raises(NotImplementedError):
+        f(right, b, q, C)
+    with pytest.raises(NotImplementedError):
+        f(torch.full((L,), 0.5), b, q, C)                                 # a bias
+    blk = torch.ones(L, dtype=torch.bool)
+    blk[C] = False
+    with pytest.raises(NotImplementedError):
+        f(blk, b, q, C)                                                   # a masked block key
+    perq = torch.ones(1, 1, q, L, dtype=torch.bool)
+    perq[0, 0, 1, 0] = False
+    with pytest.raises(NotImplementedError):
+        f(perq, b, q, C)                                                  # query-dependent
+    with pytest.raises(ValueError):
+        f(torch.zeros(L + 1), b, q, C)
+
+
+def test_oracle_masked_sdpa_matches_truncation():
+    """The oracle's SDPA mask (dflash.py:315): masking keys equals dropping
+    them, additive -1e4 included."""
+    import torch
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(2, 4, n, 16, generator=g, dtype=torch.float64) for n in (5, 9, 9))
+    keep = torch.ones(2, 1, 1, 9, dtype=torch.bool)
+    keep[1, :, :, :3] = False
+    full = O.sdpa(q, k, v, 0.25, torch.where(keep, 0.0, -1e4).double())
+    assert torch.allclose(full[0], O.sdpa(q[:1], k[:1], v[:1], 0.25)[0], atol=1e-12)
+    assert torch.allclose(full[1], O.sdpa(q[1:], k[1:, :, 3:], v[1:, :, 3:], 0.25)[0], atol=1e-12)

@@ -293,3 +293,31 @@ def test_forward_activations_beyond_f16_range(pkg):
     check_hidden(hid, ref, label="W8A16, activations beyond the f16 range")
     check_tokens(toks, O.draft_logits(dense, ref, ocfg.block_size), MARGIN)
     model.close()
+
+
+@pytest.mark.parametrize("additive", [False, True])
+def test_forward_left_padding_mask(pkg, additive):
+    """``__call__`` with a key-padding mask (dflash.py:315 passes it to SDPA):
+    3 sequences in one [b, ctx, F*H] buffer keeping their last 40 / 75 / 0
+    context rows, against the oracle's masked SDPA over the padded inputs (each
+    kept key at its own position), as a boolean mask and as the ANE's additive
+    -1e4 padding."""
+    ocfg = tiny_cfg()
+    b, C, B = 3, 75, ocfg.block_size
+    q8, dense = O.synth_weights(ocfg, seed=21)
+    model = gpu_model(pkg, ocfg, q8, max_batch=b, max_ctx=C)
+    noise, th = O.synth_inputs(ocfg, b, C, B, seed=22)
+    keep = torch.ones(b, 1, 1, C + B, dtype=torch.bool)
+    keep[0, :, :, :C - 40] = False
+    keep[2, :, :, :C] = False
+    mask = torch.where(keep, 0.0, -1e4) if additive else keep
+    hid = model(noise.to(torch.bfloat16).cuda(), th.to(torch.bfloat16).cuda(), mask=mask)
+    torch.cuda.synchronize()
+    ref = O.draft_forward(ocfg, dense, noise.to(torch.bfloat16).float(), th.to(torch.bfloat16).float(),
+                          mask=mask.double() if additive else keep)
+    check_hidden(hid, ref, label=f"left-padding mask ({'additive' if additive else 'boolean'})")
+    with pytest.raises(NotImplementedError):
+        right = torch.ones(C + B, dtype=torch.bool)
+        right[C - 5:C] = False
+        model(noise.to(torch.bfloat16).cuda(), th.to(torch.bfloat16).cuda(), mask=right)
+    model.close()
