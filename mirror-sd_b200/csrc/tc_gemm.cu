@@ -65,6 +65,22 @@ __device__ __forceinline__ void tc_tile(int t, int nmb, int nnb, int& mb, int& n
 
 
 
+// Context K|V (per layer: K heads, then V heads, 128 columns each): tile
+// column n-block nb runs over every layer's K blocks first and then every
+// layer's V blocks, so a CTA's last tile is a V tile.  The last tile's
+// epilogue overlaps nothing, and a V tile's (scale, store) takes ~8 us where a
+// K tile's (RMSNorm, RoPE) takes ~24.  Identity when a layer's K half is not a
+// whole number of 256-column blocks.
+template <int MODE>
+__device__ __forceinline__ int tc_nb_phys(int nb, int nnb, int nkv) {
+  if (MODE != kTcCtxKV || nkv % 2) return nb;
+  const int half = nkv / 2;          // 256-column blocks per K (or V) half of a layer
+  const int kb = nnb / 2;            // all layers' K blocks
+  const int v = nb >= kb ? 1 : 0;
+  const int i = nb - v * kb;
+  return (i / half) * (2 * half) + v * half + i % half;
+}
+
 // Work of CTA c (grid G, T tiles): tiles c, c + G, ... of the first
 // R = T / G rounds; with a tail split S > 0 the T - R*G tiles of the last,
 // partial round are cut along K into S parts each, P = (T - R*G) * S parts
@@ -233,6 +249,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const TcItem w = tc_item(ti, ntiles, nk, p.split, G, cidx);
         int mb, nb;
         tc_tile(w.tile, nmb, nnb, mb, nb);
+        nb = tc_nb_phys<MODE>(nb, nnb, p.nkv);
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++it) {
           const int s = it % CF::STAGES;
           const uint32_t ph = (it / CF::STAGES) & 1;
@@ -318,6 +335,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const TcItem w = tc_item(ti, ntiles, nk, p.split, G, cidx);
       int mb, nb;
       tc_tile(w.tile, nmb, nnb, mb, nb);
+      nb = tc_nb_phys<MODE>(nb, nnb, p.nkv);
       const int n0 = nb * TC_BN;
       const int row = (mb * CF::NR + (int)rank) * TC_BM + row_local;
       const bool row_ok = row < p.M;
