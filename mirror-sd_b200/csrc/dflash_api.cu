@@ -5,6 +5,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -1255,17 +1256,12 @@ int dflash_w8_linear(const int8_t* q, const uint16_t* s, int N, int K, const uin
   CK(cudaMemsetAsync(cnt, 0, (size_t)(N / 128) * sizeof(int), st));
   cudaError_t e = w8tc_launch(wt, p, kStore, err, part, pf, cnt, sms, st);
   int hv = 0;
-  if (e == cudaSuccess) {
-    cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
-    e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  for (void* ptr : {(void*)sp, (void*)xl, (void*)xs, (void*)wt, (void*)part, (void*)cnt, (void*)err}) {
+    const cudaError_t f = cudaFreeAsync(ptr, st);
+    if (e == cudaSuccess) e = f;
   }
-  cudaFreeAsync(sp, st);
-  cudaFreeAsync(xl, st);
-  cudaFreeAsync(xs, st);
-  cudaFreeAsync(wt, st);
-  cudaFreeAsync(part, st);
-  cudaFreeAsync(cnt, st);
-  cudaFreeAsync(err, st);
   CK(e);
   if (hv) return fail(DFLASH_ERR_DEVICE, "W8A16 kernel gave up on a bounded wait (code %d)", hv);
   return DFLASH_OK;
@@ -1293,13 +1289,12 @@ int dflash_tc_gemm(const uint16_t* A, const uint16_t* B, int M, int N, int K, in
   CK(cudaMemsetAsync(p.tail_cnt, 0, (size_t)sms * sizeof(int), st));
   cudaError_t e = tc_gemm_launch(A, B, ab_bf16 != 0, kTcStoreF32, p, st);
   int hv = 0;
-  if (e == cudaSuccess) {
-    cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
-    e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&hv, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  for (void* ptr : {(void*)p.tail_part, (void*)p.tail_cnt, (void*)err}) {
+    const cudaError_t f = cudaFreeAsync(ptr, st);
+    if (e == cudaSuccess) e = f;
   }
-  cudaFreeAsync(p.tail_part, st);
-  cudaFreeAsync(p.tail_cnt, st);
-  cudaFreeAsync(err, st);
   CK(e);
   if (hv) return fail(DFLASH_ERR_DEVICE, "tcgen05 GEMM gave up on a bounded wait (code %d)", hv);
   return DFLASH_OK;
