@@ -133,7 +133,11 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   using C = TaCfg<NG, NS_, HALVES>;
   constexpr int TA_NS = C::NS;
   static_assert(HALVES == 1 || NG == 1, "column halves need a single query group");
-  griddep_wait();
+  // The producer warps wait for the previous kernel only after requesting the
+  // K/V tiles that kernel cannot have written (below); every other warp waits
+  // here, before it touches global memory.
+  const bool prod_warp = (threadIdx.x >> 5) >= C::PROD_WARP0 && (threadIdx.x >> 5) < C::MMA_WARP;
+  if (!prod_warp) griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -192,6 +196,33 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   if (warp >= C::PROD_WARP0 && warp < C::MMA_WARP) {
     // ---- producers: Q once, then the K/V tiles (rows through the KvMap)
     const int t = threadIdx.x - 32 * C::PROD_WARP0;  // 0..127
+    const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
+    const int plane = kseq * p.nkv + kvh;
+    // The previous kernel writes Q and this forward's block rows of K/V, the
+    // last p.block logical rows; the context rows come from the context K|V
+    // GEMM, which completed before that kernel could start.  So whole,
+    // contiguous tiles below the block rows go to the ring (one per stage, at
+    // most TA_NS) before the dependency wait, while the previous kernel drains.
+    int npre = 0;
+    {
+      const int pre_end = kv_len - p.block;
+      for (int j = 0; j < ntiles && j < TA_NS; ++j) {
+        const int row0 = kv0 + j * TA_TK;
+        if (row0 + TA_TK > kv1 || row0 + TA_TK > pre_end) break;
+        const int slot0 = mapped ? kv_slot(p.kv, row0, rs) : row0;
+        if ((mapped ? kv_slot(p.kv, row0 + TA_TK - 1, rs) : row0 + TA_TK - 1) != slot0 + TA_TK - 1) break;
+        if (t == 0) {
+          uint8_t* st = smem + C::KV_OFF + j * TA_STAGE;
+          mbar_arrive_expect_tx(&full[j], TA_STAGE);
+          for (int ch = 0; ch < 2; ++ch) {
+            tma_load_3d(st + ch * (TA_TK * 128), &map_k, &full[j], ch * 64, slot0, plane);
+            tma_load_3d(st + TA_KV_BYTES + ch * (TA_TK * 128), &map_v, &full[j], ch * 64, slot0, plane);
+          }
+        }
+        ++npre;
+      }
+    }
+    griddep_wait();
     const __half* qg = p.q + ((size_t)bi * p.nq + (size_t)kvh * G) * p.block * 128;
     for (int idx = t; idx < NG * 128 * 16; idx += 32 * TA_PROD) {
       const int r = idx >> 4, c = idx & 15;  // 16-byte piece c of the 256-byte row r
@@ -205,17 +236,15 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
     fence_proxy_async_smem();
     mbar_arrive(q_ready);
 
-    const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
     const __half* kg = p.k + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
     const __half* vg = p.v + ((size_t)kseq * p.nkv + kvh) * (size_t)p.kv_cap * 128;
-    const int plane = kseq * p.nkv + kvh;
     // Producer thread 0 alone waits for free stages and issues the TMA tiles;
     // the other producer threads sleep on a named barrier and join only for the
     // tiles copied row by row.  Nobody leaves the loop early: every producer
     // thread reaches the same named barriers, and after a timeout (thread 0's
     // `dead`) the copies are skipped while the bounded waits elsewhere unwind.
     bool dead = false;
-    for (int j = 0; j < ntiles; ++j) {
+    for (int j = npre; j < ntiles; ++j) {
       const int s = j % TA_NS;
       uint8_t* st = smem + C::KV_OFF + s * TA_STAGE;
       const int row0 = kv0 + j * TA_TK;
