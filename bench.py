@@ -784,14 +784,20 @@ def main():
         node, local_cpus = gpu_numa(dev)
         saved_aff = os.sched_getaffinity(0)
         if local_cpus:
-            os.sched_setaffinity(0, local_cpus)
+            try:
+                os.sched_setaffinity(0, local_cpus)
+            except OSError:   # the placement is an optimisation, never a requirement
+                local_cpus = None
         noise_h = noise.cpu().pin_memory()
         th_h = th.cpu().pin_memory()
         tgt_h = target.cpu().pin_memory()
         tok_h = torch.empty((args.batch, B - 1), dtype=torch.int32).pin_memory()
         acc_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
         cor_h = torch.empty((args.batch,), dtype=torch.int32).pin_memory()
-        os.sched_setaffinity(0, saved_aff)
+        try:
+            os.sched_setaffinity(0, saved_aff)
+        except OSError:
+            pass
         # this rank's host->device rate alone (one copy of target_hidden)
         th_probe = torch.empty_like(th)
         torch.cuda.synchronize(dev)
