@@ -78,6 +78,11 @@ struct WiCfg {
   static constexpr size_t SMEM = (size_t)NS * STAGE + RED_BYTES + 1024 + 256;
 };
 
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void named_bar(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -411,13 +416,43 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
         for (int m = 0; m < MP; ++m) dst[m * 128 + ch] = r[m];
         __threadfence();
         named_bar(1, 128);
-        if (et == 0) *last_flag = (atomicAdd(args.counters + tile, 1) == n_seg - 1);
+        // Split plan: the tile's n_seg CTAs stream equal K-slices and finish
+        // together, so each waits (bounded) for the others' partials and then
+        // merges and finishes its own share of the rows, n_seg times less
+        // work than one CTA taking them all.  The counter counts arrivals to
+        // n_seg, then departures to 2 n_seg, and the last departure resets
+        // it.  Stream-K contributors finish at different times: there the
+        // last to arrive takes every row.
+        const bool coop = !args.stream_k;
+        int r0 = 0, r1 = p.M;
+        if (coop) {
+          r0 = sg.slot * p.M / n_seg;
+          r1 = (sg.slot + 1) * p.M / n_seg;
+        }
+        if (et == 0) {
+          const int prev = atomicAdd(args.counters + tile, 1);
+          if (!coop) {
+            *last_flag = prev == n_seg - 1;
+          } else {
+            bool arrived = true;
+            for (uint32_t i = 0; ld_acquire_gpu(args.counters + tile) < n_seg; ++i) {
+              if (i >= kSpinLimit || *abort_flag) {
+                if (!*abort_flag) atomicExch(args.err, kDevMbarTimeout);
+                *abort_flag = 1;
+                arrived = false;
+                break;
+              }
+              __nanosleep(32);
+            }
+            *last_flag = arrived;
+          }
+        }
         named_bar(1, 128);
         if (*last_flag) {
           __threadfence();
           const float* src = args.part + (size_t)tile * args.maxseg * MP * 128;
           // two rows per pass, every slot's partial loaded before any add
-          for (int m0 = q; m0 < p.M && live; m0 += 8) {
+          for (int m0 = r0 + q; m0 < r1 && live; m0 += 8) {
             float4 va[2][8], ua[2][8];
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr)
@@ -426,7 +461,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
                 const int m = m0 + 4 * rr;
                 va[rr][s] = make_float4(0.f, 0.f, 0.f, 0.f);
                 ua[rr][s] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (s < n_seg && m < p.M) {
+                if (s < n_seg && m < r1) {
                   const float* rowp = src + ((size_t)s * MP + m) * 128;
                   if (EPC == 4) {
                     va[rr][s] = __ldcg(reinterpret_cast<const float4*>(rowp + lane * 4));
@@ -441,7 +476,7 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
 #pragma unroll
             for (int rr = 0; rr < 2; ++rr) {
               const int m = m0 + 4 * rr;
-              if (m < p.M) {
+              if (m < r1) {
                 float v[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                 for (int s = 0; s < 8; ++s) {  // fixed slot order: deterministic
@@ -452,9 +487,11 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
               }
             }
           }
-          if (et == 0) args.counters[tile] = 0;  // ready for the next launch
+          if (et == 0 && !coop) args.counters[tile] = 0;  // ready for the next launch
         }
         named_bar(1, 128);
+        if (coop && et == 0 && atomicAdd(args.counters + tile, 1) == 2 * n_seg - 1)
+          args.counters[tile] = 0;  // every contributor is done with the tile
       }
     }
   }
