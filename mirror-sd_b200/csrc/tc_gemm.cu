@@ -338,7 +338,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       nb = tc_nb_phys<MODE>(nb, nnb, p.nkv);
       const int n0 = nb * TC_BN;
       const int row = (mb * CF::NR + (int)rank) * TC_BM + row_local;
-      const bool row_ok = row < p.M;
+      bool row_ok = row < p.M;
+      int ci = -1;   // tail counter of this part's (slot, rank), -1 for a whole tile
       // No epilogue warp leaves the loop early: after a timeout (the abort
       // flag) the items are walked without work, so every named barrier of
       // the tail parts below is reached by all four warps.
@@ -362,18 +363,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         __threadfence();
         named_bar_sync(2, 128);
+        // The tile's parts finish together (equal K slices), so each waits,
+        // bounded, until all have written their partials and then merges
+        // and finishes its 1/split of the rows, instead of the last to
+        // arrive taking all 128.  The counter counts arrivals to split, then
+        // departures to 2 split (every part counts, after an abort too); the
+        // last departure resets it for the next launch.
+        ci = slot * CF::NR + (int)rank;
         if (threadIdx.x == 64) {
-          // every part counts, after an abort too, so the counter always
-          // returns to zero for the next launch
-          const int ci = slot * CF::NR + (int)rank;
-          const bool last = atomicAdd(p.tail_cnt + ci, 1) == p.split - 1;
-          if (last) p.tail_cnt[ci] = 0;
-          *tail_flag = last;
+          atomicAdd(p.tail_cnt + ci, 1);
+          bool arrived = true;
+          for (uint32_t i = 0; ld_acquire_gpu(p.tail_cnt + ci) < p.split; ++i) {
+            if (i >= kSpinLimit || *abort_flag) {
+              if (!*abort_flag) atomicExch(p.err, kDevMbarTimeout);
+              *abort_flag = 1;
+              arrived = false;
+              break;
+            }
+            __nanosleep(32);
+          }
+          *tail_flag = arrived;
         }
         named_bar_sync(2, 128);
-        run = live && *tail_flag != 0;
+        const int r0 = w.part * TC_BM / p.split, r1 = (w.part + 1) * TC_BM / p.split;
+        row_ok = row_ok && row_local >= r0 && row_local < r1;
+        // a warp with none of the part's rows skips the merge and the epilogue
+        run = live && *tail_flag != 0 && __any_sync(0xffffffffu, row_local >= r0 && row_local < r1);
         if (run) {
-          // the last part: sum the parts in fixed order into the accumulator
+          // sum the parts in fixed order into the accumulator (all lanes of
+          // the warp; only the part's rows are stored by the epilogue)
           __threadfence();
           const float* base = p.tail_part + ((size_t)slot * p.split * CF::NR + rank) * (TC_BM * TC_BN);
 #pragma unroll 1
@@ -566,6 +584,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
+      if (ci >= 0 && threadIdx.x == 64 && atomicAdd(p.tail_cnt + ci, 1) == 2 * p.split - 1)
+        p.tail_cnt[ci] = 0;   // every part of the tile is done
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {  // accumulator free for tile ti + 2 (rank 0 issues the MMAs of a pair)
