@@ -411,36 +411,39 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
         for (int m = 0; m < MP; ++m) dst[m * 128 + ch] = r[m];
         __threadfence();
         named_bar(1, 128);
-        // Split plan: the tile's n_seg CTAs stream equal K-slices and finish
-        // together, so each waits (bounded) for the others' partials and then
-        // merges and finishes its own share of the rows, n_seg times less
-        // work than one CTA taking them all.  The counter counts arrivals to
-        // n_seg, then departures to 2 n_seg, and the last departure resets
-        // it.  Stream-K contributors finish at different times: there the
-        // last to arrive takes every row.
-        const bool coop = !args.stream_k;
-        int r0 = 0, r1 = p.M;
-        if (coop) {
-          r0 = sg.slot * p.M / n_seg;
-          r1 = (sg.slot + 1) * p.M / n_seg;
+        // The contributors that finish together merge the tile together: each
+        // waits (bounded) for every partial, then sums the slots of its share
+        // of the rows in slot order (deterministic) and runs the fused
+        // epilogue on them.  In the split plan every contributor takes part
+        // (equal K slices).  In stream-K the tile is the last segment of every
+        // contributor's run but possibly the highest one's, whose run goes on
+        // into the next tile: that one only leaves its partial, so no SM is
+        // held back from the next kernel.  The counter counts the n_seg
+        // arrivals, then the participants' departures; the last departure
+        // resets it.  With one CTA taking all 32 rows the merge tail was
+        // ~10 us.
+        int npart = n_seg, pidx = sg.slot;
+        if (args.stream_k) {
+          const int last_owner = sk_owner(tile * nkb + nkb - 1, sch.U, sch.G);
+          const bool last_late = (sk_begin(last_owner + 1, sch.U, sch.G) - 1) / nkb == tile;
+          npart = n_seg - (last_late ? 0 : 1);
+          pidx = seg == nseg - 1 ? sg.slot : -1;
         }
+        const int r0 = pidx >= 0 ? pidx * p.M / npart : 0;
+        const int r1 = pidx >= 0 ? (pidx + 1) * p.M / npart : 0;
         if (et == 0) {
-          const int prev = atomicAdd(args.counters + tile, 1);
-          if (!coop) {
-            *last_flag = prev == n_seg - 1;
-          } else {
-            bool arrived = true;
-            for (uint32_t i = 0; ld_acquire_gpu(args.counters + tile) < n_seg; ++i) {
-              if (i >= kSpinLimit || *abort_flag) {
-                if (!*abort_flag) atomicExch(args.err, kDevMbarTimeout);
-                *abort_flag = 1;
-                arrived = false;
-                break;
-              }
-              __nanosleep(32);
+          atomicAdd(args.counters + tile, 1);
+          bool arrived = pidx >= 0;
+          for (uint32_t i = 0; arrived && ld_acquire_gpu(args.counters + tile) < n_seg; ++i) {
+            if (i >= kSpinLimit || *abort_flag) {
+              if (!*abort_flag) atomicExch(args.err, kDevMbarTimeout);
+              *abort_flag = 1;
+              arrived = false;
+              break;
             }
-            *last_flag = arrived;
+            __nanosleep(32);
           }
+          *last_flag = arrived;
         }
         named_bar(1, 128);
         if (*last_flag) {
@@ -482,11 +485,10 @@ __global__ void __launch_bounds__(WI_THREADS, 1)
               }
             }
           }
-          if (et == 0 && !coop) args.counters[tile] = 0;  // ready for the next launch
         }
         named_bar(1, 128);
-        if (coop && et == 0 && atomicAdd(args.counters + tile, 1) == 2 * n_seg - 1)
-          args.counters[tile] = 0;  // every contributor is done with the tile
+        if (pidx >= 0 && et == 0 && atomicAdd(args.counters + tile, 1) == n_seg + npart - 1)
+          args.counters[tile] = 0;  // every participant is done with the tile
       }
     }
   }
