@@ -732,9 +732,10 @@ static bool map_i8_rows(CUtensorMap* m, const void* base, uint64_t K, uint64_t r
 // Split plan: S in 1..8 and groups = floor(SMs / S) from a small cost model
 // (a slice streams nkb/S blocks of 16 KB at ~42 GB/s per SM; S > 1 adds a
 // merge of ~4 us per tile, hidden behind the next tile's stream when that is
-// longer, exposed once at the end).
-static void w8i_split_plan(int tiles, int nkb, int num_sms, int* splits, int* groups) {
-  const double t_kb = 16384.0 / 42e3;
+// longer, exposed once at the end). Returns the estimate in us.
+static constexpr double kW8BlockUs = 16384.0 / 42e3;
+static double w8i_split_plan(int tiles, int nkb, int num_sms, int* splits, int* groups) {
+  const double t_kb = kW8BlockUs;
   double best = 1e30;
   int bs = 1, bg = num_sms < tiles ? num_sms : tiles;
   for (int s = 1; s <= 8 && s <= nkb; ++s) {
@@ -749,6 +750,7 @@ static void w8i_split_plan(int tiles, int nkb, int num_sms, int* splits, int* gr
   }
   *splits = bs;
   *groups = bg;
+  return best;
 }
 
 // The launch schedule: grid size, split plan, stream-K or not, partial slots.
@@ -759,10 +761,19 @@ struct W8Schedule {
 static W8Schedule w8i_schedule(int N, int K, int num_sms) {
   const int tiles = N / 128, nkb = K / 128;
   W8Schedule w{};
-  if (nkb >= 64) {
+  int splits = 1, groups = 1;
+  const double split_est = w8i_split_plan(tiles, nkb, num_sms, &splits, &groups);
+  // Stream-K for long K, and for wide shapes (at least one tile per SM) whose
+  // split plan ends on a poorly filled round: there the even share of the
+  // units, ceil(U / SMs) block times plus the shared merge, is shorter.
+  // Narrow shapes keep the split plan; their many 3-4-way shared tiles merge
+  // slower than this estimate says.
+  const long long units = (long long)tiles * nkb;
+  const double sk_est = (double)((units + num_sms - 1) / num_sms) * kW8BlockUs + 4.0;
+  if (nkb >= 64 || (tiles >= num_sms && sk_est < split_est - 1e-9)) {
     // stream-K: one CTA per SM (never more CTAs than units), shrunk until no
     // tile is shared by more than 8 CTAs
-    const long long U = (long long)tiles * nkb;
+    const long long U = units;
     int G = (int)std::min<long long>(num_sms, U);
     for (;;) {
       int ms = 1;
@@ -775,7 +786,8 @@ static W8Schedule w8i_schedule(int N, int K, int num_sms) {
       --G;
     }
   }
-  w8i_split_plan(tiles, nkb, num_sms, &w.splits, &w.groups);
+  w.splits = splits;
+  w.groups = groups;
   w.grid = w.splits * w.groups;
   w.stream_k = 0;
   w.maxseg = w.splits;

@@ -40,7 +40,10 @@ def test_quantizer_bit_exact_random(pkg):
 
 
 @pytest.mark.parametrize("M,N,Kd", [(1, 256, 128), (8, 384, 640), (16, 1024, 4096), (32, 768, 5120),
-                                    (31, 256, 17408), (64, 512, 1024)])
+                                    (31, 256, 17408), (64, 512, 1024),
+                                    # at least one tile per SM on a poorly filled last
+                                    # round: stream-K with short K (8B and 4B gate|up)
+                                    (16, 24576, 4096), (32, 19456, 2560)])
 def test_w8_linear_vs_fp32(K, M, N, Kd):
     g = torch.Generator().manual_seed(M * 7 + N)
     w = torch.randn(N, Kd, generator=g) * 0.02
