@@ -24,7 +24,8 @@
 //       TMEM lane.  O is rescaled in TMEM only when
 //       the running max grows by more than 2^8 (P then stays below 256), so
 //       most tiles need no O traffic.  Warps whose 32 rows are all padding
-//       take no part.
+//       take no part.  Group 1's real rows sit in its top lanes, so its
+//       softmax warps share no scheduler with group 0's first warp.
 //   4 producer warps  K/V tiles into the swizzled stages of the ring.  A full
 //       tile whose 64 rows sit in 64 consecutive slots (always in the
 //       stateless forward; in a cache ring except at the sink / wrap
@@ -33,7 +34,8 @@
 //       copied row by row through the KvMap with cp.async, zero-filling the
 //       rows past the end (stale V rows must not reach P.V).
 //   1 MMA warp        single-thread issue: S(j) of every group, then PV(j-1)
-//       of every group once its P is ready.
+//       of every group once its P is ready.  It is warp 4NG + 1, on
+//       scheduler 1; the TMA-issuing producer is warp 4NG, on scheduler 0.
 // Every mbarrier wait is bounded; a timeout sets the error word and unwinds.
 #include "kernels.cuh"
 
@@ -61,9 +63,13 @@ struct TaCfg {
   // registers per thread: two CTAs of THREADS threads must fit in 64K
   static constexpr int MAX_REGS = NS_ == 2 ? 112 : 255;
   static constexpr int SOFT_WARPS = 4 * NG;
+  // Warp w issues on scheduler w % 4.  The MMA warp sits on scheduler 1,
+  // beside one softmax warp, and not on scheduler 0, which also runs the
+  // TMA-issuing producer warp (PROD_WARP0).  The producers are warps
+  // PROD_WARP0 and PROD_WARP0 + 2 .. PROD_WARP0 + 4.
   static constexpr int PROD_WARP0 = SOFT_WARPS;
-  static constexpr int MMA_WARP = SOFT_WARPS + TA_PROD;
-  static constexpr int THREADS = 32 * (MMA_WARP + 1);
+  static constexpr int MMA_WARP = SOFT_WARPS + 1;
+  static constexpr int THREADS = 32 * (SOFT_WARPS + TA_PROD + 1);
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = NG * TA_QG;
   static constexpr int BAR_OFF = KV_OFF + NS * TA_STAGE;
@@ -136,7 +142,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   // The producer warps wait for the previous kernel only after requesting the
   // K/V tiles that kernel cannot have written (below); every other warp waits
   // here, before it touches global memory.
-  const bool prod_warp = (threadIdx.x >> 5) >= C::PROD_WARP0 && (threadIdx.x >> 5) < C::MMA_WARP;
+  const bool prod_warp = (threadIdx.x >> 5) >= C::PROD_WARP0 && (threadIdx.x >> 5) != C::MMA_WARP;
   if (!prod_warp) griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
@@ -161,6 +167,10 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   const int kv1 = min(kv_len, kv0 + p.chunk);
   const int ntiles = kv1 > kv0 ? (kv1 - kv0 + TA_TK - 1) / TA_TK : 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Group 1's real rows occupy its top TMEM lanes (g1_shift = 128 - those rows
+  // rounded up to 32), so with 32 of them their softmax warp is warp 7, on
+  // scheduler 3, not on scheduler 0 beside group 0's first softmax warp.
+  const int g1_shift = NG == 2 ? 128 - (R - 128 + 31) / 32 * 32 : 0;
   const size_t pbase = (((size_t)bi * p.nkv + kvh) * p.splits + split) * (size_t)R;
 
   if (threadIdx.x == 0) {
@@ -193,9 +203,10 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= C::PROD_WARP0 && warp < C::MMA_WARP) {
+  if (prod_warp) {
     // ---- producers: Q once, then the K/V tiles (rows through the KvMap)
-    const int t = threadIdx.x - 32 * C::PROD_WARP0;  // 0..127
+    const int pw = warp == C::PROD_WARP0 ? 0 : warp - C::PROD_WARP0 - 1;
+    const int t = 32 * pw + lane;  // 0..127
     const int kseq = mapped ? p.kv.seq[bi].cseq : bi;   // K/V store sequence
     const int plane = kseq * p.nkv + kvh;
     // The previous kernel writes Q and this forward's block rows of K/V, the
@@ -228,8 +239,10 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       const int r = idx >> 4, c = idx & 15;  // 16-byte piece c of the 256-byte row r
       const int g = r >> 7, rr = r & 127, ch = c >> 3, cc = c & 7;
       uint8_t* dst = smem + C::Q_OFF + g * TA_QG + ch * (128 * 128) + rr * 128 + ((cc ^ (rr & 7)) << 4);
-      const int src = HALVES == 2 ? (r & 63) : r;   // halves: MMA rows 64-127 repeat rows 0-63
-      cp_async16_zfill(smem_u32(dst), qg + (size_t)min(src, R - 1) * 128 + c * 8, src < R);
+      // halves: MMA rows 64-127 repeat rows 0-63; group 1 sits g1_shift lanes up
+      const int src = HALVES == 2 ? (r & 63) : g == 1 ? r - g1_shift : r;
+      const bool real = src < R && (g == 0 || rr >= g1_shift);
+      cp_async16_zfill(smem_u32(dst), qg + (size_t)max(0, min(src, R - 1)) * 128 + c * 8, real);
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -349,10 +362,12 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
     constexpr int CW = TA_TK / HALVES;  // kv columns per thread and tile
     const int half = HALVES == 2 ? (r >> 6) : 0;
     const int coff = half * CW;
-    const int qrow = HALVES == 2 ? (r & 63) : g * 128 + r;
-    const bool valid = qrow < R;
+    const int qrow = HALVES == 2 ? (r & 63) : g * 128 + r - (g == 1 ? g1_shift : 0);
+    const bool valid = qrow < R && (g == 0 || r >= g1_shift);
     // the warp holds a real row
-    const bool active = (HALVES == 2 ? ((32 * (warp & 3)) & 63) : g * 128 + 32 * (warp & 3)) < R;
+    const bool active = HALVES == 2 ? ((32 * (warp & 3)) & 63) < R
+                                    : (g == 0 || 32 * (warp & 3) >= g1_shift) &&
+                                          g * 128 + 32 * (warp & 3) - (g == 1 ? g1_shift : 0) < R;
     const uint32_t lane_off = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t o_t = tmem + C::O_COL + g * 128 + lane_off;
     const float c = p.scale_log2;
