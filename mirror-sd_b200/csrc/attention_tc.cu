@@ -150,8 +150,11 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + TA_NS;
   uint64_t* s_ready = empty + TA_NS;    // [NG][2] S(j) in TMEM buffer j & 1
-  uint64_t* p_ready = s_ready + 2 * NG;  // [NG][2] P(j) stored over S(j)
-  uint64_t* pv_done = p_ready + 2 * NG;  // [NG][2] PV(j) complete (S/P buffer free, O current)
+  // P(j) stored over S(j) by every group, and PV(j) of every group complete
+  // (S/P buffers free, O current), per buffer j & 1: one barrier for all
+  // groups, so the MMA thread waits once per tile and commits once
+  uint64_t* p_ready = s_ready + 2 * NG;  // [2]
+  uint64_t* pv_done = p_ready + 2 * NG;  // [2]
   uint64_t* o_ready = pv_done + 2 * NG;  // [NG]
   uint64_t* q_ready = o_ready + NG;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
@@ -178,17 +181,18 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       mbar_init(&full[s], 1);  // producer thread 0 (with the TMA bytes, or after cp.async)
       mbar_init(&empty[s], 1);
     }
+    int nthr = 0;
     for (int g = 0; g < NG; ++g) {
       // softmax threads of group g: its warps holding at least one real row
       // (with halves: rows 0-63 twice)
       const int rows = min(128, R - g * 128);
-      const int nthr = HALVES == 2 ? 64 * ((rows + 31) / 32) : 32 * ((rows + 31) / 32);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&s_ready[2 * g + b], 1);
-        mbar_init(&p_ready[2 * g + b], nthr);
-        mbar_init(&pv_done[2 * g + b], 1);
-      }
+      nthr += HALVES == 2 ? 64 * ((rows + 31) / 32) : 32 * ((rows + 31) / 32);
+      for (int b = 0; b < 2; ++b) mbar_init(&s_ready[2 * g + b], 1);
       mbar_init(&o_ready[g], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&p_ready[b], nthr);
+      mbar_init(&pv_done[b], 1);
     }
     mbar_init(q_ready, 32 * TA_PROD);
     *abort_flag = 0;
@@ -336,19 +340,13 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
         }
         if (j >= 1 && ok) {
           const int jj = j - 1, s = jj % TA_NS, b = jj & 1;
-          for (int g = 0; g < NG && ok; ++g) {
-            if (!mbar_wait(&p_ready[2 * g + b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
-          }
-          if (!ok) break;
+          if (!mbar_wait(&p_ready[b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
           for (int ks = 0; ks < TA_TK / 16; ++ks)
-            for (int g = 0; g < NG; ++g) {
-              issue_pv_step(g, s, b, jj > 0, ks);
-              if (ks == TA_TK / 16 - 1) {
-                umma_commit(&pv_done[2 * g + b]);
-                if (jj == ntiles - 1) umma_commit(&o_ready[g]);
-              }
-            }
+            for (int g = 0; g < NG; ++g) issue_pv_step(g, s, b, jj > 0, ks);
+          umma_commit(&pv_done[b]);
+          if (jj == ntiles - 1)
+            for (int g = 0; g < NG; ++g) umma_commit(&o_ready[g]);
           umma_commit(&empty[s]);  // every read of stage s is issued
         }
       }
@@ -418,7 +416,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       const float m_new = grow ? m_cand : m_used;
       if (__any_sync(0xffffffffu, grow) && j > 0) {
         // O must hold tiles < j before it is rescaled
-        if (!mbar_wait(&pv_done[2 * g + (b ^ 1)], ((j - 1) >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&pv_done[b ^ 1], ((j - 1) >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const float f = grow ? ex2_approx(m_used - m_new) : 1.f;
 #pragma unroll 1
@@ -465,7 +463,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       tmem_st32(s_t, pk);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&p_ready[2 * g + b]);
+      mbar_arrive(&p_ready[b]);
     }
     if (HALVES == 2) {
       // merge the halves: the upper copy hands (O, m, l) to the lower one
