@@ -149,13 +149,13 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty = full + TA_NS;
-  uint64_t* s_ready = empty + TA_NS;    // [NG][2] S(j) in TMEM buffer j & 1
-  // P(j) stored over S(j) by every group, and PV(j) of every group complete
-  // (S/P buffers free, O current), per buffer j & 1: one barrier for all
-  // groups, so the MMA thread waits once per tile and commits once
-  uint64_t* p_ready = s_ready + 2 * NG;  // [2]
-  uint64_t* pv_done = p_ready + 2 * NG;  // [2]
-  uint64_t* o_ready = pv_done + 2 * NG;  // [NG]
+  uint64_t* s_ready = empty + TA_NS;    // [2] S(j) of every group in TMEM buffer j & 1 (one commit)
+  // P(j) stored over S(j) by every group, per buffer j & 1: one barrier for
+  // all groups, so the MMA thread waits once per tile.  PV(j) complete is
+  // empty[j % TA_NS] (the stage's last reader), which the softmax also waits
+  // on before it rescales O.
+  uint64_t* p_ready = s_ready + 2;      // [2]
+  uint64_t* o_ready = p_ready + 2;       // [NG]
   uint64_t* q_ready = o_ready + NG;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -187,12 +187,11 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       // (with halves: rows 0-63 twice)
       const int rows = min(128, R - g * 128);
       nthr += HALVES == 2 ? 64 * ((rows + 31) / 32) : 32 * ((rows + 31) / 32);
-      for (int b = 0; b < 2; ++b) mbar_init(&s_ready[2 * g + b], 1);
       mbar_init(&o_ready[g], 1);
     }
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_ready[b], 1);
       mbar_init(&p_ready[b], nthr);
-      mbar_init(&pv_done[b], 1);
     }
     mbar_init(q_ready, 32 * TA_PROD);
     *abort_flag = 0;
@@ -333,10 +332,8 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
           // held by one chain of dependent accumulations (batch 16, ctx 32K:
           // 886 -> 796 us together with the softmax's full-tile path).
           for (int kk = 0; kk < 8; ++kk)
-            for (int g = 0; g < NG; ++g) {
-              issue_s_step(g, s, b, kk);
-              if (kk == 7) umma_commit(&s_ready[2 * g + b]);
-            }
+            for (int g = 0; g < NG; ++g) issue_s_step(g, s, b, kk);
+          umma_commit(&s_ready[b]);
         }
         if (j >= 1 && ok) {
           const int jj = j - 1, s = jj % TA_NS, b = jj & 1;
@@ -344,10 +341,9 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
           tc_fence_after();
           for (int ks = 0; ks < TA_TK / 16; ++ks)
             for (int g = 0; g < NG; ++g) issue_pv_step(g, s, b, jj > 0, ks);
-          umma_commit(&pv_done[b]);
           if (jj == ntiles - 1)
             for (int g = 0; g < NG; ++g) umma_commit(&o_ready[g]);
-          umma_commit(&empty[s]);  // every read of stage s is issued
+          umma_commit(&empty[s]);  // every read of stage s, and PV(jj), is issued
         }
       }
     }
@@ -373,7 +369,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
     bool ok = true;
     for (int j = 0; j < ntiles && active; ++j) {
       const int b = j & 1;
-      if (!mbar_wait(&s_ready[2 * g + b], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s_ready[b], (j >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
       tc_fence_after();
       uint32_t sv[CW];
       const uint32_t s_t = tmem + C::S_COL + (2 * g + b) * TA_TK + lane_off;
@@ -416,7 +412,9 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       const float m_new = grow ? m_cand : m_used;
       if (__any_sync(0xffffffffu, grow) && j > 0) {
         // O must hold tiles < j before it is rescaled
-        if (!mbar_wait(&pv_done[b ^ 1], ((j - 1) >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+        // (empty[(j - 1) % TA_NS] completes with PV(j - 1); its next phase
+        // needs P(j - 1 + TA_NS), so the parity cannot alias)
+        if (!mbar_wait(&empty[(j - 1) % TA_NS], ((j - 1) / TA_NS) & 1, p.err, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const float f = grow ? ex2_approx(m_used - m_new) : 1.f;
 #pragma unroll 1
