@@ -119,6 +119,23 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// max of three (exact, like two fmaxf)
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// (a0, a1) * (b, b) + (c, c) as one packed fp32 FMA: two fmaf, rounded alike
+__device__ __forceinline__ float2 ffma2_bc(float a0, float a1, float b, float c) {
+  uint64_t x, y, z, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(y) : "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(z) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(x), "l"(y), "l"(z));
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+  return o;
+}
 // two base-2 exponentials in one MUFU op: the f16 pair ex2(x0), ex2(x1)
 __device__ __forceinline__ uint32_t ex2_f16x2(float x0, float x1) {
   const uint32_t a = pack_f16x2(x0, x1);
@@ -323,7 +340,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       for (int j = 0; j <= ntiles && ok; ++j) {
         if (j < ntiles) {
           const int s = j % TA_NS, b = j & 1;
-          if (!mbar_wait(&full[s], (j / TA_NS) & 1, p.err, abort_flag)) break;
+          if (!mbar_wait_ready(&full[s], (j / TA_NS) & 1, p.err, abort_flag)) break;
           tc_fence_after();
           // S(j) overwrites the S/P buffer PV(j-2) read: tcgen05.mma ops of
           // one thread execute in issue order, so no wait is needed here.
@@ -337,7 +354,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
         }
         if (j >= 1 && ok) {
           const int jj = j - 1, s = jj % TA_NS, b = jj & 1;
-          if (!mbar_wait(&p_ready[b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+          if (!mbar_wait_ready(&p_ready[b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
           tc_fence_after();
           for (int ks = 0; ks < TA_TK / 16; ++ks)
             for (int g = 0; g < NG; ++g) issue_pv_step(g, s, b, jj > 0, ks);
@@ -398,8 +415,9 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
         // four interleaved chains (the max is exact in any order)
         float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int e = 0; e < CW; ++e) m4[e & 3] = fmaxf(m4[e & 3], __uint_as_float(sv[e]));
-        mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+        for (int e = 0; e < CW; e += 2)
+          m4[(e >> 1) & 3] = fmax3f(m4[(e >> 1) & 3], __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]));
+        mx = fmax3f(fmaxf(m4[0], m4[1]), m4[2], m4[3]);
       } else {
 #pragma unroll
         for (int e = 0; e < CW; ++e)
@@ -438,8 +456,10 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
       const float neg_m = -m_used;
       if (full_tile) {
 #pragma unroll
-        for (int e = 0; e < CW; e += 2)
-          own[e / 2] = ex2_f16x2(fmaf(__uint_as_float(sv[e]), c, neg_m), fmaf(__uint_as_float(sv[e + 1]), c, neg_m));
+        for (int e = 0; e < CW; e += 2) {
+          const float2 x = ffma2_bc(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), c, neg_m);
+          own[e / 2] = ex2_f16x2(x.x, x.y);
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < CW; e += 2) {

@@ -59,6 +59,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of a phase: no suspension when it has not completed.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait.  Returns false (and raises *err) when the phase never flips.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
                                           volatile int* abort_flag) {
@@ -69,6 +80,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   if (err) atomicExch(err, kDevMbarTimeout);
   if (abort_flag) *abort_flag = 1;
   return false;
+}
+// The same wait for a phase that has usually completed already: one
+// non-blocking test first, then the bounded try_wait loop.
+__device__ __forceinline__ bool mbar_wait_ready(uint64_t* bar, uint32_t parity, int* err,
+                                                volatile int* abort_flag) {
+  return mbar_test_wait(bar, parity) || mbar_wait(bar, parity, err, abort_flag);
 }
 
 // acquire load of a global counter that other CTAs advance with atomics
