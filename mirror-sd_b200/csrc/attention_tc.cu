@@ -26,23 +26,25 @@
 //       most tiles need no O traffic.  Warps whose 32 rows are all padding
 //       take no part.  Group 1's real rows sit in its top lanes, so its
 //       softmax warps share no scheduler with group 0's first warp.
-//   4 producer warps  K/V tiles into the swizzled stages of the ring.  A full
+//   3 producer warps  K/V tiles into the swizzled stages of the ring.  A full
 //       tile whose 64 rows sit in 64 consecutive slots (always in the
 //       stateless forward; in a cache ring except at the sink / wrap
 //       boundaries) is one TMA copy per 64-column half, completed by
 //       transaction bytes, so NS tiles stay in flight.  Other tiles are
 //       copied row by row through the KvMap with cp.async, zero-filling the
 //       rows past the end (stale V rows must not reach P.V).
-//   1 MMA warp        single-thread issue: S(j) of every group, then PV(j-1)
-//       of every group once its P is ready.  It is warp 4NG + 1, on
-//       scheduler 1; the TMA-issuing producer is warp 4NG, on scheduler 0.
+//   2 MMA warps       one issuing thread each, on different schedulers:
+//       S(j) of every group (warp 4NG + 4, scheduler 0) and PV(j) of every
+//       group once its P is ready (warp 4NG + 1, scheduler 1).  A single
+//       issuing thread spent about a third of each tile on its own waits,
+//       commits and fences with the tensor pipe idle.
 // Every mbarrier wait is bounded; a timeout sets the error word and unwinds.
 #include "kernels.cuh"
 
 namespace dfl {
 
 constexpr int TA_TK = 64;                  // kv rows per tile
-constexpr int TA_PROD = 4;                 // producer warps
+constexpr int TA_PROD = 3;                 // producer warps
 constexpr int TA_KV_BYTES = TA_TK * 256;   // K (or V) of one tile: 64 rows x 128 f16
 constexpr int TA_STAGE = 2 * TA_KV_BYTES;  // K then V
 constexpr int TA_QG = 128 * 256;           // one query group: 128 rows x 128 f16
@@ -63,13 +65,14 @@ struct TaCfg {
   // registers per thread: two CTAs of THREADS threads must fit in 64K
   static constexpr int MAX_REGS = NS_ == 2 ? 112 : 255;
   static constexpr int SOFT_WARPS = 4 * NG;
-  // Warp w issues on scheduler w % 4.  The MMA warp sits on scheduler 1,
-  // beside one softmax warp, and not on scheduler 0, which also runs the
-  // TMA-issuing producer warp (PROD_WARP0).  The producers are warps
-  // PROD_WARP0 and PROD_WARP0 + 2 .. PROD_WARP0 + 4.
+  // Warp w issues on scheduler w % 4.  The two MMA-issuing warps sit on
+  // different schedulers: the PV warp (which also owns the TMEM allocation)
+  // on scheduler 1, the S warp on scheduler 0.  The producers are warps
+  // PROD_WARP0 (the TMA issuer), PROD_WARP0 + 2 and PROD_WARP0 + 3.
   static constexpr int PROD_WARP0 = SOFT_WARPS;
   static constexpr int MMA_WARP = SOFT_WARPS + 1;
-  static constexpr int THREADS = 32 * (SOFT_WARPS + TA_PROD + 1);
+  static constexpr int S_WARP = SOFT_WARPS + 4;
+  static constexpr int THREADS = 32 * (SOFT_WARPS + TA_PROD + 2);
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = NG * TA_QG;
   static constexpr int BAR_OFF = KV_OFF + NS * TA_STAGE;
@@ -159,7 +162,8 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   // The producer warps wait for the previous kernel only after requesting the
   // K/V tiles that kernel cannot have written (below); every other warp waits
   // here, before it touches global memory.
-  const bool prod_warp = (threadIdx.x >> 5) >= C::PROD_WARP0 && (threadIdx.x >> 5) != C::MMA_WARP;
+  const bool prod_warp = (threadIdx.x >> 5) >= C::PROD_WARP0 && (threadIdx.x >> 5) != C::MMA_WARP &&
+                         (threadIdx.x >> 5) != C::S_WARP;
   if (!prod_warp) griddep_wait();
   griddep_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
@@ -317,50 +321,60 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
         if (t == 0 && !dead) mbar_arrive(&full[s]);
       }
     }
-  } else if (warp == C::MMA_WARP) {
-    // ---- single-thread MMA issue: S(j) of every group, then PV(j-1)
+  } else if (warp == C::MMA_WARP || warp == C::S_WARP) {
+    // ---- MMA issue by two single threads on different schedulers, so the
+    // waits, commits and fences of one overlap the other's queued MMAs:
+    //   S warp:  S(j) of every group once stage j is full and PV(j-2), the
+    //            last reader of S/P buffer j & 1, has completed;
+    //   PV warp: PV(j) of every group once P(j) is stored, then the stage's
+    //            free barrier, which also tells the softmax that O holds PV(j).
+    // MMAs of one thread execute in issue order; across the two threads the
+    // only hazards are the S/P buffer (above), stage reuse (S(j) completes
+    // before P(j) exists, hence before PV(j) frees the stage) and O, which
+    // only the PV thread writes.
     if (lane == 0 && ntiles > 0) {
-      constexpr uint32_t idesc_s = umma_idesc_f16(128, TA_TK, 0);
-      constexpr uint32_t idesc_o = umma_idesc_f16(128, 128, 0) | (1u << 16);  // B (V) MN-major
       const uint32_t qa = smem_u32(smem + C::Q_OFF), kva = smem_u32(smem + C::KV_OFF);
-      // k-step kk (16 head dims) of S_g = Q_g K^T
-      auto issue_s_step = [&](int g, int s, int b, int kk) {
-        const int ch = kk >> 2, w = kk & 3;
-        const uint64_t ad = umma_desc_sw128(qa + g * TA_QG + ch * (128 * 128)) + 2 * w;
-        const uint64_t bd = umma_desc_sw128(kva + s * TA_STAGE + ch * (TA_TK * 128)) + 2 * w;
-        umma_f16(tmem + C::S_COL + (2 * g + b) * TA_TK, ad, bd, idesc_s, kk > 0);
-      };
-      // k-step ks (16 kv rows) of O_g += P_g V: P as 8 TMEM columns of f16 pairs
-      auto issue_pv_step = [&](int g, int s, int b, bool acc, int ks) {
-        const uint32_t pt = tmem + C::S_COL + (2 * g + b) * TA_TK + ks * 8;
-        const uint64_t bd = umma_desc_sw128_mn(kva + s * TA_STAGE + TA_KV_BYTES + ks * 2048, TA_TK * 128);
-        umma_f16_ts(tmem + C::O_COL + g * 128, pt, bd, idesc_o, (acc || ks > 0) ? 1u : 0u);
-      };
       bool ok = mbar_wait(q_ready, 0, p.err, abort_flag);
-      for (int j = 0; j <= ntiles && ok; ++j) {
-        if (j < ntiles) {
+      if (warp == C::S_WARP) {
+        constexpr uint32_t idesc_s = umma_idesc_f16(128, TA_TK, 0);
+        // k-step kk (16 head dims) of S_g = Q_g K^T
+        auto issue_s_step = [&](int g, int s, int b, int kk) {
+          const int ch = kk >> 2, w = kk & 3;
+          const uint64_t ad = umma_desc_sw128(qa + g * TA_QG + ch * (128 * 128)) + 2 * w;
+          const uint64_t bd = umma_desc_sw128(kva + s * TA_STAGE + ch * (TA_TK * 128)) + 2 * w;
+          umma_f16(tmem + C::S_COL + (2 * g + b) * TA_TK, ad, bd, idesc_s, kk > 0);
+        };
+        for (int j = 0; j < ntiles && ok; ++j) {
           const int s = j % TA_NS, b = j & 1;
           if (!mbar_wait_ready(&full[s], (j / TA_NS) & 1, p.err, abort_flag)) break;
+          // (empty[(j - 2) % TA_NS] next completes with PV(j - 2 + TA_NS),
+          // which needs S(j - 2 + TA_NS) from this thread: no parity alias)
+          if (j >= 2 && !mbar_wait_ready(&empty[(j - 2) % TA_NS], ((j - 2) / TA_NS) & 1, p.err, abort_flag))
+            break;
           tc_fence_after();
-          // S(j) overwrites the S/P buffer PV(j-2) read: tcgen05.mma ops of
-          // one thread execute in issue order, so no wait is needed here.
-          // With two groups their k-steps alternate, so consecutive MMAs
-          // accumulate into different TMEM buffers and the tensor pipe is not
-          // held by one chain of dependent accumulations (batch 16, ctx 32K:
-          // 886 -> 796 us together with the softmax's full-tile path).
+          // the two groups' k-steps alternate, so consecutive MMAs accumulate
+          // into different TMEM buffers
           for (int kk = 0; kk < 8; ++kk)
             for (int g = 0; g < NG; ++g) issue_s_step(g, s, b, kk);
           umma_commit(&s_ready[b]);
         }
-        if (j >= 1 && ok) {
-          const int jj = j - 1, s = jj % TA_NS, b = jj & 1;
-          if (!mbar_wait_ready(&p_ready[b], (jj >> 1) & 1, p.err, abort_flag)) { ok = false; break; }
+      } else {
+        constexpr uint32_t idesc_o = umma_idesc_f16(128, 128, 0) | (1u << 16);  // B (V) MN-major
+        // k-step ks (16 kv rows) of O_g += P_g V: P as 8 TMEM columns of f16 pairs
+        auto issue_pv_step = [&](int g, int s, int b, bool acc, int ks) {
+          const uint32_t pt = tmem + C::S_COL + (2 * g + b) * TA_TK + ks * 8;
+          const uint64_t bd = umma_desc_sw128_mn(kva + s * TA_STAGE + TA_KV_BYTES + ks * 2048, TA_TK * 128);
+          umma_f16_ts(tmem + C::O_COL + g * 128, pt, bd, idesc_o, (acc || ks > 0) ? 1u : 0u);
+        };
+        for (int j = 0; j < ntiles && ok; ++j) {
+          const int s = j % TA_NS, b = j & 1;
+          if (!mbar_wait_ready(&p_ready[b], (j >> 1) & 1, p.err, abort_flag)) break;
           tc_fence_after();
           for (int ks = 0; ks < TA_TK / 16; ++ks)
-            for (int g = 0; g < NG; ++g) issue_pv_step(g, s, b, jj > 0, ks);
-          if (jj == ntiles - 1)
+            for (int g = 0; g < NG; ++g) issue_pv_step(g, s, b, j > 0, ks);
+          if (j == ntiles - 1)
             for (int g = 0; g < NG; ++g) umma_commit(&o_ready[g]);
-          umma_commit(&empty[s]);  // every read of stage s, and PV(jj), is issued
+          umma_commit(&empty[s]);  // every read of stage s, and PV(j), is issued
         }
       }
     }
