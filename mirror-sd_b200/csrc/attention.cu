@@ -25,7 +25,7 @@ namespace dfl {
 
 constexpr int AT_TK = 64;          // kv rows per shared tile
 constexpr int AT_LD = 128 + 8;     // halves per shared row (+16 B pad)
-constexpr int kAttnCtaCost = 4;    // per-CTA cost of a split in kv tiles (setup, partial write)
+constexpr int kAttnCtaCost = 6;    // per-CTA cost of a split in kv tiles (setup, partial write)
 constexpr int kAttnMaxWaveSplits = 8;  // largest split the wave model may pick
 
 __device__ __forceinline__ void normrope_row(__half* row, const float* w, const float2* cs_row,
@@ -419,7 +419,9 @@ int attn_max_splits(int batch, int nkv, int num_sms, int rows) {
 // 18 splits (144 CTAs) take 69 us where 19 (152 CTAs, 4 in a second wave) took
 // 117 us; at batch 16, 8 splits (1024 CTAs, 6.9 waves) take 886 us against 964
 // for 2.  kAttnCtaCost, the per-CTA setup and partial write in tile units,
-// fits the c4 sweep (1, 2, 8, 15, 18, 37 and 55 splits at ctx 8K-32K).
+// fits the c4 sweep (1, 2, 8, 15, 18, 37 and 55 splits at ctx 8K-32K); it was
+// 4 until the tiles got faster, which left batch 16 / ctx 16K on 8 splits
+// (342 us) where one split covers 128 SMs in one wave.
 void attn_pick_split(int batch, int nkv, int kv_len, int num_sms, int rows, int* chunk, int* splits) {
   const int per = batch * nkv;
   const int tiles = (kv_len + AT_TK - 1) / AT_TK;

@@ -84,7 +84,7 @@ def test_extract_context_feature_and_sample(pkg):
 def _attn_splits(batch, nkv, kv_len, sms, rows):
     """Restatement of the library's KV split choice (attention.cu
     attn_pick_split): with more than 128 query rows per kv head (one CTA per
-    SM) minimise waves * (kv tiles per CTA + 4); otherwise cover the SMs once."""
+    SM) minimise waves * (kv tiles per CTA + 6); otherwise cover the SMs once."""
     per = batch * nkv
     tiles = -(-kv_len // 64)
     s = -(-sms // per)
@@ -93,7 +93,7 @@ def _attn_splits(batch, nkv, kv_len, sms, rows):
         for c in range(1, min(cap, tiles) + 1):
             per_cta = -(-tiles // c)
             se = -(-tiles // per_cta)
-            cost = -(-(per * se) // sms) * (per_cta + 4)
+            cost = -(-(per * se) // sms) * (per_cta + 6)
             if best is None or cost < best:
                 best, s = cost, se
     s = max(1, min(s, tiles))
@@ -123,6 +123,7 @@ def test_attention_split_waves(pkg):
         assert _attn_splits(1, 8, 32800, 148, 160) == 18      # 144 CTAs, one wave (19 left 4 in a second)
         assert _attn_splits(16, 8, 32800, 148, 160) == 8      # 1024 CTAs, 6.9 waves
         assert _attn_splits(16, 8, 8224, 148, 160) == 1
+        assert _attn_splits(16, 8, 16416, 148, 160) == 1
         assert _attn_splits(1, 8, 4128, 148, 160) == 17       # the c3 step: 136 CTAs
 
 
