@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(TaCfg<NG, NS_, HALVES>::THREADS) __maxnreg__((
   uint64_t* empty = full + TA_NS;
   uint64_t* s_ready = empty + TA_NS;    // [2] S(j) of every group in TMEM buffer j & 1 (one commit)
   // P(j) stored over S(j) by every group, per buffer j & 1: one barrier for
-  // all groups, so the MMA thread waits once per tile.  PV(j) complete is
+  // all groups, so the PV thread waits once per tile.  PV(j) complete is
   // empty[j % TA_NS] (the stage's last reader), which the softmax also waits
   // on before it rescales O.
   uint64_t* p_ready = s_ready + 2;      // [2]
