@@ -127,6 +127,34 @@ def test_attention_split_waves(pkg):
         assert _attn_splits(1, 8, 4128, 148, 160) == 17       # the c3 step: 136 CTAs
 
 
+def test_attention_split_model_properties(pkg):
+    """Across random shapes, the library's attention workspace equals the
+    restated split choice, and the splits tile the kv rows: chunks are whole
+    64-row tiles, every split holds at least one kv row, and together they
+    cover kv_len."""
+    from hypothesis import given, settings, strategies as st
+    import torch
+    lib = pkg._native.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+
+    @settings(max_examples=300, deadline=None, derandomize=True)
+    @given(batch=st.integers(1, 300), nkv=st.sampled_from([1, 2, 4, 8]), g=st.integers(1, 8),
+           block=st.integers(1, 64), kv_len=st.integers(1, 40000))
+    def check(batch, nkv, g, block, kv_len):
+        rows = g * block
+        if rows > 256:
+            return
+        s = _attn_splits(batch, nkv, kv_len, sms, rows)
+        per = batch * nkv * s * rows
+        want = per * 130 * 4 + (kv_len + block) * 64 * 8 + 64 * 4 + 256
+        assert lib.dflash_attention_workspace_size(batch, g * nkv, nkv, block, kv_len) == want
+        ch = -(-(-(-kv_len // s)) // 64) * 64
+        assert ch % 64 == 0 and s >= 1
+        assert (s - 1) * ch < kv_len <= s * ch
+
+    check()
+
+
 def test_key_padding_lengths(pkg):
     """The masks DFlashDraftModel.__call__ takes (dflash.py:315 passes them to
     SDPA): all-kept -> None, left padding -> kept context counts, anything the
